@@ -1,0 +1,28 @@
+// Host-side internals shared by the .cu translation units: error reporting, launch accounting, device facts.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+
+#include "../../include/comp_b200.h"
+
+namespace b2q {
+
+// Records a printf-style message as the calling thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+
+// Checks the CUDA launch status of the kernel just enqueued and counts it.
+int after_launch(const char* what);
+
+// Per-device facts, cached after the first query (thread-safe).
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem_optin = 0;  // bytes of dynamic shared memory one CTA may opt into
+};
+int device_info(DeviceInfo* out);
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace b2q

@@ -1,0 +1,698 @@
+// Q4_0 x q8_0 and TQ2_0 x q8_K decode GEMVs for sm_100a (HBM-bound weight streaming, integer dp4a block dots).
+//
+// Replaces COMP's Triton kernels q4_0_gemv / tq2_0_gemv (src/komp/kernels.py:48-142). Same results: every int32
+// block dot is exact and identical; Y[m][n] = sum over blocks of the per-block f32 product in the reference's
+// multiply order (q4_0: f32(s) * dw * dx, kernels.py:93; tq2_0: dx * dw * f32(s), kernels.py:141), summed in a
+// fixed (deterministic) order that differs from the reference's, as the reference's own order differs from KURN's.
+//
+// Schedule (one design for both formats; a "chunk" is 16 consecutive quant bytes of one weight row):
+//   * The CTA is one team of T = 32*ceil(C/CPT/32) threads, where C = chunks per row (K/32 for Q4_0, K/64 for
+//     TQ2_0). Thread t owns chunks t, t+T, ... (CPT of them) of every row it touches: one 128-bit streaming load per
+//     chunk and row, coalesced across the CTA (consecutive threads, consecutive 16-byte chunks of the same row).
+//   * Work unit = a group of R consecutive rows. Each CTA takes a contiguous range of groups. The next unit's weight
+//     loads are issued before the current unit is computed (register double buffer), and the first unit's loads are
+//     issued before the activation prologue, so HBM latency overlaps staging and math.
+//   * Activations (int8 q8 planes, or f32 quantized in the prologue) are staged once per CTA into shared memory in a
+//     permuted layout: for column m, bit-field j and chunk c, the 16 activation bytes that multiply bit-field j of
+//     weight chunk c sit at xs[m][j][c] (one conflict-free 128-bit shared load per thread). Q4_0 has j in {lo, hi}
+//     nibble; TQ2_0 has j in {crumb 0..3}.
+//   * Math per chunk and column: the weight word is masked once per bit-field and dotted with dp4a; the high fields
+//     are left in place (u32 x s32 dp4a) and the exact multiple of 2^k is shifted out afterwards, e.g. Q4_0:
+//     s = dp4a(w & 0x0F0F0F0F, xl) + (dp4a_u(w & 0xF0F0F0F0, xh) >> 4) - 8 * sum(x). The offsets (-8 for Q4_0,
+//     -1 for TQ2_0) are folded in with per-chunk activation sums precomputed in the prologue. TQ2_0 blocks span 4
+//     chunks (4 adjacent threads), whose partial dots are combined with two xor-shuffles before scaling.
+//   * Per-unit reduction: warp shuffles, then a cross-warp sum in shared memory in fixed warp order.
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "b2q_device.cuh"
+#include "b2q_internal.h"
+
+namespace b2q {
+
+constexpr int kMaxThreads = 512;
+constexpr int kMaxColumns = 4;  // columns per launch; more are processed in groups of 4 (weights re-read per group)
+
+struct GemvParams {
+  const uint8_t* wq;
+  int64_t ldwq;
+  const int16_t* ws;
+  const int8_t* xq;       // int8 activations [M][K] (null when x_f32 is given)
+  const float* xd;        // activation scales [M][nblk] (null when x_f32 is given)
+  const float* x_f32;     // f32 activations [M][ldx] for the fused quantizer prologue, or null
+  int64_t ldx;
+  int8_t* xq_out;         // fused prologue: CTA 0 also stores the quantized activations here (nullable)
+  float* xd_out;
+  float* y;               // [M][ldy]; output row index is row0 + local row
+  int64_t ldy;
+  int64_t row0;
+  int32_t* s;             // [M][N][nblk] int32 block dots (nullable)
+  // fused all-gather epilogue (multi-GPU): y is this rank's copy; every CTA also copies its rows to the peers
+  float* const* y_peers;  // device array [nranks] or null
+  uint32_t* const* flags_peers;  // device array [nranks] of flag arrays (each [nranks + 1] uint32) or null
+  int32_t* status;
+  int rank, nranks;
+  uint32_t epoch;
+  long long spin_limit;
+  int64_t N;              // rows in this launch
+  int64_t K;
+  int M;                  // columns in this launch (1..kMaxColumns)
+  int C;                  // 16-byte chunks per row
+  int CPT;                // chunks per thread per row
+  int64_t groups;         // ceil(N / R)
+};
+
+template <int FMT>
+struct Fmt;
+template <>
+struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibbles)
+  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2;
+};
+template <>
+struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
+  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4;
+};
+
+// Position (in 16-byte units, within one activation column) of the q-th 16-byte piece of the natural int8 layout.
+template <int FMT>
+__device__ __forceinline__ int perm_unit(int q, int C) {
+  if (FMT == 0) return (q & 1) * C + (q >> 1);  // block b = q/2, nibble field h = q%2
+  const int b = q >> 4, o = q & 15;              // 16 pieces per 256-value block
+  const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
+  return j * C + 4 * b + c;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Activation prologue: fills xs (permuted int8), xsum (per-chunk offset correction) and xscale (per-block f32 scale).
+// ------------------------------------------------------------------------------------------------------------------
+template <int FMT>
+__device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int* xsum, float* xscale) {
+  const int T = blockDim.x, tt = threadIdx.x;
+  const int K = (int)p.K, C = p.C, M = p.M;
+  const int nblk = K / Fmt<FMT>::kBlock;
+  const int units = K / 16;
+  if (p.x_f32 == nullptr) {
+    for (int idx = tt; idx < M * units; idx += T) {
+      const int m = idx / units, q = idx - m * units;
+      const uint4 v = *reinterpret_cast<const uint4*>(p.xq + (int64_t)m * K + (int64_t)q * 16);
+      *reinterpret_cast<uint4*>(xs + (int64_t)m * K + perm_unit<FMT>(q, C) * 16) = v;
+    }
+    for (int idx = tt; idx < M * nblk; idx += T) xscale[idx] = p.xd[idx];
+  } else if (FMT == 0) {
+    // q8_0: 8 lanes per 32-value block, 4 blocks per warp per iteration (warp-uniform loop for the shuffles)
+    const int lane = tt & 31, sub = lane & 7, nw = T / 32;
+    const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
+    for (int base = (tt >> 5) * 4; base < M * nblk; base += nw * 4) {
+      const int g = base + (lane >> 3);
+      const bool ok = g < M * nblk;
+      const int m = ok ? g / nblk : 0, b = ok ? g - m * nblk : 0;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok) v = *reinterpret_cast<const float4*>(p.x_f32 + (int64_t)m * p.ldx + b * 32 + sub * 4);
+      float d;
+      const uint32_t q = q8_0_quant4(v, &d);
+      if (ok) {
+        *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + ((sub >> 2) * C + b) * 16 + (sub & 3) * 4) = q;
+        const float ds = q8_0_stored_scale(d);
+        if (sub == 0) xscale[m * nblk + b] = ds;
+        if (writer) {
+          *reinterpret_cast<uint32_t*>(p.xq_out + (int64_t)m * K + b * 32 + sub * 4) = q;
+          if (sub == 0 && p.xd_out) p.xd_out[m * nblk + b] = ds;
+        }
+      }
+    }
+  } else {
+    // q8_K: one warp per 256-value block, lane l holds values 8l..8l+7
+    const int lane = tt & 31, nw = T / 32;
+    const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
+    for (int g = tt >> 5; g < M * nblk; g += nw) {
+      const int m = g / nblk, b = g - m * nblk;
+      const float* src = p.x_f32 + (int64_t)m * p.ldx + b * 256 + lane * 8;
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 c4 = *reinterpret_cast<const float4*>(src + 4);
+      const float v[8] = {a.x, a.y, a.z, a.w, c4.x, c4.y, c4.z, c4.w};
+      uint32_t qlo, qhi;
+      const float d = q8_K_quant8(v, lane, &qlo, &qhi);
+      const int o = lane >> 1;  // 16-value piece within the block
+      const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
+      *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + 4 * b + c) * 16 + (lane & 1) * 8) = make_uint2(qlo, qhi);
+      if (lane == 0) xscale[m * nblk + b] = d;
+      if (writer) {
+        *reinterpret_cast<uint2*>(p.xq_out + (int64_t)m * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
+        if (lane == 0 && p.xd_out) p.xd_out[m * nblk + b] = d;
+      }
+    }
+  }
+  __syncthreads();
+  // per-chunk activation sums: Q4_0 8 * (sum of the block's 32 values); TQ2_0 sum of the chunk's 64 values
+  for (int idx = tt; idx < M * C; idx += T) {
+    const int m = idx / C, c = idx - m * C;
+    const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * K);
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
+      const uint4 v = col[j * C + c];
+      sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
+    }
+    xsum[idx] = (FMT == 0) ? 8 * sum : sum;
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Integer block dots of one chunk: weight word w (4 words of 16 bytes) against the activation fields of column m.
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
+  return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+}
+
+template <int FMT, bool BYTES>
+__device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
+  if (!BYTES) {
+    if (FMT == 0) {
+      int lo = 0, hi = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wk = word_of(w, k);
+        lo = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(x[0], k), lo);
+        hi = dp4a_us(wk & 0xF0F0F0F0u, (int)word_of(x[1], k), hi);
+      }
+      return lo + (hi >> 4) - xsum;
+    } else {
+      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wk = word_of(w, k);
+        a0 = dp4a_us(wk & 0x03030303u, (int)word_of(x[0], k), a0);
+        a1 = dp4a_us(wk & 0x0C0C0C0Cu, (int)word_of(x[1], k), a1);
+        a2 = dp4a_us(wk & 0x30303030u, (int)word_of(x[2], k), a2);
+        a3 = dp4a_us(wk & 0xC0C0C0C0u, (int)word_of(x[3], k), a3);
+      }
+      return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - xsum;
+    }
+  } else {
+    // byte-wise variant (the reference's MODE 0): every value unpacked to an int32, no offset correction needed
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t wk = word_of(w, k);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int wb = (int)((wk >> (8 * t)) & 0xffu);
+#pragma unroll
+        for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
+          const int xb = (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
+          const int val = (FMT == 0) ? ((wb >> (4 * j)) & 15) - 8 : ((wb >> (2 * j)) & 3) - 1;
+          s += val * xb;
+        }
+      }
+    }
+    return s;
+  }
+}
+
+template <int R>
+struct WeightRegs {
+  uint4 w[R];
+  uint16_t sc[R];
+};
+
+template <int FMT, int R>
+__device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i, bool active, WeightRegs<R>& u) {
+  const int c = (int)threadIdx.x + i * (int)blockDim.x;
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int64_t row = g * R + r;
+    if (active && c < p.C && row < p.N) {
+      u.w[r] = ld_stream_v4(p.wq + row * p.ldwq + (int64_t)c * 16);
+      u.sc[r] = ld_stream_u16(p.ws + row * nblk + (c >> Fmt<FMT>::kChunkShift));
+    } else {
+      u.w[r] = make_uint4(0u, 0u, 0u, 0u);
+      u.sc[r] = 0;
+    }
+  }
+}
+
+template <int FMT, int R, int MC, bool BYTES>
+__global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int M = p.M, C = p.C;
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  uint8_t* xs = smem;                                                    // [M][K] permuted int8
+  int* xsum = reinterpret_cast<int*>(smem + (size_t)M * p.K);             // [M][C]
+  float* xscale = reinterpret_cast<float*>(xsum + M * C);                // [M][nblk]
+  float* red = xscale + M * nblk;                                        // [2][warps][R*MC]
+  const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // contiguous range of row groups for this CTA
+  const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
+  const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
+
+  WeightRegs<R> cur, nxt;
+  load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
+  stage_activations<FMT>(p, xs, xsum, xscale);
+
+  float acc[R][MC];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MC; ++m) acc[r][m] = 0.f;
+
+  int buf = 0;
+  int64_t g = g_begin;
+  int i = 0;
+  while (g < g_end) {
+    // prefetch the next unit
+    int64_t gn = g;
+    int in = i + 1;
+    if (in == p.CPT) {
+      in = 0;
+      gn = g + 1;
+    }
+    load_unit<FMT, R>(p, gn, in, gn < g_end, nxt);
+
+    const int c = (int)threadIdx.x + i * (int)blockDim.x;
+    const bool valid = c < C;
+    const int blk = c >> Fmt<FMT>::kChunkShift;
+    float dw[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) dw[r] = f16_bits_to_f32(cur.sc[r]);
+#pragma unroll
+    for (int m = 0; m < MC; ++m) {
+      if (m < M) {
+        uint4 x[4];
+        int xs_sum = 0;
+        float dx = 0.f;
+        if (valid) {
+          const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * p.K);
+#pragma unroll
+          for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = col[j * C + c];
+          xs_sum = xsum[m * C + c];
+          dx = xscale[m * nblk + blk];
+        } else {
+#pragma unroll
+          for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          int s = chunk_dot<FMT, BYTES>(cur.w[r], x, xs_sum);
+          if (FMT == 1) {  // a TQ2_0 block spans 4 adjacent threads: exact int32 sum of the 4 partial dots
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+          }
+          const bool lead = valid && (FMT == 0 || (c & 3) == 0);
+          const int64_t row = g * R + r;
+          if (lead && row < p.N) {
+            if (p.s) p.s[((int64_t)m * p.N + row) * nblk + blk] = s;
+            if (FMT == 0)
+              acc[r][m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), dx, acc[r][m]);
+            else
+              acc[r][m] = __fmaf_rn(__fmul_rn(dx, dw[r]), (float)s, acc[r][m]);
+          }
+        }
+      }
+    }
+
+    if (in == 0) {  // the unit's row group is complete: reduce across the CTA and store
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int m = 0; m < MC; ++m) {
+          float v = acc[r][m];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) red[(buf * nwarps + warp) * (R * MC) + r * MC + m] = v;
+          acc[r][m] = 0.f;
+        }
+      __syncthreads();
+      if ((int)threadIdx.x < R * MC) {
+        const int r = threadIdx.x / MC, m = threadIdx.x - (threadIdx.x / MC) * MC;
+        const int64_t row = g * R + r;
+        if (m < M && row < p.N) {
+          float v = 0.f;
+          for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * (R * MC) + threadIdx.x];
+          p.y[(int64_t)m * p.ldy + p.row0 + row] = v;
+        }
+      }
+      buf ^= 1;
+    }
+    cur = nxt;
+    g = gn;
+    i = in;
+  }
+
+  if (p.y_peers != nullptr) {
+    // fused all-gather: copy this CTA's output rows to every peer's copy of Y, then the last CTA runs the barrier
+    __syncthreads();
+    const int64_t r_begin = g_begin * R, r_end = min(g_end * R, p.N);
+    for (int m = 0; m < M; ++m) {
+      const int64_t base = (int64_t)m * p.ldy + p.row0;
+      for (int64_t row = r_begin + threadIdx.x; row < r_end; row += blockDim.x) {
+        const float v = p.y[base + row];
+        for (int q = 0; q < p.nranks; ++q)
+          if (q != p.rank) p.y_peers[q][base + row] = v;
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t* own = p.flags_peers[p.rank];
+      const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
+      if (arrived == gridDim.x - 1) {
+        own[p.nranks] = 0u;  // reset the arrival counter for the next call
+        __threadfence_system();
+        for (int q = 0; q < p.nranks; ++q) {
+          uint32_t* f = p.flags_peers[q] + p.rank;
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
+        }
+        int err = 0;
+        for (int q = 0; q < p.nranks && !err; ++q) {
+          long long spins = 0;
+          uint32_t v;
+          for (;;) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
+            if ((int32_t)(v - p.epoch) >= 0) break;
+            if (++spins > p.spin_limit) {
+              err = 1 + q;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+        if (err && p.status) *p.status = err;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Host side: planning and launch
+// ------------------------------------------------------------------------------------------------------------------
+
+using KernelFn = void (*)(const GemvParams);
+
+template <int FMT, bool BYTES>
+static KernelFn pick_kernel(int R, int MC) {
+  if (MC == 1) {
+    if (R == 1) return gemv_kernel<FMT, 1, 1, BYTES>;
+    if (R == 2) return gemv_kernel<FMT, 2, 1, BYTES>;
+    return gemv_kernel<FMT, 4, 1, BYTES>;
+  }
+  if (R == 1) return gemv_kernel<FMT, 1, 4, BYTES>;
+  if (R == 2) return gemv_kernel<FMT, 2, 4, BYTES>;
+  return gemv_kernel<FMT, 4, 4, BYTES>;
+}
+
+static KernelFn kernel_for(int fmt, bool bytes, int R, int MC) {
+  if (fmt == 0) return bytes ? pick_kernel<0, true>(R, MC) : pick_kernel<0, false>(R, MC);
+  return bytes ? pick_kernel<1, true>(R, MC) : pick_kernel<1, false>(R, MC);
+}
+
+struct OccKey {
+  int dev;
+  KernelFn fn;
+  int threads;
+  size_t smem;
+  bool operator==(const OccKey& o) const {
+    return dev == o.dev && fn == o.fn && threads == o.threads && smem == o.smem;
+  }
+};
+struct OccHash {
+  size_t operator()(const OccKey& k) const {
+    return std::hash<const void*>()((const void*)k.fn) ^ (k.threads * 131u) ^ (k.smem * 7919u) ^ (k.dev * 31u);
+  }
+};
+static std::mutex g_occ_mu;
+static std::unordered_map<OccKey, int, OccHash> g_occ;
+
+// Resident CTAs per SM for this kernel and launch shape (opts the kernel into large dynamic shared memory first).
+static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  OccKey key{dev, fn, threads, smem};
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
+  if (cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_optin) !=
+      cudaSuccess)
+    return -1;
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, (const void*)fn, threads, smem) != cudaSuccess)
+    return -1;
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  g_occ[key] = blocks;
+  return blocks;
+}
+
+static int g_tune_rows = 0;   // 0 = planner's choice
+static int g_tune_cpt = 0;
+static int g_tune_grid = 0;
+
+struct Plan {
+  int R, T, CPT, grid;
+  size_t smem;
+  KernelFn fn;
+};
+
+static size_t smem_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T) {
+  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  return (size_t)M * K + (size_t)M * C * 4 + (size_t)M * nblk * 4 + (size_t)2 * (T / 32) * R * MC * 4;
+}
+
+static int make_plan(int fmt, bool bytes, int64_t N, int64_t K, int M, Plan* out) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int C = (int)(K / (fmt == 0 ? 32 : 64));
+  const int MC = M == 1 ? 1 : kMaxColumns;
+  int CPT = (C + kMaxThreads - 1) / kMaxThreads;
+  if (g_tune_cpt > 0) CPT = g_tune_cpt;
+  const int T = std::min(kMaxThreads, ((C + CPT - 1) / CPT + 31) / 32 * 32);
+  if ((int64_t)T * CPT < C)
+    return fail(B2Q_ERANGE, "gemv: K=%lld needs more than %d chunks per thread", (long long)K, CPT);
+  Plan best{};
+  double best_eff = -1.0;
+  const int cand[3] = {4, 2, 1};
+  for (int ci = 0; ci < 3; ++ci) {
+    const int R = cand[ci];
+    if (g_tune_rows > 0 && R != g_tune_rows) continue;
+    const size_t smem = smem_bytes(fmt, K, M, C, R, MC, T);
+    if (smem > (size_t)di.max_smem_optin) continue;
+    KernelFn fn = kernel_for(fmt, bytes, R, MC);
+    const int occ = occupancy(fn, T, smem, di.max_smem_optin);
+    if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
+    if (occ == 0) continue;
+    const int64_t groups = (N + R - 1) / R;
+    int64_t grid = std::min<int64_t>(groups, (int64_t)occ * di.sms);
+    if (g_tune_grid > 0) grid = std::min<int64_t>(groups, g_tune_grid);
+    // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
+    const int64_t per = (groups + grid - 1) / grid;
+    double eff = (double)groups / (double)(per * grid);
+    // shorter rows amortize less per reduction: prefer larger R on near-ties
+    eff += 0.002 * R;
+    if (eff > best_eff) {
+      best_eff = eff;
+      best = Plan{R, T, CPT, (int)grid, smem, fn};
+    }
+  }
+  if (best_eff < 0)
+    return fail(B2Q_ERANGE, "gemv: K=%lld with %d columns does not fit in shared memory (%d bytes max)",
+                (long long)K, M, di.max_smem_optin);
+  *out = best;
+  return B2Q_OK;
+}
+
+static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws,
+                           const void* x, const float* xd, const float* y, int64_t N, int64_t K, int64_t M,
+                           bool f32_input) {
+  const int blk = fmt == 0 ? 32 : 256;
+  if (N < 0 || K < 0 || M < 0) return fail(B2Q_EINVAL, "%s: negative size", who);
+  if (K % blk) return fail(B2Q_EINVAL, "%s: K=%lld is not a multiple of the %d-value block", who, (long long)K, blk);
+  if (N == 0 || M == 0) return B2Q_OK;  // empty output: no pointer is touched
+  if (!y) return fail(B2Q_EINVAL, "%s: null pointer", who);
+  if (!aligned(y, 4)) return fail(B2Q_EALIGN, "%s: y must be 4-byte aligned", who);
+  if (K == 0) return B2Q_OK;  // empty sums: only Y (= 0) is written
+  if (!wq || !ws || !x || (!f32_input && !xd)) return fail(B2Q_EINVAL, "%s: null pointer", who);
+  const int64_t qbytes = K / (fmt == 0 ? 2 : 4);
+  if (ldwq < qbytes) return fail(B2Q_EINVAL, "%s: ldwq=%lld < %lld quant bytes per row", who, (long long)ldwq,
+                                 (long long)qbytes);
+  if (!aligned(wq, 16) || (ldwq % 16)) return fail(B2Q_EALIGN, "%s: wq must be 16-byte aligned, ldwq %% 16 == 0", who);
+  if (!aligned(ws, 2)) return fail(B2Q_EALIGN, "%s: ws must be 2-byte aligned", who);
+  if (!aligned(x, 16)) return fail(B2Q_EALIGN, "%s: activations must be 16-byte aligned", who);
+  if (xd && !aligned(xd, 4)) return fail(B2Q_EALIGN, "%s: xd must be 4-byte aligned", who);
+  if (K > (int64_t)1 << 30 || N > ((int64_t)1 << 40)) return fail(B2Q_ERANGE, "%s: size too large", who);
+  return B2Q_OK;
+}
+
+struct LaunchArgs {
+  int fmt;
+  bool bytes;
+  const uint8_t* wq;
+  int64_t ldwq;
+  const int16_t* ws;
+  const int8_t* xq;
+  const float* xd;
+  const float* x_f32;
+  int64_t ldx;
+  int8_t* xq_out;
+  float* xd_out;
+  float* y;
+  int64_t ldy;
+  int64_t row0;
+  int32_t* s;
+  float* const* y_peers;
+  uint32_t* const* flags_peers;
+  int32_t* status;
+  int rank, nranks;
+  uint32_t epoch;
+  long long spin_limit;
+  int64_t N, K, M;
+};
+
+static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
+  if (a.N == 0 || a.M == 0 || a.K == 0) {
+    // empty reductions: Y = 0 (K == 0); nothing to do for N == 0 or M == 0
+    if (a.K == 0 && a.N > 0 && a.M > 0) {
+      for (int64_t m = 0; m < a.M; ++m) {
+        cudaError_t e = cudaMemsetAsync(a.y + m * a.ldy + a.row0, 0, (size_t)a.N * 4, stream);
+        if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemv: cudaMemsetAsync: %s", cudaGetErrorString(e));
+      }
+    }
+    return B2Q_OK;
+  }
+  const int blk = a.fmt == 0 ? 32 : 256;
+  const int64_t nblk = a.K / blk;
+  for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
+    const int Mc = (int)std::min<int64_t>(kMaxColumns, a.M - m0);
+    Plan pl;
+    int rc = make_plan(a.fmt, a.bytes, a.N, a.K, Mc, &pl);
+    if (rc) return rc;
+    GemvParams p{};
+    p.wq = a.wq;
+    p.ldwq = a.ldwq;
+    p.ws = a.ws;
+    p.xq = a.xq ? a.xq + m0 * a.K : nullptr;
+    p.xd = a.xd ? a.xd + m0 * nblk : nullptr;
+    p.x_f32 = a.x_f32 ? a.x_f32 + m0 * a.ldx : nullptr;
+    p.ldx = a.ldx;
+    p.xq_out = a.xq_out ? a.xq_out + m0 * a.K : nullptr;
+    p.xd_out = a.xd_out ? a.xd_out + m0 * nblk : nullptr;
+    p.y = a.y + m0 * a.ldy;
+    p.ldy = a.ldy;
+    p.row0 = a.row0;
+    p.s = a.s ? a.s + m0 * a.N * nblk : nullptr;
+    p.y_peers = a.y_peers;  // the exchange path is limited to one column group (M <= kMaxColumns) by its entry point
+    p.flags_peers = a.flags_peers;
+    p.status = a.status;
+    p.rank = a.rank;
+    p.nranks = a.nranks;
+    p.epoch = a.epoch;
+    p.spin_limit = a.spin_limit;
+    p.N = a.N;
+    p.K = a.K;
+    p.M = Mc;
+    p.C = (int)(a.K / (a.fmt == 0 ? 32 : 64));
+    p.CPT = pl.CPT;
+    p.groups = (a.N + pl.R - 1) / pl.R;
+    pl.fn<<<pl.grid, pl.T, pl.smem, stream>>>(p);
+    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
+    if (rc) return rc;
+  }
+  return B2Q_OK;
+}
+
+}  // namespace b2q
+
+using namespace b2q;
+
+extern "C" {
+
+int b2q_gemv_q4_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
+  int rc = check_gemv_args("b2q_gemv_q4_0", 0, wq, ldwq, ws, xq, xd, y, N, K, M, false);
+  if (rc) return rc;
+  if (variant < 0 || variant > 2) return fail(B2Q_EINVAL, "b2q_gemv_q4_0: variant %d not in 0..2", variant);
+  if (s && !aligned(s, 4)) return fail(B2Q_EALIGN, "b2q_gemv_q4_0: s must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = 0;
+  a.bytes = variant == B2Q_VARIANT_BYTES;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.xq = xq, a.xd = xd, a.y = y, a.ldy = N, a.s = s;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
+int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                   int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
+  int rc = check_gemv_args("b2q_gemv_tq2_0", 1, wq, ldwq, ws, xq, xd, y, N, K, M, false);
+  if (rc) return rc;
+  if (variant < 0 || variant > 2) return fail(B2Q_EINVAL, "b2q_gemv_tq2_0: variant %d not in 0..2", variant);
+  if (s && !aligned(s, 4)) return fail(B2Q_EALIGN, "b2q_gemv_tq2_0: s must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = 1;
+  a.bytes = variant == B2Q_VARIANT_BYTES;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.xq = xq, a.xd = xd, a.y = y, a.ldy = N, a.s = s;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
+int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                   int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream) {
+  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not Q4_0 (0) or TQ2_0 (1)", fmt);
+  int rc = check_gemv_args("b2q_quant_gemv", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
+  if (rc) return rc;
+  if (ldx < K || (ldx % 4)) return fail(B2Q_EALIGN, "b2q_quant_gemv: ldx must be >= K and a multiple of 4");
+  if ((xq == nullptr) != (xd == nullptr)) return fail(B2Q_EINVAL, "b2q_quant_gemv: give both xq and xd, or neither");
+  if (xq && !aligned(xq, 16)) return fail(B2Q_EALIGN, "b2q_quant_gemv: xq must be 16-byte aligned");
+  if (xd && !aligned(xd, 4)) return fail(B2Q_EALIGN, "b2q_quant_gemv: xd must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = fmt;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx, a.xq_out = xq, a.xd_out = xd, a.y = y, a.ldy = N;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
+int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq,
+                       const float* xd, float* const* y_peers, uint32_t* const* flags_peers, int32_t* status,
+                       int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M, int rank, int nranks,
+                       uint32_t epoch, long long spin_limit, b2q_stream_t stream) {
+  (void)fmt;
+  (void)wq;
+  (void)ldwq;
+  (void)ws;
+  (void)xq;
+  (void)xd;
+  (void)y_peers;
+  (void)flags_peers;
+  (void)status;
+  (void)row0;
+  (void)n_local;
+  (void)N_total;
+  (void)K;
+  (void)M;
+  (void)rank;
+  (void)nranks;
+  (void)epoch;
+  (void)spin_limit;
+  (void)stream;
+  return fail(B2Q_EINVAL, "b2q_gemv_allgather: not enabled in this build");
+}
+
+// Benchmark/tuning hook: force rows per group (1, 2, 4), chunks per thread and grid size; 0 restores the planner.
+int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
+  if (rows_per_group != 0 && rows_per_group != 1 && rows_per_group != 2 && rows_per_group != 4)
+    return fail(B2Q_EINVAL, "b2q_set_tuning: rows_per_group must be 0, 1, 2 or 4");
+  if (chunks_per_thread < 0 || grid < 0) return fail(B2Q_EINVAL, "b2q_set_tuning: negative value");
+  g_tune_rows = rows_per_group;
+  g_tune_cpt = chunks_per_thread;
+  g_tune_grid = grid;
+  return B2Q_OK;
+}
+
+}  // extern "C"

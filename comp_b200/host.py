@@ -1,0 +1,233 @@
+"""Host side of the B200 backend: KURN split layouts from ggml blocks, and the CUDA launches.
+
+Drop-in for COMP's `komp.host` (src/komp/host.py): same names, argument meanings and return values. `quantize` and
+`gemv` launch this package's sm_100a kernels through the C-ABI library (include/comp_b200.h); they take CUDA
+tensors only and raise on anything else -- there is no CPU path.
+
+Tuning arguments of the Triton kernels (`bb`, `block_n`, `nb`, `num_warps`) are accepted and ignored: the CUDA
+schedule is planned from (N, K, M) by the library, and results do not depend on them. `mode` selects the variant:
+0 = byte-wise unpack, 1 or 2 = packed-word dp4a; all variants give identical int32 block dots and identical Y.
+"""
+
+import numpy as np
+import torch
+
+from . import _lib
+
+# weights: block values, block bytes, quant offset/bytes in the ggml block, scale offset, activation format
+# (the same table as src/komp/host.py:9-12)
+FORMATS = {
+    "q4_0": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
+    "tq2_0": dict(block=256, nbytes=66, qoff=0, qbytes=64, soff=64, act="q8_K"),
+}
+MODES = {"bytes": 0, "dp4a": 2}  # src/komp/host.py:13
+ACT_BLOCK = {"q8_0": 32, "q8_K": 256}
+FMT_ID = {"q4_0": 0, "tq2_0": 1}
+
+
+def _fmt(fmt):
+    if fmt not in FORMATS:
+        raise ValueError(f"unknown weight format {fmt!r}: expected one of {sorted(FORMATS)}")
+    return FORMATS[fmt]
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Layout helpers (numpy, host memory). Same semantics as src/komp/host.py:16-56.
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def split(fmt, W, n, k):
+    """ggml blocks (bytes, n rows of k values) -> (WQ uint8 [n][quant bytes per row], WS int16 [n][k/block])."""
+    f = _fmt(fmt)
+    if k % f["block"]:
+        raise ValueError(f"k={k} is not a multiple of the {fmt} block ({f['block']})")
+    nb = k // f["block"]
+    raw = np.frombuffer(W, dtype=np.uint8)
+    if raw.size != n * nb * f["nbytes"]:
+        raise ValueError(f"{raw.size} bytes do not hold {n} x {nb} {fmt} blocks of {f['nbytes']} bytes")
+    blocks = raw.reshape(n, nb, f["nbytes"])
+    wq = blocks[:, :, f["qoff"] : f["qoff"] + f["qbytes"]].reshape(n, nb * f["qbytes"]).copy()
+    ws = blocks[:, :, f["soff"] : f["soff"] + 2].copy().view(np.int16).reshape(n, nb)
+    return wq, ws
+
+
+def split_q4_0(W, n, k):
+    return split("q4_0", W, n, k)
+
+
+def tq2_0_qplane(W, nblk):
+    """ggml tq2_0 blocks -> quant plane uint8 [nblk][64] (the f16 scale at byte 64 goes to the scale plane)."""
+    return np.frombuffer(W, dtype=np.uint8).reshape(nblk, 66)[:, :64].copy()
+
+
+def q8_0_blocks(xq, xd):
+    """q8_0 split planes (numpy) -> ggml q8_0 blocks (bytes): f16 d, then 32 int8 per block."""
+    xq, xd = np.asarray(xq), np.asarray(xd)
+    m, k = xq.shape
+    nb = k // 32
+    out = np.empty((m, nb, 34), dtype=np.uint8)
+    out[:, :, 0:2] = np.asarray(xd, dtype=np.float32).astype(np.float16).view(np.uint8).reshape(m, nb, 2)
+    out[:, :, 2:34] = xq.astype(np.int8).view(np.uint8).reshape(m, nb, 32)
+    return out.tobytes()
+
+
+def q8_K_bsums(xq):
+    """int16 sums of each run of 16 quants: [m][k/256][16] (ggml block_q8_K.bsums)."""
+    xq = np.asarray(xq)
+    m, k = xq.shape
+    return xq.astype(np.int32).reshape(m, k // 256, 16, 16).sum(axis=-1).astype(np.int16)
+
+
+def q8_K_blocks(xq, xd):
+    """q8_K split planes (numpy) -> ggml q8_K blocks (bytes): f32 d, 256 int8, 16 int16 bsums."""
+    xq, xd = np.asarray(xq), np.asarray(xd)
+    m, k = xq.shape
+    nb = k // 256
+    out = np.empty((m, nb, 292), dtype=np.uint8)
+    out[:, :, 0:4] = np.asarray(xd, dtype=np.float32).view(np.uint8).reshape(m, nb, 4)
+    out[:, :, 4:260] = xq.astype(np.int8).view(np.uint8).reshape(m, nb, 256)
+    out[:, :, 260:292] = q8_K_bsums(xq).view(np.uint8).reshape(m, nb, 32)
+    return out.tobytes()
+
+
+def act_blocks(fmt, xq, xd):
+    return (q8_0_blocks if _fmt(fmt)["act"] == "q8_0" else q8_K_blocks)(xq, xd)
+
+
+def device():
+    """'cuda' when a GPU is visible. Unlike the reference there is no CPU execution: compute calls need CUDA."""
+    return "cuda" if torch.cuda.is_available() else "cpu"
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Launches
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def _need_cuda(name, *tensors):
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+            raise RuntimeError(f"comp_b200.{name}: tensors must be CUDA tensors (this backend has no CPU path)")
+    dev = tensors[0].device
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise RuntimeError(f"comp_b200.{name}: tensors on different devices ({dev} and {t.device})")
+    return dev
+
+
+def _check(t, name, dtype, shape):
+    if t.dtype != dtype:
+        raise TypeError(f"{name}: dtype {t.dtype}, expected {dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _rows_aligned(t):
+    """Returns a tensor with unit column stride and a 16-byte aligned base (copies only when needed)."""
+    if t.stride(-1) != 1 or t.data_ptr() % 16 or (t.dim() == 2 and t.stride(0) % 4):
+        t = t.clone(memory_format=torch.contiguous_format)
+    return t
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def quantize(fmt, x, bb=4):
+    """f32 [M][K] CUDA tensor -> (XQ int8 [M][K], XD f32 [M][K/block]) with the q8_0 / q8_K quantizer of `fmt`'s
+    activation format (src/komp/host.py:63-73). Bytes equal ggml's reference quantizers."""
+    del bb  # Triton block-count hint; the CUDA kernel has its own schedule
+    act = _fmt(fmt)["act"]
+    dev = _need_cuda("quantize", x)
+    if x.dtype != torch.float32 or x.dim() != 2:
+        raise TypeError(f"quantize: x must be a 2-D float32 tensor, got {x.dtype} {tuple(x.shape)}")
+    m, k = x.shape
+    blk = ACT_BLOCK[act]
+    if k % blk:
+        raise ValueError(f"quantize: K={k} is not a multiple of the {act} block ({blk})")
+    x = _rows_aligned(x)
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xd = torch.empty((m, k // blk), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        if act == "q8_0":
+            _lib.call("b2q_quant_q8_0", x.data_ptr(), x.stride(0), xq.data_ptr(), xd.data_ptr(), m, k, _stream(dev))
+        else:
+            _lib.call("b2q_quant_q8_K", x.data_ptr(), x.stride(0), xq.data_ptr(), xd.data_ptr(), None, m, k,
+                      _stream(dev))
+    return xq, xd
+
+
+def quantize_q8_K_bsums(x):
+    """q8_K of f32 [M][K] -> (XQ, XD, bsums int16 [M][K/256][16]): the full ggml block_q8_K content, on the GPU."""
+    dev = _need_cuda("quantize_q8_K_bsums", x)
+    m, k = x.shape
+    if k % 256:
+        raise ValueError(f"K={k} is not a multiple of 256")
+    x = _rows_aligned(x)
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xd = torch.empty((m, k // 256), dtype=torch.float32, device=dev)
+    bs = torch.empty((m, k // 256, 16), dtype=torch.int16, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("b2q_quant_q8_K", x.data_ptr(), x.stride(0), xq.data_ptr(), xd.data_ptr(), bs.data_ptr(), m, k,
+                  _stream(dev))
+    return xq, xd, bs
+
+
+def _check_weights(fmt, wq, ws, n, k):
+    f = _fmt(fmt)
+    if k % f["block"]:
+        raise ValueError(f"gemv: k={k} is not a multiple of the {fmt} block ({f['block']})")
+    qbytes = k // f["block"] * f["qbytes"]
+    if wq.dtype != torch.uint8 or wq.dim() != 2 or wq.shape[0] != n or wq.shape[1] < qbytes or wq.stride(1) != 1:
+        raise ValueError(f"gemv: wq must be uint8 [{n}][>= {qbytes}] with unit column stride, got {wq.dtype} "
+                         f"{tuple(wq.shape)}")
+    _check(ws, "ws", torch.int16, (n, k // f["block"]))
+    if not ws.is_contiguous():
+        raise ValueError("gemv: ws must be contiguous")
+
+
+def gemv(fmt, wq, ws, xq, xd, n, k, block_n=32, nb=4, mode=0, num_warps=4, store_s=False):
+    """-> (Y f32 [M][N], S int32 [M][N][blocks] or None) (src/komp/host.py:76-85).
+
+    mode: 0 bytes, 1 dp4a (the reference's interpreter fallback), 2 dp4a; all give identical results."""
+    del block_n, nb, num_warps  # Triton schedule hints; the CUDA schedule is planned by the library
+    f = _fmt(fmt)
+    if mode not in (0, 1, 2):
+        raise ValueError(f"gemv: mode {mode} not in (0, 1, 2)")
+    dev = _need_cuda("gemv", wq, ws, xq, xd)
+    _check_weights(fmt, wq, ws, n, k)
+    m = xq.shape[0]
+    _check(xq, "xq", torch.int8, (m, k))
+    _check(xd, "xd", torch.float32, (m, k // f["block"]))
+    xq = _rows_aligned(xq.contiguous())
+    xd = xd.contiguous()
+    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    s = torch.empty((m, n, k // f["block"]), dtype=torch.int32, device=dev) if store_s else None
+    name = "b2q_gemv_q4_0" if fmt == "q4_0" else "b2q_gemv_tq2_0"
+    with torch.cuda.device(dev):
+        _lib.call(name, wq.data_ptr(), wq.stride(0), ws.data_ptr(), xq.data_ptr(), xd.data_ptr(), y.data_ptr(),
+                  s.data_ptr() if store_s else None, n, k, m, mode, _stream(dev))
+    return y, s
+
+
+def quant_gemv(fmt, wq, ws, x, n, k, return_act=False):
+    """Fused quantize + gemv in one launch: f32 x [M][K] -> Y f32 [M][N] (and (XQ, XD) when return_act).
+
+    Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule, same f32 order)."""
+    f = _fmt(fmt)
+    dev = _need_cuda("quant_gemv", wq, ws, x)
+    _check_weights(fmt, wq, ws, n, k)
+    if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != k:
+        raise ValueError(f"quant_gemv: x must be float32 [M][{k}], got {x.dtype} {tuple(x.shape)}")
+    m = x.shape[0]
+    x = _rows_aligned(x)
+    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    xq = xd = None
+    if return_act:
+        xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+        xd = torch.empty((m, k // f["block"]), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("b2q_quant_gemv", FMT_ID[fmt], wq.data_ptr(), wq.stride(0), ws.data_ptr(), x.data_ptr(),
+                  x.stride(0), xq.data_ptr() if return_act else None, xd.data_ptr() if return_act else None,
+                  y.data_ptr(), n, k, m, _stream(dev))
+    return (y, xq, xd) if return_act else y

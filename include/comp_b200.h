@@ -1,0 +1,149 @@
+/*
+ * comp_b200.h -- C ABI of the B200-native quantized decode path.
+ *
+ * Four operations on KURN's `split` layout, each a drop-in for one COMP (komp) Triton kernel:
+ *
+ *   quant_q8_0   f32 activations [M][K] -> int8 XQ [M][K] + f32 XD [M][K/32]   (ggml quantize_row_q8_0_ref)
+ *   quant_q8_K   f32 activations [M][K] -> int8 XQ [M][K] + f32 XD [M][K/256]  (ggml quantize_row_q8_K_ref)
+ *   gemv_q4_0    Q4_0 weights (WQ u8 [N][K/2], WS f16 bits [N][K/32]) x q8_0 activations -> Y f32 [M][N]
+ *   gemv_tq2_0   TQ2_0 weights (WQ u8 [N][K/4], WS f16 bits [N][K/256]) x q8_K activations -> Y f32 [M][N]
+ *
+ * Conventions shared by every entry point:
+ *   - All data pointers are DEVICE pointers of the current CUDA device; the library never allocates or frees
+ *     device memory (the caller owns every buffer).
+ *   - Sizes and strides are int64 element counts (bytes for u8/i8 planes).
+ *   - Work is enqueued on `stream` (NULL = legacy default stream) and is asynchronous.
+ *   - Return 0 on success, a negative B2Q_E* code otherwise; b2q_last_error() gives the message for the calling
+ *     thread. Nothing aborts the process.
+ *   - Alignment: x, xq and wq must be 16-byte aligned, with ldx % 4 == 0 and ldwq % 16 == 0 (the layouts the
+ *     reference's typed signatures assume: 16-byte aligned pointers, K % 32 == 0).
+ *
+ * The matching COMP (reference) interfaces are cited per entry point as path:line inside the komp project.
+ */
+#ifndef COMP_B200_H
+#define COMP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; declared here so FFI users need no CUDA header. */
+typedef struct CUstream_st* b2q_stream_t;
+
+#define B2Q_OK 0
+#define B2Q_EINVAL (-1)    /* bad shape / null pointer / K not a multiple of the block */
+#define B2Q_EALIGN (-2)    /* pointer or stride misaligned */
+#define B2Q_ECUDA (-3)     /* CUDA runtime error (launch, attribute, device query) */
+#define B2Q_ERANGE (-4)    /* size beyond what this build supports (e.g. K*M too large for shared memory) */
+#define B2Q_ETIMEOUT (-5)  /* a bounded device-side wait gave up (multi-GPU exchange) */
+
+/* Weight formats and GEMV variants. Variant 0 = byte-wise unpack ("bytes"), 1/2 = packed-word dp4a ("dp4a").
+ * All variants return identical int32 block dots and identical Y. Mirrors host.MODES (src/komp/host.py:13). */
+#define B2Q_FMT_Q4_0 0
+#define B2Q_FMT_TQ2_0 1
+#define B2Q_VARIANT_BYTES 0
+#define B2Q_VARIANT_DP4A 2
+
+/* Library version string, e.g. "comp_b200 0.1.0 sm_100a". */
+const char* b2q_version(void);
+
+/* Copies the calling thread's last error message into buf (always NUL-terminated); returns its full length. */
+int b2q_last_error(char* buf, size_t len);
+
+/* Number of kernels this library has launched in this process (all devices, all threads). */
+long long b2q_launch_count(void);
+
+/*
+ * Activation quantizer, q8_0 (32-value blocks): per block d = amax/127 (IEEE div), id = 1/d (0 if d == 0),
+ * q = roundf(x*id) with q from the unrounded f32 d, XD = f32(f16_rne(d)).
+ * Replaces kernel quant_q8_0 (src/komp/kernels.py:22-33) launched by host.quantize (src/komp/host.py:63-69);
+ * math of ktl.q8_0_quantize (patches/0001-language-extra-kurn.patch:104-114).
+ * x: f32 [M][ldx] (first K columns used); xq: int8 [M][K]; xd: f32 [M][K/32]. K % 32 == 0.
+ */
+int b2q_quant_q8_0(const float* x, int64_t ldx, int8_t* xq, float* xd, int64_t M, int64_t K, b2q_stream_t stream);
+
+/*
+ * Activation quantizer, q8_K (256-value blocks): signed max-|x| (first index on ties), iscale = -127/max,
+ * q = min(127, rint(iscale*x)), d = 1/iscale; all-zero block -> q = 0, d = 0.
+ * Replaces kernel quant_q8_K (src/komp/kernels.py:36-45) launched by host.quantize (src/komp/host.py:70-72);
+ * math of ktl.q8_K_quantize (patch:117-131). bsums (nullable) receives ggml's 16 int16 sums of 16 quants per
+ * block, [M][K/256][16], which host.q8_K_blocks (src/komp/host.py:43-52) adds on the host in the reference.
+ */
+int b2q_quant_q8_K(const float* x, int64_t ldx, int8_t* xq, float* xd, int16_t* bsums, int64_t M, int64_t K,
+                   b2q_stream_t stream);
+
+/*
+ * Q4_0 x q8_0 decode GEMV: Y[m][n] = sum_b f32(s[m][n][b]) * dw[n][b] * dx[m][b], with s the exact int32 block dot
+ * sum_i (nibble_i - 8) * xq_i. Replaces kernel q4_0_gemv (src/komp/kernels.py:48-94) launched by host.gemv
+ * (src/komp/host.py:76-85).
+ *   wq: u8 [N][ldwq] quant plane (16 bytes per 32-value block; byte i = value i (low nibble), value i+16 (high))
+ *   ws: int16 [N][K/32] f16 bit patterns of the block scales
+ *   xq: int8 [M][K], xd: f32 [M][K/32]  (q8_0 split planes from b2q_quant_q8_0)
+ *   y:  f32 [M][N]
+ *   s:  int32 [M][N][K/32] or NULL: when given, every int32 block dot is stored (host.gemv store_s=True).
+ *   variant: B2Q_VARIANT_BYTES or B2Q_VARIANT_DP4A (1 is accepted as DP4A).
+ */
+int b2q_gemv_q4_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
+
+/*
+ * TQ2_0 x q8_K decode GEMV: Y[m][n] = sum_b dx[m][b] * dw[n][b] * f32(s[m][n][b]), s = sum_v (crumb_v - 1) * xq_v
+ * where value v of a block is in quant byte (v/128)*32 + v%32 at bits 2*((v%128)/32).
+ * Replaces kernel tq2_0_gemv (src/komp/kernels.py:97-142) launched by host.gemv (src/komp/host.py:76-85).
+ *   wq: u8 [N][ldwq] (64 bytes per 256-value block), ws: int16 [N][K/256], xq: int8 [M][K], xd: f32 [M][K/256],
+ *   y: f32 [M][N], s: int32 [M][N][K/256] or NULL.
+ */
+int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                   int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
+
+/*
+ * Fused quantizer prologue + GEMV (one launch): every CTA quantizes f32 x into shared memory with exactly the math of
+ * b2q_quant_q8_0 / b2q_quant_q8_K, then runs the GEMV. xq/xd (nullable) also receive the quantized activations
+ * (written by CTA 0 only), byte-identical to the standalone quantizer. fmt = B2Q_FMT_Q4_0 or B2Q_FMT_TQ2_0.
+ * Fuses host.quantize + host.gemv (src/komp/host.py:63-85) into one kernel; no reference counterpart as one call.
+ */
+int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                   int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream);
+
+/*
+ * Row-sharded GEMV with the output all-gather fused into the epilogue (multi-GPU, one process per GPU).
+ * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows.
+ * Every output value is stored to y_peers[p] + m*N_total + row0 + r for every rank p (P2P stores over NVLink),
+ * then the ranks meet at a flag barrier: rank r writes `epoch` into flags_peers[p][r] for every p and waits,
+ * for at most `spin_limit` polls per peer, until its own flags[q] >= epoch for every q.
+ * y_peers / flags_peers are device arrays (length nranks) of peer-mapped pointers (CUDA IPC), flags are uint32.
+ * Returns B2Q_ETIMEOUT if a peer never arrived (the device writes a nonzero code to *status, a device int32).
+ * No reference counterpart (the reference has no multi-GPU path); replaces an NCCL all-gather after host.gemv.
+ */
+int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq,
+                       const float* xd, float* const* y_peers, uint32_t* const* flags_peers, int32_t* status,
+                       int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M, int rank, int nranks,
+                       uint32_t epoch, long long spin_limit, b2q_stream_t stream);
+
+/* Benchmark/tuning hook (process-wide): force rows per group (1, 2, 4), chunks per thread and grid size of the
+ * GEMV schedule; 0 restores the planner's choice. Results do not depend on it (except the f32 summation order). */
+int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid);
+
+/* CUDA IPC helpers for the multi-GPU path: export a device allocation as a 64-byte handle, open a peer's handle. */
+int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64);
+int b2q_ipc_open_handle(const void* handle64, void** dev_ptr_out);
+int b2q_ipc_close_handle(void* dev_ptr);
+
+/*
+ * Unit probes (test-only counterparts of the reference's probe kernels):
+ *   b2q_probe_dp4a:    out[i] = c[i] + dot of the 4 signed bytes of a[i], b[i]  (kernels.py:145-149, dp4a_probe)
+ *   b2q_decode_q4_0:   [R][16] quant bytes -> [R][32] int32 values nibble-8 in natural order (kernels.py:152-157)
+ *   b2q_decode_tq2_0:  [R][64] quant bytes -> [R][256] int32 values crumb-1 in value order (kernels.py:160-170)
+ */
+int b2q_probe_dp4a(const int32_t* a, const int32_t* b, const int32_t* c, int32_t* out, int64_t n, b2q_stream_t stream);
+int b2q_decode_q4_0(const uint8_t* wq, int32_t* out, int64_t R, b2q_stream_t stream);
+int b2q_decode_tq2_0(const uint8_t* wq, int32_t* out, int64_t R, b2q_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COMP_B200_H */

@@ -1,0 +1,325 @@
+"""TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): numpy restatement of the reference's math.
+
+Each function cites the reference file:line it restates (paths inside the komp project). Float work is done in the
+precision the reference uses (f32 for the quantizers, IEEE round-to-nearest; f64 for KURN's reference dot), so the
+results are bit-identical, not approximate.
+"""
+
+import numpy as np
+
+BLOCK = {"q4_0": 32, "tq2_0": 256}
+ACT = {"q4_0": "q8_0", "tq2_0": "q8_K"}
+QBYTES = {"q4_0": 16, "tq2_0": 64}
+NBYTES = {"q4_0": 18, "tq2_0": 66}
+TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:113)
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Rounding (patches/0001-language-extra-kurn.patch:84-101)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def round_half_away(x):
+    """roundf(): nearest integer, halfway cases away from zero (patch:85-90). f32 in, f32 out, exact."""
+    x = np.asarray(x, dtype=F32)
+    a = np.abs(x)
+    f = np.floor(a)
+    r = np.where(a - f >= F32(0.5), f + F32(1), f).astype(F32)
+    return np.where(x < 0, -r, r).astype(F32)
+
+
+def round_half_even(x):
+    """nearbyint() in round-to-nearest-even mode (patch:94-101). numpy's rint is exactly that."""
+    return np.rint(np.asarray(x, dtype=F32)).astype(F32)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Activation quantizers
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def quant_q8_0(x):
+    """f32 [M][K] -> (xq int8 [M][K], xd f32 [M][K/32]): ggml quantize_row_q8_0_ref as restated by
+    ktl.q8_0_quantize (patch:104-114) and stored by kernel quant_q8_0 (src/komp/kernels.py:22-33):
+    d = amax / 127 (f32 division), id = 1/d (0 when d == 0), q = roundf(x * id) from the UNROUNDED d,
+    stored scale = f32(f16(d))."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    m, k = x.shape
+    if k % 32:
+        raise ValueError("K must be a multiple of 32")
+    b = x.reshape(m, k // 32, 32)
+    amax = np.abs(b).max(axis=-1) if k else np.zeros((m, 0), F32)
+    d = (amax / F32(127)).astype(F32)
+    nz = d != 0
+    idv = np.where(nz, (F32(1) / np.where(nz, d, F32(1))).astype(F32), F32(0)).astype(F32)
+    q = round_half_away((b * idv[..., None]).astype(F32))
+    return q.astype(np.int8).reshape(m, k), d.astype(np.float16).astype(F32)
+
+
+def quant_q8_K(x):
+    """f32 [M][K] -> (xq int8 [M][K], xd f32 [M][K/256], bsums int16 [M][K/256][16]): ggml quantize_row_q8_K_ref
+    as restated by ktl.q8_K_quantize (patch:117-131) with the bsums host.q8_K_blocks adds (src/komp/host.py:43-52).
+    mx = the signed value of largest magnitude, lowest index on ties; iscale = -127/mx; q = min(127, rint(iscale*x));
+    d = 1/iscale; an all-zero block gives q = 0, d = 0."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    m, k = x.shape
+    if k % 256:
+        raise ValueError("K must be a multiple of 256")
+    nb = k // 256
+    b = x.reshape(m, nb, 256)
+    ax = np.abs(b)
+    amax = ax.max(axis=-1) if k else np.zeros((m, 0), F32)
+    first = np.argmax(ax == amax[..., None], axis=-1) if k else np.zeros((m, 0), np.int64)
+    mx = np.take_along_axis(b, first[..., None], axis=-1)[..., 0] if k else np.zeros((m, 0), F32)
+    nz = amax != 0
+    iscale = (F32(-127) / np.where(nz, mx, F32(1))).astype(F32)
+    q = np.minimum(round_half_even((iscale[..., None] * b).astype(F32)), F32(127))
+    q = np.where(nz[..., None], q, F32(0))
+    d = np.where(nz, (F32(1) / iscale).astype(F32), F32(0)).astype(F32)
+    xq = q.astype(np.int8).reshape(m, k)
+    bsums = xq.astype(np.int32).reshape(m, nb, 16, 16).sum(axis=-1).astype(np.int16)
+    return xq, d, bsums
+
+
+def quantize(fmt, x):
+    """The activation quantizer of weight format `fmt` (src/komp/host.py:63-73): -> (xq, xd)."""
+    if ACT[fmt] == "q8_0":
+        return quant_q8_0(x)
+    xq, xd, _ = quant_q8_K(x)
+    return xq, xd
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Weight decode (patch:16-19, 39-63; verify.py:142-152)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def decode_q4_0(wq, k):
+    """Q4_0 quant plane uint8 [n][k/2] -> int8 values [n][k] = nibble - 8 in natural order: byte i of a block
+    holds value i (low nibble) and value i + 16 (high nibble) (patch:16-17, 39-55)."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    n = wq.shape[0]
+    blocks = wq[:, : k // 2].reshape(n, k // 32, 16)
+    lo = (blocks & 15).astype(np.int8) - 8
+    hi = (blocks >> 4).astype(np.int8) - 8
+    return np.concatenate([lo, hi], axis=-1).reshape(n, k)
+
+
+_TQ2_BYTE = np.array([(v // 128) * 32 + v % 32 for v in range(256)], dtype=np.int64)
+_TQ2_SHIFT = np.array([2 * ((v % 128) // 32) for v in range(256)], dtype=np.uint8)
+
+
+def decode_tq2_0(wq, k):
+    """TQ2_0 quant plane uint8 [n][k/4] -> int8 values [n][k] = crumb - 1: value v of a block sits in byte
+    (v/128)*32 + v%32 at bits 2*((v%128)/32) (patch:18-19, 58-63; verify.py:147-152). Crumb 3 decodes to +2."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    n = wq.shape[0]
+    blocks = wq[:, : k // 4].reshape(n, k // 256, 64)
+    vals = (blocks[:, :, _TQ2_BYTE] >> _TQ2_SHIFT) & 3
+    return (vals.astype(np.int8) - 1).reshape(n, k)
+
+
+def decode(fmt, wq, k):
+    return decode_q4_0(wq, k) if fmt == "q4_0" else decode_tq2_0(wq, k)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GEMV: exact block dots, KURN's reference dot, relative error (verify.py:94-137)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def idots(fmt, wq, xq, k):
+    """Exact block dots int64 [M][N][K/block] of the decoded weight values with the int8 activations
+    (verify.exact_idots, src/komp/verify.py:179-185). Computed as f64 matmuls, exact since |dot| < 2^53."""
+    blk = BLOCK[fmt]
+    vals = decode(fmt, wq, k).astype(np.float64)
+    n = vals.shape[0]
+    xq = np.asarray(xq)
+    m = xq.shape[0]
+    nb = k // blk
+    if nb == 0 or n == 0 or m == 0:
+        return np.zeros((m, n, nb), dtype=np.int64)
+    v = vals.reshape(n, nb, blk).transpose(1, 0, 2)                   # [nb][n][blk]
+    q = xq.astype(np.float64).reshape(m, nb, blk).transpose(1, 2, 0)  # [nb][blk][m]
+    out = np.matmul(v, q)                                             # [nb][n][m]
+    return np.rint(out).astype(np.int64).transpose(2, 1, 0).copy()    # [m][n][nb]
+
+
+def reference_dot(fmt, ws, xd, s):
+    """KURN's kurn.formats.reference_dot for every output, from the int block dots s [M][N][nb]: per output a
+    sequential Python-float (f64) sum over blocks of d_w * d_x * s (q4_0) or d_x * d_w * s (tq2_0), the exact
+    float operations and order of verify.rebuild_reference (src/komp/verify.py:188-205). -> f64 [M][N]."""
+    dw = np.asarray(ws, dtype=np.int16).view(np.float16).astype(np.float64)  # [n][nb]
+    xd = np.asarray(xd, dtype=np.float32)
+    # q8_0 blocks carry an f16 scale (the stored xd is already f16-exact); q8_K blocks carry the f32 scale
+    dx = (xd.astype(np.float16) if fmt == "q4_0" else xd).astype(np.float64)  # [m][nb]
+    s = np.asarray(s)
+    m, n, nb = s.shape
+    total = np.zeros((m, n), dtype=np.float64)
+    for b in range(nb):
+        sb = s[:, :, b].astype(np.float64)
+        if fmt == "q4_0":
+            total += (dw[None, :, b] * dx[:, None, b]) * sb
+        else:
+            total += (dx[:, None, b] * dw[None, :, b]) * sb
+    return total
+
+
+def gemv(fmt, wq, ws, xq, xd, k):
+    """-> (reference f64 [M][N], exact block dots int64 [M][N][nb]) for the GEMV of src/komp/kernels.py:48-142."""
+    s = idots(fmt, wq, xq, k)
+    return reference_dot(fmt, ws, xd, s), s
+
+
+def relerr(y, ref):
+    """Normwise relative error max|y - ref| / max|ref| (KURN's `ref.relerr` is not in the reference archive; this
+    is the definition used here, applied to every output of a problem at once)."""
+    y = np.asarray(y, dtype=np.float64).reshape(-1)
+    r = np.asarray(ref, dtype=np.float64).reshape(-1)
+    if r.size == 0:
+        return 0.0
+    scale = np.max(np.abs(r))
+    return float(np.max(np.abs(y - r)) / (scale if scale > 0 else 1.0))
+
+
+def dp4a_ref(a, b, c):
+    """PTX dp4a.s32.s32: c + sum of the products of the four signed bytes of a and b, int32 wraparound
+    (src/komp/verify.py:122-126). Vectorized over int arrays."""
+    a = np.asarray(a, dtype=np.int64) & 0xFFFFFFFF
+    b = np.asarray(b, dtype=np.int64) & 0xFFFFFFFF
+    r = np.asarray(c, dtype=np.int64).copy()
+    for i in range(4):
+        sa = ((a >> (8 * i)) & 0xFF).astype(np.int64)
+        sb = ((b >> (8 * i)) & 0xFF).astype(np.int64)
+        sa = np.where(sa >= 128, sa - 256, sa)
+        sb = np.where(sb >= 128, sb - 256, sb)
+        r = r + sa * sb
+    return ((r + 2**31) % 2**32 - 2**31).astype(np.int64)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Seeded synthetic inputs (the distributions BASELINE.json's configs name; KURN's generators are not available)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def weight_blocks(fmt, rng, n, k, extreme=False):
+    """ggml weight blocks (bytes) for n rows of k values.
+
+    random:  q4_0 quant bytes uniform 0..255, d = f16(|N(0, 0.02)|); tq2_0 crumbs uniform {0,1,2},
+             d = f16(|N(0, 0.05)|).
+    extreme: q4_0 nibbles only 0 or 15; tq2_0 crumbs 0, 2 and 3 (3 decodes to +2); scales include 0, f16 subnormals,
+             the largest normal f16 below 2^8 and negative scales."""
+    blk = BLOCK[fmt]
+    nb = k // blk
+    out = np.zeros((n, nb, NBYTES[fmt]), dtype=np.uint8)
+    if fmt == "q4_0":
+        if extreme:
+            nib = rng.choice(np.array([0, 15], dtype=np.uint8), size=(n, nb, 32))
+        else:
+            nib = rng.integers(0, 16, size=(n, nb, 32), dtype=np.uint8)
+        q = (nib[:, :, :16] | (nib[:, :, 16:] << 4)).astype(np.uint8)
+        sd = 0.02
+    else:
+        crumbs = rng.choice(np.array([0, 2, 3], dtype=np.uint8), size=(n, nb, 256)) if extreme else \
+            rng.integers(0, 3, size=(n, nb, 256), dtype=np.uint8)
+        q = np.zeros((n, nb, 64), dtype=np.uint8)
+        for v in range(256):
+            q[:, :, _TQ2_BYTE[v]] |= (crumbs[:, :, v] << _TQ2_SHIFT[v]).astype(np.uint8)
+        sd = 0.05
+    d = np.abs(rng.normal(0.0, sd, size=(n, nb))).astype(np.float16)
+    if extreme and n * nb:
+        flat = d.reshape(-1)
+        pick = rng.choice(flat.size, size=min(flat.size, 8), replace=False)
+        specials = np.array([0.0, 6e-8, 3e-5, 255.9, -0.75, -1e-3, 1.0, 2.0 ** -14], dtype=np.float16)
+        flat[pick] = specials[: pick.size]
+    qoff = 2 if fmt == "q4_0" else 0
+    soff = 0 if fmt == "q4_0" else 64
+    out[:, :, qoff : qoff + QBYTES[fmt]] = q
+    out[:, :, soff : soff + 2] = d.view(np.uint8).reshape(n, nb, 2)
+    return out.tobytes()
+
+
+def activations(rng, m, k, extreme=False):
+    """f32 [m][k]: N(0, 1). extreme: plus 5% exact zeros, 1% +-1e4 outliers, an all-zero 256-block, a block at
+    exact rounding half-points (amax 127 so q8_0's id is 1.0, max -127 so q8_K's iscale is 1.0) and a block whose
+    largest magnitude is tied between signs."""
+    x = rng.standard_normal((m, k)).astype(F32)
+    if extreme and k:
+        x[rng.random((m, k)) < 0.05] = 0.0
+        out = rng.random((m, k)) < 0.01
+        x[out] = np.where(rng.random(out.sum()) < 0.5, -1e4, 1e4).astype(F32)
+        blocks = k // 32
+        for row in range(m):
+            if k >= 256:
+                z = rng.integers(0, k // 256)
+                x[row, z * 256 : (z + 1) * 256] = 0.0
+            if blocks >= 2:
+                b = rng.integers(0, blocks)
+                half = (rng.integers(-126, 126, size=32) + 0.5).astype(F32)
+                half[rng.integers(0, 32)] = -127.0
+                x[row, b * 32 : (b + 1) * 32] = half
+                b2 = (b + 1) % blocks
+                tie = rng.standard_normal(32).astype(F32)
+                i, j = rng.choice(32, size=2, replace=False)
+                tie[min(i, j)], tie[max(i, j)] = 7.25, -7.25
+                x[row, b2 * 32 : (b2 + 1) * 32] = tie
+    return x
+
+
+def quant_config_input(seed=0, m=4, k=14336):
+    """f32 [4][14336], N(0,1) with 5% exact zeros, 1% +-1e4 outliers, one all-zero 32-block, one
+    all-zero 256-block, and blocks of exact rounding half-points for both quantizers."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k)).astype(F32)
+    x[rng.random((m, k)) < 0.05] = 0.0
+    out = rng.random((m, k)) < 0.01
+    x[out] = np.where(rng.random(out.sum()) < 0.5, -1e4, 1e4).astype(F32)
+    x[0, 32:64] = 0.0                       # all-zero q8_0 block (its 256-block is not all zero)
+    x[1, 512:768] = 0.0                     # all-zero q8_K block
+    half = (np.arange(-16, 16) + 0.5).astype(F32)
+    half[5] = 127.0                         # q8_0: amax 127 -> d = 1, id = 1, q = roundf(k + 0.5)
+    x[2, 64:96] = half
+    blk = (rng.integers(-120, 120, size=256) + 0.5).astype(F32)
+    blk[17] = -127.0                        # q8_K: max is -127 -> iscale = 1, q = rint(k + 0.5)
+    x[3, 1024:1280] = blk
+    tie = rng.standard_normal(256).astype(F32)
+    tie[40], tie[200] = -9.5, 9.5           # q8_K tie on |x|: the first (negative) one wins
+    x[2, 2048:2304] = tie
+    return x
+
+
+def problem(fmt, n, k, m, seed=0, extreme=False):
+    """(ggml weight bytes, f32 activations [m][k]) for one GEMV problem."""
+    rng = np.random.default_rng(seed)
+    W = weight_blocks(fmt, rng, n, k, extreme)
+    x = activations(rng, m, k, extreme)
+    return W, x
+
+
+def split(fmt, W, n, k):
+    """ggml blocks -> (WQ uint8 [n][qbytes*k/blk], WS int16 [n][k/blk]) (src/komp/host.py:16-22)."""
+    blk = BLOCK[fmt]
+    b = np.frombuffer(W, dtype=np.uint8).reshape(n, k // blk, NBYTES[fmt])
+    qoff = 2 if fmt == "q4_0" else 0
+    soff = 0 if fmt == "q4_0" else 64
+    wq = np.ascontiguousarray(b[:, :, qoff : qoff + QBYTES[fmt]]).reshape(n, -1)
+    ws = np.ascontiguousarray(b[:, :, soff : soff + 2]).view(np.int16).reshape(n, k // blk)
+    return wq, ws
+
+
+def random_split(fmt, rng, n, k):
+    """Split planes directly (fast path for large synthetic layers): same distributions as weight_blocks."""
+    blk = BLOCK[fmt]
+    nb = k // blk
+    if fmt == "q4_0":
+        wq = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        d = np.abs(rng.normal(0.0, 0.02, size=(n, nb))).astype(np.float16)
+    else:
+        # crumbs uniform in {0,1,2}: draw each byte's 4 crumbs from base-3 digits of a uniform 0..80
+        t = rng.integers(0, 81, size=(n, k // 4), dtype=np.uint8)
+        c0, c1, c2, c3 = t % 3, (t // 3) % 3, (t // 9) % 3, (t // 27) % 3
+        wq = (c0 | (c1 << 2) | (c2 << 4) | (c3 << 6)).astype(np.uint8)
+        d = np.abs(rng.normal(0.0, 0.05, size=(n, nb))).astype(np.float16)
+    return wq, d.view(np.int16)

@@ -1,0 +1,239 @@
+"""Parity of the CUDA path (through the C-ABI, via comp_b200.host) with the reference and the oracle.
+
+Bars: quantizer bytes and every int32 block dot bit-exact; f32 Y within KURN's relative-error rule (1e-5) of the
+exact reference dot, which is itself rebuilt bit-identically from our int32 dots. Mirrors the reference's checks in
+src/komp/verify.py (check_dp4a, check_decode, check_gemv) on the reference's own recorded outputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from comp_b200 import _lib, host
+from oracle import native, ref
+
+from .conftest import golden_case_ids
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5  # KURN's rule (src/komp/verify.py:113)
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _same_f32(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# probes (verify.check_dp4a / check_decode)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_dp4a_probe_matches_reference(cuda, golden):
+    a, b, c = (_t(golden[f"dp4a/{k}"], cuda) for k in "abc")
+    out = torch.empty_like(a)
+    _lib.call("b2q_probe_dp4a", a.data_ptr(), b.data_ptr(), c.data_ptr(), out.data_ptr(), a.numel(),
+              torch.cuda.current_stream().cuda_stream)
+    assert np.array_equal(out.cpu().numpy(), golden["dp4a/out"])
+
+
+def test_decode_probes_match_reference(cuda, golden):
+    for fmt, vals in (("q4_0", 32), ("tq2_0", 256)):
+        wq = _t(golden[f"decode/{fmt}/wq"], cuda)
+        out = torch.empty((wq.shape[0], vals), dtype=torch.int32, device=cuda)
+        _lib.call(f"b2q_decode_{fmt}", wq.data_ptr(), out.data_ptr(), wq.shape[0],
+                  torch.cuda.current_stream().cuda_stream)
+        assert np.array_equal(out.cpu().numpy(), golden[f"decode/{fmt}/out"]), fmt
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# quantizers
+# ---------------------------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "tq2_0"])
+def test_quantizer_bytes_match_reference(cuda, golden, fmt):
+    x = golden["quant/x"]
+    xq, xd = host.quantize(fmt, _t(x, cuda))
+    act = ref.ACT[fmt]
+    assert np.array_equal(xq.cpu().numpy(), golden[f"quant/{act}/xq"])
+    assert _same_f32(xd.cpu().numpy(), golden[f"quant/{act}/xd"])
+    # ggml block bytes, as verify.check_gemv compares them (src/komp/verify.py:212-215)
+    oq, od = ref.quantize(fmt, x)
+    assert host.act_blocks(fmt, xq.cpu().numpy(), xd.cpu().numpy()) == host.act_blocks(fmt, oq, od)
+
+
+def test_q8_K_bsums_match_oracle(cuda, golden):
+    x = golden["quant/x"]
+    xq, xd, bs = host.quantize_q8_K_bsums(_t(x, cuda))
+    oq, od, obs = ref.quant_q8_K(x)
+    assert np.array_equal(xq.cpu().numpy(), oq) and _same_f32(xd.cpu().numpy(), od)
+    assert np.array_equal(bs.cpu().numpy(), obs)
+
+
+def test_quantizer_row_stride_and_tails(cuda):
+    rng = np.random.default_rng(5)
+    for m, k, ldx in ((3, 96, 100), (1, 32, 32), (5, 512, 520), (2, 0, 4)):
+        big = rng.standard_normal((m, ldx)).astype(np.float32) * 3
+        xt = _t(big, cuda)[:, :k]
+        for fmt in ("q4_0", "tq2_0"):
+            if k % ref.BLOCK[fmt] and fmt == "tq2_0":
+                continue
+            xq, xd = host.quantize(fmt, xt)
+            oq, od = ref.quantize(fmt, big[:, :k])
+            assert np.array_equal(xq.cpu().numpy(), oq), (fmt, m, k)
+            assert _same_f32(xd.cpu().numpy(), od), (fmt, m, k)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GEMVs on the reference's recorded problems (verify.PROBLEMS + config-0/1 row slices, random and extreme)
+# ---------------------------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("cid", golden_case_ids())
+def test_gemv_matches_reference(cuda, golden, cid):
+    c = next(c for c in golden.cases() if c["id"] == cid)
+    g = golden.case(cid)
+    fmt, n, k, m = c["fmt"], c["n"], c["k"], c["m"]
+    wq, ws = host.split(fmt, g["W"].tobytes(), n, k)
+    xq, xd = host.quantize(fmt, _t(g["x"], cuda))
+    assert np.array_equal(xq.cpu().numpy(), g["xq"]) and _same_f32(xd.cpu().numpy(), g["xd"])
+    r, _ = ref.gemv(fmt, wq, ws, g["xq"], g["xd"], k)
+    ys = []
+    for mode in (0, 1, 2):
+        y, s = host.gemv(fmt, _t(wq, cuda), _t(ws, cuda), xq, xd, n, k, mode=mode, store_s=True)
+        s = s.cpu().numpy()
+        assert np.array_equal(s, g["s0"]), f"int32 block dots differ (mode {mode})"
+        # KURN's reference dot rebuilt from our dots, same float ops and order, is bit-identical
+        assert np.array_equal(ref.reference_dot(fmt, ws, g["xd"], s).view(np.uint64), r.view(np.uint64))
+        y = y.cpu().numpy()
+        assert ref.relerr(y, r) <= TOL, f"mode {mode}: relerr {ref.relerr(y, r):.2e}"
+        assert ref.relerr(g["y0"], r) <= TOL  # the reference's own f32 output, for scale
+        ys.append(y)
+    # every variant gives the same f32 Y, bit for bit (schedule-independent summation order)
+    assert _same_f32(ys[0], ys[1]) and _same_f32(ys[1], ys[2])
+    # without store_s the same Y
+    y, s = host.gemv(fmt, _t(wq, cuda), _t(ws, cuda), xq, xd, n, k, mode=2)
+    assert s is None and _same_f32(y.cpu().numpy(), ys[2])
+    # fused quantizer prologue: same activations, same Y
+    yf, fq, fd = host.quant_gemv(fmt, _t(wq, cuda), _t(ws, cuda), _t(g["x"], cuda), n, k, return_act=True)
+    assert np.array_equal(fq.cpu().numpy(), g["xq"]) and _same_f32(fd.cpu().numpy(), g["xd"])
+    assert _same_f32(yf.cpu().numpy(), ys[2])
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# BASELINE-size problems against the oracle
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def _layer(fmt, n, k, m, seed, dev):
+    rng = np.random.default_rng(seed)
+    wq, ws = ref.random_split(fmt, rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    return wq, ws, x, _t(wq, dev), _t(ws, dev), _t(x, dev)
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [
+    ("q4_0", 4096, 4096, 1),    # config 0
+    ("tq2_0", 4096, 4096, 1),   # config 1
+    ("tq2_0", 4096, 4096, 3),   # config 1, 3 columns
+    ("q4_0", 4100, 4096, 3),    # config 3 row tail
+    ("q4_0", 4096, 14336, 2),   # config 3 down (tall K)
+    ("q4_0", 300, 28672, 1),    # K = 28672: two chunks per thread
+])
+def test_gemv_full_size_matches_oracle(cuda, fmt, n, k, m):
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 11, cuda)
+    xq, xd = host.quantize(fmt, tx)
+    oq, od = ref.quantize(fmt, x)
+    assert np.array_equal(xq.cpu().numpy(), oq) and _same_f32(xd.cpu().numpy(), od)
+    y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+    r, os_ = native.gemv(fmt, wq, ws, oq, od, k, want_s=True)
+    assert np.array_equal(s.cpu().numpy(), os_)
+    assert ref.relerr(y.cpu().numpy(), r) <= TOL
+
+
+@pytest.mark.parametrize("fmt,n,k", [("tq2_0", 57344, 8192), ("tq2_0", 8192, 28672), ("q4_0", 128256, 8192),
+                                     ("q4_0", 28672, 4096), ("q4_0", 6144, 4096)])
+def test_gemv_large_layers_sampled_rows(cuda, fmt, n, k):
+    """Configs 3/4 at full size: every output row checked against the C oracle on a sample of rows (the row
+    result does not depend on the other rows), plus the int32 dots of the sampled rows."""
+    rng = np.random.default_rng(23)
+    wq, ws = ref.random_split(fmt, rng, n, k)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    twq, tws = _t(wq, cuda), _t(ws, cuda)
+    y = host.quant_gemv(fmt, twq, tws, _t(x, cuda), n, k).cpu().numpy()
+    rows = np.unique(np.concatenate([rng.choice(n, 512, replace=False), [0, n - 1]]))
+    oq, od = ref.quantize(fmt, x)
+    r, _ = native.gemv(fmt, wq[rows], ws[rows], oq, od, k)
+    assert ref.relerr(y[:, rows], r) <= TOL
+    del twq, tws
+    torch.cuda.empty_cache()
+
+
+def test_gemv_many_columns_and_row_stride(cuda):
+    """M > 4 (column groups) and a weight row stride larger than the quant bytes."""
+    rng = np.random.default_rng(3)
+    for fmt, n, k, m in (("q4_0", 37, 416, 9), ("tq2_0", 37, 768, 6)):
+        wq, ws = ref.random_split(fmt, rng, n, k)
+        wide = np.zeros((n, wq.shape[1] + 48), np.uint8)
+        wide[:, : wq.shape[1]] = wq
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        xq, xd = host.quantize(fmt, _t(x, cuda))
+        twide = _t(wide, cuda)[:, : wq.shape[1]]
+        y, s = host.gemv(fmt, twide, _t(ws, cuda), xq, xd, n, k, mode=2, store_s=True)
+        r, os_ = ref.gemv(fmt, wq, ws, xq.cpu().numpy(), xd.cpu().numpy(), k)
+        assert np.array_equal(s.cpu().numpy(), os_)
+        assert ref.relerr(y.cpu().numpy(), r) <= TOL
+
+
+def test_gemv_edge_sizes(cuda):
+    rng = np.random.default_rng(4)
+    for fmt in ("q4_0", "tq2_0"):
+        blk = ref.BLOCK[fmt]
+        for n, k, m in ((0, blk, 1), (3, blk, 0), (1, blk, 1), (2, 0, 2)):
+            wq, ws = ref.random_split(fmt, rng, n, k)
+            if wq.shape[1] == 0:
+                wq = np.zeros((n, 16), np.uint8)
+            x = rng.standard_normal((m, k)).astype(np.float32)
+            xq, xd = host.quantize(fmt, _t(x, cuda)) if m else (
+                torch.empty((0, k), dtype=torch.int8, device=cuda), torch.empty((0, k // blk), device=cuda))
+            y, s = host.gemv(fmt, _t(wq, cuda), _t(ws, cuda), xq, xd, n, k, mode=2, store_s=True)
+            assert tuple(y.shape) == (m, n)
+            r, os_ = ref.gemv(fmt, wq, ws, xq.cpu().numpy(), xd.cpu().numpy(), k)
+            assert np.array_equal(s.cpu().numpy(), os_)
+            assert np.array_equal(y.cpu().numpy(), r.astype(np.float32)) or ref.relerr(y.cpu().numpy(), r) <= TOL
+
+
+def test_gemv_rejects_bad_arguments(cuda):
+    wq = torch.zeros((4, 32), dtype=torch.uint8, device=cuda)
+    ws = torch.zeros((4, 2), dtype=torch.int16, device=cuda)
+    xq = torch.zeros((1, 64), dtype=torch.int8, device=cuda)
+    xd = torch.zeros((1, 2), dtype=torch.float32, device=cuda)
+    with pytest.raises(ValueError):  # misaligned quant plane
+        raw = torch.zeros(4 * 32 + 16, dtype=torch.uint8, device=cuda)
+        host.gemv("q4_0", raw[1:129].view(4, 32), ws, xq, xd, 4, 64)
+    with pytest.raises(ValueError):  # K not a multiple of the block
+        host.gemv("q4_0", wq, ws, xq, xd, 4, 48)
+    with pytest.raises(RuntimeError):  # CPU tensors: no CPU path
+        host.gemv("q4_0", wq.cpu(), ws.cpu(), xq.cpu(), xd.cpu(), 4, 64)
+    with pytest.raises(ValueError):  # C-ABI direct: K % 32 != 0
+        _lib.call("b2q_gemv_q4_0", wq.data_ptr(), 32, ws.data_ptr(), xq.data_ptr(), xd.data_ptr(), xd.data_ptr(),
+                  None, 4, 48, 1, 2, None)
+
+
+def test_gemv_deterministic(cuda):
+    wq, ws, x, twq, tws, tx = _layer("tq2_0", 8192, 8192, 1, 5, cuda)
+    a = host.quant_gemv("tq2_0", twq, tws, tx, 8192, 8192).cpu().numpy()
+    b = host.quant_gemv("tq2_0", twq, tws, tx, 8192, 8192).cpu().numpy()
+    assert _same_f32(a, b)
+
+
+def test_launch_counter_counts_kernels(cuda):
+    before = _lib.launch_count()
+    wq, ws, x, twq, tws, tx = _layer("q4_0", 64, 512, 1, 2, cuda)
+    xq, xd = host.quantize("q4_0", tx)
+    host.gemv("q4_0", twq, tws, xq, xd, 64, 512, mode=2)
+    assert _lib.launch_count() - before == 2
