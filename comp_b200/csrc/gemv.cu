@@ -5,13 +5,17 @@
 // multiply order (q4_0: f32(s) * dw * dx, kernels.py:93; tq2_0: dx * dw * f32(s), kernels.py:141), summed in a
 // fixed (deterministic) order that differs from the reference's, as the reference's own order differs from KURN's.
 //
-// Schedule (one design for both formats; a "chunk" is 16 consecutive quant bytes of one weight row):
-//   * The CTA is one team of T = 32*ceil(C/CPT/32) threads, where C = chunks per row (K/32 for Q4_0, K/64 for
-//     TQ2_0). Thread t owns chunks t, t+T, ... (CPT of them) of every row it touches: one 128-bit streaming load per
-//     chunk and row, coalesced across the CTA (consecutive threads, consecutive 16-byte chunks of the same row).
-//   * Work unit = a group of R consecutive rows. Each CTA takes a contiguous range of groups. The next unit's weight
-//     loads are issued before the current unit is computed (register double buffer), and the first unit's loads are
-//     issued before the activation prologue, so HBM latency overlaps staging and math.
+// Schedule (a "chunk" is 16 consecutive quant bytes of one weight row; C = chunks per row = K/32 for Q4_0, K/64 for
+// TQ2_0):
+//   * One CTA of T = 32*ceil(C/CPT/32) threads works on a group of R consecutive rows at a time; thread t owns chunks
+//     t, t+T, ... (CPT of them) of every row. Each CTA takes a contiguous range of row groups (persistent grid).
+//   * Weight streaming, "ring" path: the R rows' quant bytes and scale bytes of a group are bulk-copied by the TMA
+//     engine (cp.async.bulk, one elected thread) into a ring of S shared-memory stages, each completing on its own
+//     mbarrier; S-1 groups are in flight while one is computed, and the first S-1 are issued before the activation
+//     prologue so the HBM stream starts at once. Stage release needs no extra barrier: the per-group reduction's
+//     __syncthreads orders every read of a stage before it is refilled. Every mbarrier wait is bounded.
+//   * "register" path (unaligned scale rows, or the byte-wise variant): 128-bit streaming loads straight into
+//     registers, double-buffered one group ahead.
 //   * Activations (int8 q8 planes, or f32 quantized in the prologue) are staged once per CTA into shared memory in a
 //     permuted layout: for column m, bit-field j and chunk c, the 16 activation bytes that multiply bit-field j of
 //     weight chunk c sit at xs[m][j][c] (one conflict-free 128-bit shared load per thread). Q4_0 has j in {lo, hi}
@@ -21,7 +25,8 @@
 //     s = dp4a(w & 0x0F0F0F0F, xl) + (dp4a_u(w & 0xF0F0F0F0, xh) >> 4) - 8 * sum(x). The offsets (-8 for Q4_0,
 //     -1 for TQ2_0) are folded in with per-chunk activation sums precomputed in the prologue. TQ2_0 blocks span 4
 //     chunks (4 adjacent threads), whose partial dots are combined with two xor-shuffles before scaling.
-//   * Per-unit reduction: warp shuffles, then a cross-warp sum in shared memory in fixed warp order.
+//   * Per-group reduction: warp shuffles, then a cross-warp sum in shared memory in fixed warp order. The summation
+//     order of a row depends only on (K, T, CPT), so Y is bit-identical across paths, variants, R and grid size.
 #include <algorithm>
 #include <mutex>
 #include <unordered_map>
@@ -33,6 +38,11 @@ namespace b2q {
 
 constexpr int kMaxThreads = 512;
 constexpr int kMaxColumns = 4;  // columns per launch; more are processed in groups of 4 (weights re-read per group)
+constexpr long long kWaitLimit = 1LL << 20;  // bounded mbarrier polls (each try_wait also suspends in hardware)
+constexpr int kErrTimeout = 1;
+
+// Set by a kernel whose bounded wait gave up (read and cleared by b2q_device_error).
+__device__ int g_device_error = 0;
 
 struct GemvParams {
   const uint8_t* wq;
@@ -61,6 +71,9 @@ struct GemvParams {
   int C;                  // 16-byte chunks per row
   int CPT;                // chunks per thread per row
   int64_t groups;         // ceil(N / R)
+  int stages;             // ring path: shared-memory stages
+  uint32_t stage_bytes;   // ring path: bytes per stage (R rows of quants, then R rows of scales, 16-byte padded)
+  int dense;              // ring path: ldwq == C*16, so a group's quant rows are one contiguous copy
 };
 
 template <int FMT>
@@ -83,67 +96,167 @@ __device__ __forceinline__ int perm_unit(int q, int C) {
   return j * C + 4 * b + c;
 }
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+// ------------------------------------------------------------------------------------------------------------------
+// mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk; sm_90+)
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Bounded wait for the phase with the given parity to complete; false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
+  for (long long i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Global -> shared bulk copy (no multicast), completion counted in bytes on `bar`. dst, src, bytes: multiples of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // Activation prologue: fills xs (permuted int8), xsum (per-chunk offset correction) and xscale (per-block f32 scale).
+// Loads are batched (kUnroll per thread in flight) so the prologue costs a few L2 round trips, not one per item.
 // ------------------------------------------------------------------------------------------------------------------
+constexpr int kUnroll = 4;
+
 template <int FMT>
 __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int* xsum, float* xscale) {
   const int T = blockDim.x, tt = threadIdx.x;
   const int K = (int)p.K, C = p.C, M = p.M;
   const int nblk = K / Fmt<FMT>::kBlock;
-  const int units = K / 16;
   if (p.x_f32 == nullptr) {
-    for (int idx = tt; idx < M * units; idx += T) {
-      const int m = idx / units, q = idx - m * units;
-      const uint4 v = *reinterpret_cast<const uint4*>(p.xq + (int64_t)m * K + (int64_t)q * 16);
-      *reinterpret_cast<uint4*>(xs + (int64_t)m * K + perm_unit<FMT>(q, C) * 16) = v;
+    const int units = K / 16;
+    const int total = M * units;
+    for (int base = tt; base < total; base += T * kUnroll) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int idx = base + u * T;
+        if (idx < total) {
+          const int m = idx / units, q = idx - m * units;
+          v[u] = *reinterpret_cast<const uint4*>(p.xq + (int64_t)m * K + (int64_t)q * 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int idx = base + u * T;
+        if (idx < total) {
+          const int m = idx / units, q = idx - m * units;
+          *reinterpret_cast<uint4*>(xs + (int64_t)m * K + perm_unit<FMT>(q, C) * 16) = v[u];
+        }
+      }
     }
     for (int idx = tt; idx < M * nblk; idx += T) xscale[idx] = p.xd[idx];
   } else if (FMT == 0) {
-    // q8_0: 8 lanes per 32-value block, 4 blocks per warp per iteration (warp-uniform loop for the shuffles)
+    // q8_0: 8 lanes per 32-value block (4 blocks per warp per slot); kUnroll slots of loads in flight per lane
     const int lane = tt & 31, sub = lane & 7, nw = T / 32;
     const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
-    for (int base = (tt >> 5) * 4; base < M * nblk; base += nw * 4) {
-      const int g = base + (lane >> 3);
-      const bool ok = g < M * nblk;
-      const int m = ok ? g / nblk : 0, b = ok ? g - m * nblk : 0;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (ok) v = *reinterpret_cast<const float4*>(p.x_f32 + (int64_t)m * p.ldx + b * 32 + sub * 4);
-      float d;
-      const uint32_t q = q8_0_quant4(v, &d);
-      if (ok) {
-        *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + ((sub >> 2) * C + b) * 16 + (sub & 3) * 4) = q;
-        const float ds = q8_0_stored_scale(d);
-        if (sub == 0) xscale[m * nblk + b] = ds;
-        if (writer) {
-          *reinterpret_cast<uint32_t*>(p.xq_out + (int64_t)m * K + b * 32 + sub * 4) = q;
-          if (sub == 0 && p.xd_out) p.xd_out[m * nblk + b] = ds;
+    const int total = M * nblk;
+    for (int base = (tt >> 5) * 4; base < total; base += nw * 4 * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int g = base + u * nw * 4 + (lane >> 3);
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g < total) {
+          const int m = g / nblk, b = g - m * nblk;
+          v[u] = *reinterpret_cast<const float4*>(p.x_f32 + (int64_t)m * p.ldx + b * 32 + sub * 4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int g = base + u * nw * 4 + (lane >> 3);
+        float d;
+        const uint32_t q = q8_0_quant4(v[u], &d);  // whole warp: shuffles inside
+        if (g < total) {
+          const int m = g / nblk, b = g - m * nblk;
+          *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + ((sub >> 2) * C + b) * 16 + (sub & 3) * 4) = q;
+          const float ds = q8_0_stored_scale(d);
+          if (sub == 0) xscale[m * nblk + b] = ds;
+          if (writer) {
+            *reinterpret_cast<uint32_t*>(p.xq_out + (int64_t)m * K + b * 32 + sub * 4) = q;
+            if (sub == 0 && p.xd_out) p.xd_out[m * nblk + b] = ds;
+          }
         }
       }
     }
   } else {
-    // q8_K: one warp per 256-value block, lane l holds values 8l..8l+7
+    // q8_K: one warp per 256-value block, lane l holds values 8l..8l+7; kUnroll blocks of loads in flight per warp
     const int lane = tt & 31, nw = T / 32;
     const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
-    for (int g = tt >> 5; g < M * nblk; g += nw) {
-      const int m = g / nblk, b = g - m * nblk;
-      const float* src = p.x_f32 + (int64_t)m * p.ldx + b * 256 + lane * 8;
-      const float4 a = *reinterpret_cast<const float4*>(src);
-      const float4 c4 = *reinterpret_cast<const float4*>(src + 4);
-      const float v[8] = {a.x, a.y, a.z, a.w, c4.x, c4.y, c4.z, c4.w};
-      uint32_t qlo, qhi;
-      const float d = q8_K_quant8(v, lane, &qlo, &qhi);
-      const int o = lane >> 1;  // 16-value piece within the block
-      const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
-      *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + 4 * b + c) * 16 + (lane & 1) * 8) = make_uint2(qlo, qhi);
-      if (lane == 0) xscale[m * nblk + b] = d;
-      if (writer) {
-        *reinterpret_cast<uint2*>(p.xq_out + (int64_t)m * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
-        if (lane == 0 && p.xd_out) p.xd_out[m * nblk + b] = d;
+    const int total = M * nblk;
+    for (int base = tt >> 5; base < total; base += nw * kUnroll) {
+      float4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int g = base + u * nw;
+        va[u] = vb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (g < total) {
+          const int m = g / nblk, b = g - m * nblk;
+          const float* src = p.x_f32 + (int64_t)m * p.ldx + b * 256 + lane * 8;
+          va[u] = *reinterpret_cast<const float4*>(src);
+          vb[u] = *reinterpret_cast<const float4*>(src + 4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int g = base + u * nw;
+        if (g < total) {  // warp-uniform
+          const int m = g / nblk, b = g - m * nblk;
+          const float v[8] = {va[u].x, va[u].y, va[u].z, va[u].w, vb[u].x, vb[u].y, vb[u].z, vb[u].w};
+          uint32_t qlo, qhi;
+          const float d = q8_K_quant8(v, lane, &qlo, &qhi);
+          const int o = lane >> 1;  // 16-value piece within the block
+          const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
+          *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + 4 * b + c) * 16 + (lane & 1) * 8) =
+              make_uint2(qlo, qhi);
+          if (lane == 0) xscale[m * nblk + b] = d;
+          if (writer) {
+            *reinterpret_cast<uint2*>(p.xq_out + (int64_t)m * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
+            if (lane == 0 && p.xd_out) p.xd_out[m * nblk + b] = d;
+          }
+        }
       }
     }
   }
@@ -215,6 +328,124 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
   }
 }
 
+// One chunk c of R rows (weights w[r], scales dw[r]) against all columns: block dots, S store, f32 accumulation.
+template <int FMT, int R, int MC, bool BYTES>
+__device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, int c, bool valid, const uint4 (&w)[R],
+                                              const float (&dw)[R], const uint8_t* xs, const int* xsum,
+                                              const float* xscale, float (&acc)[R][MC]) {
+  const int C = p.C, M = p.M;
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const int blk = c >> Fmt<FMT>::kChunkShift;
+#pragma unroll
+  for (int m = 0; m < MC; ++m) {
+    if (m < M) {
+      uint4 x[4];
+      int xs_sum = 0;
+      float dx = 0.f;
+      if (valid) {
+        const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * p.K);
+#pragma unroll
+        for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = col[j * C + c];
+        xs_sum = xsum[m * C + c];
+        dx = xscale[m * nblk + blk];
+      } else {
+#pragma unroll
+        for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        int s = chunk_dot<FMT, BYTES>(w[r], x, xs_sum);
+        if (FMT == 1) {  // a TQ2_0 block spans 4 adjacent threads: exact int32 sum of the 4 partial dots
+          s += __shfl_xor_sync(0xffffffffu, s, 1);
+          s += __shfl_xor_sync(0xffffffffu, s, 2);
+        }
+        const bool lead = valid && (FMT == 0 || (c & 3) == 0);
+        const int64_t row = g * R + r;
+        if (lead && row < p.N) {
+          if (p.s) p.s[((int64_t)m * p.N + row) * nblk + blk] = s;
+          if (FMT == 0)
+            acc[r][m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), dx, acc[r][m]);
+          else
+            acc[r][m] = __fmaf_rn(__fmul_rn(dx, dw[r]), (float)s, acc[r][m]);
+        }
+      }
+    }
+  }
+}
+
+// Group reduction: warp shuffles, cross-warp sum in fixed order, store of R x M outputs. Contains __syncthreads.
+template <int R, int MC>
+__device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, float (&acc)[R][MC], float* red,
+                                             int buf) {
+  const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MC; ++m) {
+      float v = acc[r][m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[(buf * nwarps + warp) * (R * MC) + r * MC + m] = v;
+      acc[r][m] = 0.f;
+    }
+  __syncthreads();
+  if ((int)threadIdx.x < R * MC) {
+    const int r = threadIdx.x / MC, m = threadIdx.x - (threadIdx.x / MC) * MC;
+    const int64_t row = g * R + r;
+    if (m < p.M && row < p.N) {
+      float v = 0.f;
+      for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * (R * MC) + threadIdx.x];
+      p.y[(int64_t)m * p.ldy + p.row0 + row] = v;
+    }
+  }
+}
+
+// Fused all-gather epilogue: copies this CTA's rows of Y to every peer, then the last CTA runs the flag barrier.
+__device__ void allgather_epilogue(const GemvParams& p, int64_t g_begin, int64_t g_end, int R) {
+  __syncthreads();
+  const int64_t r_begin = g_begin * R, r_end = min(g_end * R, p.N);
+  for (int m = 0; m < p.M; ++m) {
+    const int64_t base = (int64_t)m * p.ldy + p.row0;
+    for (int64_t row = r_begin + threadIdx.x; row < r_end; row += blockDim.x) {
+      const float v = p.y[base + row];
+      for (int q = 0; q < p.nranks; ++q)
+        if (q != p.rank) p.y_peers[q][base + row] = v;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* own = p.flags_peers[p.rank];
+    const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
+    if (arrived == gridDim.x - 1) {
+      own[p.nranks] = 0u;  // reset the arrival counter for the next call
+      __threadfence_system();
+      for (int q = 0; q < p.nranks; ++q) {
+        uint32_t* f = p.flags_peers[q] + p.rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
+      }
+      int err = 0;
+      for (int q = 0; q < p.nranks && !err; ++q) {
+        long long spins = 0;
+        uint32_t v;
+        for (;;) {
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
+          if ((int32_t)(v - p.epoch) >= 0) break;
+          if (++spins > p.spin_limit) {
+            err = 1 + q;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      if (err && p.status) *p.status = err;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Register path: weights streamed straight into registers, double-buffered one unit (group, chunk round) ahead.
+// ------------------------------------------------------------------------------------------------------------------
 template <int R>
 struct WeightRegs {
   uint4 w[R];
@@ -239,7 +470,7 @@ __device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i,
 }
 
 template <int FMT, int R, int MC, bool BYTES>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int M = p.M, C = p.C;
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
@@ -247,9 +478,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p
   int* xsum = reinterpret_cast<int*>(smem + (size_t)M * p.K);             // [M][C]
   float* xscale = reinterpret_cast<float*>(xsum + M * C);                // [M][nblk]
   float* red = xscale + M * nblk;                                        // [2][warps][R*MC]
-  const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // contiguous range of row groups for this CTA
   const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
   const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
 
@@ -267,7 +496,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p
   int64_t g = g_begin;
   int i = 0;
   while (g < g_end) {
-    // prefetch the next unit
     int64_t gn = g;
     int in = i + 1;
     if (in == p.CPT) {
@@ -277,117 +505,123 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p
     load_unit<FMT, R>(p, gn, in, gn < g_end, nxt);
 
     const int c = (int)threadIdx.x + i * (int)blockDim.x;
-    const bool valid = c < C;
-    const int blk = c >> Fmt<FMT>::kChunkShift;
     float dw[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) dw[r] = f16_bits_to_f32(cur.sc[r]);
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      if (m < M) {
-        uint4 x[4];
-        int xs_sum = 0;
-        float dx = 0.f;
-        if (valid) {
-          const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * p.K);
-#pragma unroll
-          for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = col[j * C + c];
-          xs_sum = xsum[m * C + c];
-          dx = xscale[m * nblk + blk];
-        } else {
-#pragma unroll
-          for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          int s = chunk_dot<FMT, BYTES>(cur.w[r], x, xs_sum);
-          if (FMT == 1) {  // a TQ2_0 block spans 4 adjacent threads: exact int32 sum of the 4 partial dots
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-          }
-          const bool lead = valid && (FMT == 0 || (c & 3) == 0);
-          const int64_t row = g * R + r;
-          if (lead && row < p.N) {
-            if (p.s) p.s[((int64_t)m * p.N + row) * nblk + blk] = s;
-            if (FMT == 0)
-              acc[r][m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), dx, acc[r][m]);
-            else
-              acc[r][m] = __fmaf_rn(__fmul_rn(dx, dw[r]), (float)s, acc[r][m]);
-          }
-        }
-      }
-    }
-
-    if (in == 0) {  // the unit's row group is complete: reduce across the CTA and store
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int m = 0; m < MC; ++m) {
-          float v = acc[r][m];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == 0) red[(buf * nwarps + warp) * (R * MC) + r * MC + m] = v;
-          acc[r][m] = 0.f;
-        }
-      __syncthreads();
-      if ((int)threadIdx.x < R * MC) {
-        const int r = threadIdx.x / MC, m = threadIdx.x - (threadIdx.x / MC) * MC;
-        const int64_t row = g * R + r;
-        if (m < M && row < p.N) {
-          float v = 0.f;
-          for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * (R * MC) + threadIdx.x];
-          p.y[(int64_t)m * p.ldy + p.row0 + row] = v;
-        }
-      }
+    compute_chunk<FMT, R, MC, BYTES>(p, g, c, c < C, cur.w, dw, xs, xsum, xscale, acc);
+    if (in == 0) {
+      reduce_store<R, MC>(p, g, acc, red, buf);
       buf ^= 1;
     }
     cur = nxt;
     g = gn;
     i = in;
   }
+  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
+}
 
-  if (p.y_peers != nullptr) {
-    // fused all-gather: copy this CTA's output rows to every peer's copy of Y, then the last CTA runs the barrier
-    __syncthreads();
-    const int64_t r_begin = g_begin * R, r_end = min(g_end * R, p.N);
-    for (int m = 0; m < M; ++m) {
-      const int64_t base = (int64_t)m * p.ldy + p.row0;
-      for (int64_t row = r_begin + threadIdx.x; row < r_end; row += blockDim.x) {
-        const float v = p.y[base + row];
-        for (int q = 0; q < p.nranks; ++q)
-          if (q != p.rank) p.y_peers[q][base + row] = v;
-      }
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t* own = p.flags_peers[p.rank];
-      const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
-      if (arrived == gridDim.x - 1) {
-        own[p.nranks] = 0u;  // reset the arrival counter for the next call
-        __threadfence_system();
-        for (int q = 0; q < p.nranks; ++q) {
-          uint32_t* f = p.flags_peers[q] + p.rank;
-          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
-        }
-        int err = 0;
-        for (int q = 0; q < p.nranks && !err; ++q) {
-          long long spins = 0;
-          uint32_t v;
-          for (;;) {
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
-            if ((int32_t)(v - p.epoch) >= 0) break;
-            if (++spins > p.spin_limit) {
-              err = 1 + q;
-              break;
-            }
-            __nanosleep(64);
-          }
-        }
-        if (err && p.status) *p.status = err;
-      }
-    }
+// ------------------------------------------------------------------------------------------------------------------
+// Ring path: TMA bulk copies of whole row groups into an S-stage shared-memory ring.
+// ------------------------------------------------------------------------------------------------------------------
+template <int FMT, int R>
+__device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint32_t stage, uint32_t bar,
+                                            uint64_t pol) {
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const uint32_t qrow = (uint32_t)p.C * 16u, srow = (uint32_t)nblk * 2u;
+  const int64_t r0 = g * R;
+  const int rows = (int)min((int64_t)R, p.N - r0);
+  mbar_expect_tx(bar, (uint32_t)rows * (qrow + srow));
+  if (p.dense) {
+    bulk_g2s(stage, p.wq + r0 * p.ldwq, (uint32_t)rows * qrow, bar, pol);
+  } else {
+    for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, p.wq + (r0 + r) * p.ldwq, qrow, bar, pol);
   }
+  bulk_g2s(stage + R * qrow, p.ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
+}
+
+template <int FMT, int R, int MC>
+__global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_abort;
+  const int M = p.M, C = p.C, S = p.stages;
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
+  uint8_t* ring = smem;                                                          // [S][stage_bytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.stage_bytes);  // [S]
+  uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((S + 1) & ~1));               // 16-byte aligned
+  int* xsum = reinterpret_cast<int*>(xs + (size_t)M * p.K);
+  float* xscale = reinterpret_cast<float*>(xsum + M * C);
+  float* red = xscale + M * nblk;
+
+  const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
+  const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
+  const int64_t ngroups = g_end - g_begin;
+  const uint32_t ring_addr = smem_addr(ring), bar_addr = smem_addr(bars);
+  uint64_t pol = 0;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < S; ++s) mbar_init(bar_addr + 8 * s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    pol = evict_first_policy();
+    for (int64_t j = 0; j < min((int64_t)(S - 1), ngroups); ++j)
+      issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
+  }
+  stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
+
+  float acc[R][MC];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MC; ++m) acc[r][m] = 0.f;
+
+  int buf = 0;
+  int64_t j = 0;
+  for (; j < ngroups; ++j) {
+    const int s = (int)(j % S);
+    if (threadIdx.x == 0 && j + S - 1 < ngroups) {
+      // stage (j-1)%S was released by the previous group's __syncthreads
+      const int sn = (int)((j + S - 1) % S);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue_group<FMT, R>(p, g_begin + j + S - 1, ring_addr + (uint32_t)sn * p.stage_bytes, bar_addr + 8 * sn, pol);
+    }
+    if (!mbar_wait(bar_addr + 8 * s, (uint32_t)((j / S) & 1), kWaitLimit)) {
+      s_abort = 1;
+      atomicCAS(&g_device_error, 0, kErrTimeout);
+    }
+    const uint32_t stage = ring_addr + (uint32_t)s * p.stage_bytes;
+    const int64_t g = g_begin + j;
+    for (int i = 0; i < p.CPT; ++i) {
+      const int c = (int)threadIdx.x + i * (int)blockDim.x;
+      const bool valid = c < C;
+      const int blk = c >> Fmt<FMT>::kChunkShift;
+      uint4 w[R];
+      float dw[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (valid) {
+          w[r] = lds_v4(stage + r * qrow + (uint32_t)c * 16u);
+          dw[r] = f16_bits_to_f32(lds_u16(stage + R * qrow + r * srow + (uint32_t)blk * 2u));
+        } else {
+          w[r] = make_uint4(0u, 0u, 0u, 0u);
+          dw[r] = 0.f;
+        }
+      }
+      compute_chunk<FMT, R, MC, false>(p, g, c, valid, w, dw, xs, xsum, xscale, acc);
+    }
+    reduce_store<R, MC>(p, g, acc, red, buf);
+    buf ^= 1;
+    if (s_abort) break;  // uniform: read after the reduction's __syncthreads
+  }
+  if (s_abort) {
+    // drain: wait (bounded) for copies that were issued but not consumed, then leave
+    if (threadIdx.x == 0) {
+      for (int64_t jj = j; jj < min(ngroups, j + S); ++jj)
+        mbar_wait(bar_addr + 8 * (uint32_t)(jj % S), (uint32_t)((jj / S) & 1), kWaitLimit);
+    }
+    return;
+  }
+  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -397,20 +631,33 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_kernel(const GemvParams p
 using KernelFn = void (*)(const GemvParams);
 
 template <int FMT, bool BYTES>
-static KernelFn pick_kernel(int R, int MC) {
+static KernelFn pick_reg(int R, int MC) {
   if (MC == 1) {
-    if (R == 1) return gemv_kernel<FMT, 1, 1, BYTES>;
-    if (R == 2) return gemv_kernel<FMT, 2, 1, BYTES>;
-    return gemv_kernel<FMT, 4, 1, BYTES>;
+    if (R == 1) return gemv_reg_kernel<FMT, 1, 1, BYTES>;
+    if (R == 2) return gemv_reg_kernel<FMT, 2, 1, BYTES>;
+    return gemv_reg_kernel<FMT, 4, 1, BYTES>;
   }
-  if (R == 1) return gemv_kernel<FMT, 1, 4, BYTES>;
-  if (R == 2) return gemv_kernel<FMT, 2, 4, BYTES>;
-  return gemv_kernel<FMT, 4, 4, BYTES>;
+  if (R == 1) return gemv_reg_kernel<FMT, 1, 4, BYTES>;
+  if (R == 2) return gemv_reg_kernel<FMT, 2, 4, BYTES>;
+  return gemv_reg_kernel<FMT, 4, 4, BYTES>;
 }
 
-static KernelFn kernel_for(int fmt, bool bytes, int R, int MC) {
-  if (fmt == 0) return bytes ? pick_kernel<0, true>(R, MC) : pick_kernel<0, false>(R, MC);
-  return bytes ? pick_kernel<1, true>(R, MC) : pick_kernel<1, false>(R, MC);
+template <int FMT>
+static KernelFn pick_ring(int R, int MC) {
+  if (MC == 1) {
+    if (R == 1) return gemv_ring_kernel<FMT, 1, 1>;
+    if (R == 2) return gemv_ring_kernel<FMT, 2, 1>;
+    return gemv_ring_kernel<FMT, 4, 1>;
+  }
+  if (R == 1) return gemv_ring_kernel<FMT, 1, 4>;
+  if (R == 2) return gemv_ring_kernel<FMT, 2, 4>;
+  return gemv_ring_kernel<FMT, 4, 4>;
+}
+
+static KernelFn kernel_for(int fmt, bool bytes, bool ring, int R, int MC) {
+  if (ring) return fmt == 0 ? pick_ring<0>(R, MC) : pick_ring<1>(R, MC);
+  if (fmt == 0) return bytes ? pick_reg<0, true>(R, MC) : pick_reg<0, false>(R, MC);
+  return bytes ? pick_reg<1, true>(R, MC) : pick_reg<1, false>(R, MC);
 }
 
 struct OccKey {
@@ -440,8 +687,11 @@ static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) 
     auto it = g_occ.find(key);
     if (it != g_occ.end()) return it->second;
   }
-  if (cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_optin) !=
-      cudaSuccess)
+  cudaFuncAttributes attr;
+  if (cudaFuncGetAttributes(&attr, (const void*)fn) != cudaSuccess) return -1;
+  if (smem + attr.sharedSizeBytes > (size_t)max_smem_optin) return 0;
+  if (cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           max_smem_optin - (int)attr.sharedSizeBytes) != cudaSuccess)
     return -1;
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, (const void*)fn, threads, smem) != cudaSuccess)
@@ -451,22 +701,32 @@ static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) 
   return blocks;
 }
 
-static int g_tune_rows = 0;   // 0 = planner's choice
-static int g_tune_cpt = 0;
-static int g_tune_grid = 0;
+// Tuning overrides (benchmark hook): 0 = planner's choice.
+static int g_tune_rows = 0, g_tune_cpt = 0, g_tune_grid = 0, g_tune_stages = 0, g_tune_path = 0;
 
 struct Plan {
-  int R, T, CPT, grid;
+  int R, T, CPT, grid, stages;
+  uint32_t stage_bytes;
   size_t smem;
+  bool ring;
   KernelFn fn;
 };
 
-static size_t smem_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T) {
+static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T) {
   const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
   return (size_t)M * K + (size_t)M * C * 4 + (size_t)M * nblk * 4 + (size_t)2 * (T / 32) * R * MC * 4;
 }
 
-static int make_plan(int fmt, bool bytes, int64_t N, int64_t K, int M, Plan* out) {
+static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
+  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  const uint32_t s = (uint32_t)R * (uint32_t)nblk * 2u;
+  return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
+}
+
+// Bytes of weights a CTA keeps in flight; the planner aims at kInflightTarget per SM.
+constexpr double kInflightTarget = 96.0 * 1024;
+
+static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -477,32 +737,52 @@ static int make_plan(int fmt, bool bytes, int64_t N, int64_t K, int M, Plan* out
   const int T = std::min(kMaxThreads, ((C + CPT - 1) / CPT + 31) / 32 * 32);
   if ((int64_t)T * CPT < C)
     return fail(B2Q_ERANGE, "gemv: K=%lld needs more than %d chunks per thread", (long long)K, CPT);
+  bool use_ring = ring_ok && !bytes && g_tune_path != 2;
+  if (g_tune_path == 1 && !use_ring) return fail(B2Q_EINVAL, "gemv: ring path forced but not applicable");
   Plan best{};
-  double best_eff = -1.0;
+  double best_score = -1.0;
   const int cand[3] = {4, 2, 1};
-  for (int ci = 0; ci < 3; ++ci) {
-    const int R = cand[ci];
-    if (g_tune_rows > 0 && R != g_tune_rows) continue;
-    const size_t smem = smem_bytes(fmt, K, M, C, R, MC, T);
-    if (smem > (size_t)di.max_smem_optin) continue;
-    KernelFn fn = kernel_for(fmt, bytes, R, MC);
-    const int occ = occupancy(fn, T, smem, di.max_smem_optin);
-    if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
-    if (occ == 0) continue;
-    const int64_t groups = (N + R - 1) / R;
-    int64_t grid = std::min<int64_t>(groups, (int64_t)occ * di.sms);
-    if (g_tune_grid > 0) grid = std::min<int64_t>(groups, g_tune_grid);
-    // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
-    const int64_t per = (groups + grid - 1) / grid;
-    double eff = (double)groups / (double)(per * grid);
-    // shorter rows amortize less per reduction: prefer larger R on near-ties
-    eff += 0.002 * R;
-    if (eff > best_eff) {
-      best_eff = eff;
-      best = Plan{R, T, CPT, (int)grid, smem, fn};
+  for (int pass = 0; pass < 2 && best_score < 0; ++pass) {
+    const bool ring = use_ring && pass == 0;
+    if (pass == 1 && g_tune_path == 1) break;
+    for (int ci = 0; ci < 3; ++ci) {
+      const int R = cand[ci];
+      if (g_tune_rows > 0 && R != g_tune_rows) continue;
+      const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T);
+      const int64_t groups = (N + R - 1) / R;
+      int stages = 0;
+      uint32_t sb = 0;
+      size_t smem = xb;
+      if (ring) {
+        sb = ring_stage_bytes(fmt, K, C, R);
+        // smallest ring with enough bytes in flight for one CTA, at least double-buffered
+        stages = (int)std::min<double>(8.0, std::max(2.0, 1.0 + std::ceil(kInflightTarget / 2 / sb)));
+        if (g_tune_stages > 0) stages = g_tune_stages;
+        while (stages > 2 && (size_t)stages * sb + 16 * (stages + 1) + xb > (size_t)di.max_smem_optin) --stages;
+        smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
+      }
+      if (smem > (size_t)di.max_smem_optin) continue;
+      KernelFn fn = kernel_for(fmt, bytes, ring, R, MC);
+      const int occ = occupancy(fn, T, smem, di.max_smem_optin);
+      if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
+      if (occ == 0) continue;
+      int64_t grid = std::min<int64_t>(groups, (int64_t)occ * di.sms);
+      if (g_tune_grid > 0) grid = std::min<int64_t>(groups, g_tune_grid);
+      // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
+      const int64_t per = (groups + grid - 1) / grid;
+      const double balance = (double)groups / (double)(per * grid);
+      // memory-level parallelism per SM relative to the target
+      double inflight = ring ? (double)std::min<int64_t>(occ, (grid + di.sms - 1) / di.sms) * (stages - 1) * sb
+                             : (double)std::min<int64_t>(occ, (grid + di.sms - 1) / di.sms) * T * R * 16 * 2;
+      const double mlp = std::min(1.0, inflight / kInflightTarget);
+      const double score = balance * (0.5 + 0.5 * mlp) + 0.002 * R;
+      if (score > best_score) {
+        best_score = score;
+        best = Plan{R, T, CPT, (int)grid, stages, sb, smem, ring, fn};
+      }
     }
   }
-  if (best_eff < 0)
+  if (best_score < 0)
     return fail(B2Q_ERANGE, "gemv: K=%lld with %d columns does not fit in shared memory (%d bytes max)",
                 (long long)K, M, di.max_smem_optin);
   *out = best;
@@ -560,19 +840,20 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   if (a.N == 0 || a.M == 0 || a.K == 0) {
     // empty reductions: Y = 0 (K == 0); nothing to do for N == 0 or M == 0
     if (a.K == 0 && a.N > 0 && a.M > 0) {
-      for (int64_t m = 0; m < a.M; ++m) {
-        cudaError_t e = cudaMemsetAsync(a.y + m * a.ldy + a.row0, 0, (size_t)a.N * 4, stream);
-        if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemv: cudaMemsetAsync: %s", cudaGetErrorString(e));
-      }
+      cudaError_t e = cudaMemset2DAsync(a.y + a.row0, (size_t)a.ldy * 4, 0, (size_t)a.N * 4, (size_t)a.M, stream);
+      if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemv: cudaMemset2DAsync: %s", cudaGetErrorString(e));
     }
     return B2Q_OK;
   }
   const int blk = a.fmt == 0 ? 32 : 256;
   const int64_t nblk = a.K / blk;
+  const int C = (int)(a.K / (a.fmt == 0 ? 32 : 64));
+  // ring path: every row's scale bytes (and so every group's) must be a whole number of 16-byte units, 16-aligned
+  const bool ring_ok = ((nblk * 2) % 16 == 0) && aligned(a.ws, 16);
   for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
     const int Mc = (int)std::min<int64_t>(kMaxColumns, a.M - m0);
     Plan pl;
-    int rc = make_plan(a.fmt, a.bytes, a.N, a.K, Mc, &pl);
+    int rc = make_plan(a.fmt, a.bytes, ring_ok, a.N, a.K, Mc, &pl);
     if (rc) return rc;
     GemvParams p{};
     p.wq = a.wq;
@@ -598,9 +879,12 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.N = a.N;
     p.K = a.K;
     p.M = Mc;
-    p.C = (int)(a.K / (a.fmt == 0 ? 32 : 64));
+    p.C = C;
     p.CPT = pl.CPT;
     p.groups = (a.N + pl.R - 1) / pl.R;
+    p.stages = pl.stages;
+    p.stage_bytes = pl.stage_bytes;
+    p.dense = (a.ldwq == (int64_t)C * 16) ? 1 : 0;
     pl.fn<<<pl.grid, pl.T, pl.smem, stream>>>(p);
     rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
     if (rc) return rc;
@@ -647,7 +931,8 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
   if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not Q4_0 (0) or TQ2_0 (1)", fmt);
   int rc = check_gemv_args("b2q_quant_gemv", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
-  if (ldx < K || (ldx % 4)) return fail(B2Q_EALIGN, "b2q_quant_gemv: ldx must be >= K and a multiple of 4");
+  if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
+    return fail(B2Q_EALIGN, "b2q_quant_gemv: ldx must be >= K and a multiple of 4");
   if ((xq == nullptr) != (xd == nullptr)) return fail(B2Q_EINVAL, "b2q_quant_gemv: give both xq and xd, or neither");
   if (xq && !aligned(xq, 16)) return fail(B2Q_EALIGN, "b2q_quant_gemv: xq must be 16-byte aligned");
   if (xd && !aligned(xd, 4)) return fail(B2Q_EALIGN, "b2q_quant_gemv: xd must be 4-byte aligned");
@@ -662,29 +947,12 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
                        const float* xd, float* const* y_peers, uint32_t* const* flags_peers, int32_t* status,
                        int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M, int rank, int nranks,
                        uint32_t epoch, long long spin_limit, b2q_stream_t stream) {
-  (void)fmt;
-  (void)wq;
-  (void)ldwq;
-  (void)ws;
-  (void)xq;
-  (void)xd;
-  (void)y_peers;
-  (void)flags_peers;
-  (void)status;
-  (void)row0;
-  (void)n_local;
-  (void)N_total;
-  (void)K;
-  (void)M;
-  (void)rank;
-  (void)nranks;
-  (void)epoch;
-  (void)spin_limit;
-  (void)stream;
+  (void)fmt, (void)wq, (void)ldwq, (void)ws, (void)xq, (void)xd, (void)y_peers, (void)flags_peers, (void)status;
+  (void)row0, (void)n_local, (void)N_total, (void)K, (void)M, (void)rank, (void)nranks, (void)epoch;
+  (void)spin_limit, (void)stream;
   return fail(B2Q_EINVAL, "b2q_gemv_allgather: not enabled in this build");
 }
 
-// Benchmark/tuning hook: force rows per group (1, 2, 4), chunks per thread and grid size; 0 restores the planner.
 int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
   if (rows_per_group != 0 && rows_per_group != 1 && rows_per_group != 2 && rows_per_group != 4)
     return fail(B2Q_EINVAL, "b2q_set_tuning: rows_per_group must be 0, 1, 2 or 4");
@@ -692,6 +960,26 @@ int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
   g_tune_rows = rows_per_group;
   g_tune_cpt = chunks_per_thread;
   g_tune_grid = grid;
+  return B2Q_OK;
+}
+
+int b2q_set_pipeline(int path, int stages) {
+  if (path < 0 || path > 2) return fail(B2Q_EINVAL, "b2q_set_pipeline: path must be 0 (auto), 1 (ring), 2 (registers)");
+  if (stages < 0 || stages == 1 || stages > 8) return fail(B2Q_EINVAL, "b2q_set_pipeline: stages must be 0 or 2..8");
+  g_tune_path = path;
+  g_tune_stages = stages;
+  return B2Q_OK;
+}
+
+int b2q_device_error(int* code, int clear) {
+  if (!code) return fail(B2Q_EINVAL, "b2q_device_error: null pointer");
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail(B2Q_ECUDA, "b2q_device_error: %s", cudaGetErrorString(e));
+  if (clear && *code) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(B2Q_ECUDA, "b2q_device_error: %s", cudaGetErrorString(e));
+  }
   return B2Q_OK;
 }
 

@@ -178,11 +178,12 @@ def _check_weights(fmt, wq, ws, n, k):
     if k % f["block"]:
         raise ValueError(f"gemv: k={k} is not a multiple of the {fmt} block ({f['block']})")
     qbytes = k // f["block"] * f["qbytes"]
-    if wq.dtype != torch.uint8 or wq.dim() != 2 or wq.shape[0] != n or wq.shape[1] < qbytes or wq.stride(1) != 1:
+    if wq.dtype != torch.uint8 or wq.dim() != 2 or wq.shape[0] != n or wq.shape[1] < qbytes or \
+            (wq.numel() and wq.stride(1) != 1):
         raise ValueError(f"gemv: wq must be uint8 [{n}][>= {qbytes}] with unit column stride, got {wq.dtype} "
                          f"{tuple(wq.shape)}")
     _check(ws, "ws", torch.int16, (n, k // f["block"]))
-    if not ws.is_contiguous():
+    if ws.numel() and not ws.is_contiguous():
         raise ValueError("gemv: ws must be contiguous")
 
 

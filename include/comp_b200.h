@@ -127,6 +127,14 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
  * GEMV schedule; 0 restores the planner's choice. Results do not depend on it (except the f32 summation order). */
 int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid);
 
+/* Benchmark/tuning hook (process-wide): weight-streaming path 0 = planner's choice, 1 = TMA bulk-copy ring in shared
+ * memory, 2 = streaming loads into registers; stages = ring depth (0 = planner, else 2..8). Results do not change. */
+int b2q_set_pipeline(int path, int stages);
+
+/* Reads (and with clear != 0 resets) the library's device error word: nonzero if a kernel's bounded wait on an
+ * mbarrier gave up (the kernel then returned early; its outputs are invalid). Synchronizes with the device. */
+int b2q_device_error(int* code, int clear);
+
 /* CUDA IPC helpers for the multi-GPU path: export a device allocation as a 64-byte handle, open a peer's handle. */
 int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64);
 int b2q_ipc_open_handle(const void* handle64, void** dev_ptr_out);
