@@ -28,636 +28,21 @@
 //   * Per-group reduction: warp shuffles, then a cross-warp sum in shared memory in fixed warp order. The summation
 //     order of a row depends only on (K, T, CPT), so Y is bit-identical across paths, variants, R and grid size.
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <unordered_map>
 
-#include "b2q_device.cuh"
-#include "b2q_internal.h"
+#include "gemv_kernels.cuh"
 
 namespace b2q {
 
-constexpr int kMaxThreads = 512;
-constexpr int kMaxColumns = 4;  // columns per launch; more are processed in groups of 4 (weights re-read per group)
-constexpr long long kWaitLimit = 1LL << 20;  // bounded mbarrier polls (each try_wait also suspends in hardware)
-constexpr int kErrTimeout = 1;
-
-// Set by a kernel whose bounded wait gave up (read and cleared by b2q_device_error).
-__device__ int g_device_error = 0;
-
-struct GemvParams {
-  const uint8_t* wq;
-  int64_t ldwq;
-  const int16_t* ws;
-  const int8_t* xq;       // int8 activations [M][K] (null when x_f32 is given)
-  const float* xd;        // activation scales [M][nblk] (null when x_f32 is given)
-  const float* x_f32;     // f32 activations [M][ldx] for the fused quantizer prologue, or null
-  int64_t ldx;
-  int8_t* xq_out;         // fused prologue: CTA 0 also stores the quantized activations here (nullable)
-  float* xd_out;
-  float* y;               // [M][ldy]; output row index is row0 + local row
-  int64_t ldy;
-  int64_t row0;
-  int32_t* s;             // [M][N][nblk] int32 block dots (nullable)
-  // fused all-gather epilogue (multi-GPU): y is this rank's copy; every CTA also copies its rows to the peers
-  float* const* y_peers;  // device array [nranks] or null
-  uint32_t* const* flags_peers;  // device array [nranks] of flag arrays (each [nranks + 1] uint32) or null
-  int32_t* status;
-  int rank, nranks;
-  uint32_t epoch;
-  long long spin_limit;
-  int64_t N;              // rows in this launch
-  int64_t K;
-  int M;                  // columns in this launch (1..kMaxColumns)
-  int C;                  // 16-byte chunks per row
-  int CPT;                // chunks per thread per row
-  int64_t groups;         // ceil(N / R)
-  int stages;             // ring path: shared-memory stages
-  uint32_t stage_bytes;   // ring path: bytes per stage (R rows of quants, then R rows of scales, 16-byte padded)
-  int dense;              // ring path: ldwq == C*16, so a group's quant rows are one contiguous copy
-};
-
-template <int FMT>
-struct Fmt;
-template <>
-struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibbles)
-  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2;
-};
-template <>
-struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
-  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4;
-};
-
-// Position (in 16-byte units, within one activation column) of the q-th 16-byte piece of the natural int8 layout.
-template <int FMT>
-__device__ __forceinline__ int perm_unit(int q, int C) {
-  if (FMT == 0) return (q & 1) * C + (q >> 1);  // block b = q/2, nibble field h = q%2
-  const int b = q >> 4, o = q & 15;              // 16 pieces per 256-value block
-  const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
-  return j * C + 4 * b + c;
-}
-
 // ------------------------------------------------------------------------------------------------------------------
-// mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk; sm_90+)
-// ------------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-// Bounded wait for the phase with the given parity to complete; false if the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
-  for (long long i = 0; i < limit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-// Global -> shared bulk copy (no multicast), completion counted in bytes on `bar`. dst, src, bytes: multiples of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
-  uint16_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-  return v;
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// Activation prologue: fills xs (permuted int8), xsum (per-chunk offset correction) and xscale (per-block f32 scale).
-// Loads are batched (kUnroll per thread in flight) so the prologue costs a few L2 round trips, not one per item.
-// ------------------------------------------------------------------------------------------------------------------
-constexpr int kUnroll = 4;
-
-template <int FMT>
-__device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int* xsum, float* xscale) {
-  const int T = blockDim.x, tt = threadIdx.x;
-  const int K = (int)p.K, C = p.C, M = p.M;
-  const int nblk = K / Fmt<FMT>::kBlock;
-  if (p.x_f32 == nullptr) {
-    const int units = K / 16;
-    const int total = M * units;
-    for (int base = tt; base < total; base += T * kUnroll) {
-      uint4 v[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int idx = base + u * T;
-        if (idx < total) {
-          const int m = idx / units, q = idx - m * units;
-          v[u] = *reinterpret_cast<const uint4*>(p.xq + (int64_t)m * K + (int64_t)q * 16);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int idx = base + u * T;
-        if (idx < total) {
-          const int m = idx / units, q = idx - m * units;
-          *reinterpret_cast<uint4*>(xs + (int64_t)m * K + perm_unit<FMT>(q, C) * 16) = v[u];
-        }
-      }
-    }
-    for (int idx = tt; idx < M * nblk; idx += T) xscale[idx] = p.xd[idx];
-  } else if (FMT == 0) {
-    // q8_0: 8 lanes per 32-value block (4 blocks per warp per slot); kUnroll slots of loads in flight per lane
-    const int lane = tt & 31, sub = lane & 7, nw = T / 32;
-    const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
-    const int total = M * nblk;
-    for (int base = (tt >> 5) * 4; base < total; base += nw * 4 * kUnroll) {
-      float4 v[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int g = base + u * nw * 4 + (lane >> 3);
-        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (g < total) {
-          const int m = g / nblk, b = g - m * nblk;
-          v[u] = *reinterpret_cast<const float4*>(p.x_f32 + (int64_t)m * p.ldx + b * 32 + sub * 4);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int g = base + u * nw * 4 + (lane >> 3);
-        float d;
-        const uint32_t q = q8_0_quant4(v[u], &d);  // whole warp: shuffles inside
-        if (g < total) {
-          const int m = g / nblk, b = g - m * nblk;
-          *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + ((sub >> 2) * C + b) * 16 + (sub & 3) * 4) = q;
-          const float ds = q8_0_stored_scale(d);
-          if (sub == 0) xscale[m * nblk + b] = ds;
-          if (writer) {
-            *reinterpret_cast<uint32_t*>(p.xq_out + (int64_t)m * K + b * 32 + sub * 4) = q;
-            if (sub == 0 && p.xd_out) p.xd_out[m * nblk + b] = ds;
-          }
-        }
-      }
-    }
-  } else {
-    // q8_K: one warp per 256-value block, lane l holds values 8l..8l+7; kUnroll blocks of loads in flight per warp
-    const int lane = tt & 31, nw = T / 32;
-    const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
-    const int total = M * nblk;
-    for (int base = tt >> 5; base < total; base += nw * kUnroll) {
-      float4 va[kUnroll], vb[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int g = base + u * nw;
-        va[u] = vb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (g < total) {
-          const int m = g / nblk, b = g - m * nblk;
-          const float* src = p.x_f32 + (int64_t)m * p.ldx + b * 256 + lane * 8;
-          va[u] = *reinterpret_cast<const float4*>(src);
-          vb[u] = *reinterpret_cast<const float4*>(src + 4);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int g = base + u * nw;
-        if (g < total) {  // warp-uniform
-          const int m = g / nblk, b = g - m * nblk;
-          const float v[8] = {va[u].x, va[u].y, va[u].z, va[u].w, vb[u].x, vb[u].y, vb[u].z, vb[u].w};
-          uint32_t qlo, qhi;
-          const float d = q8_K_quant8(v, lane, &qlo, &qhi);
-          const int o = lane >> 1;  // 16-value piece within the block
-          const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
-          *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + 4 * b + c) * 16 + (lane & 1) * 8) =
-              make_uint2(qlo, qhi);
-          if (lane == 0) xscale[m * nblk + b] = d;
-          if (writer) {
-            *reinterpret_cast<uint2*>(p.xq_out + (int64_t)m * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
-            if (lane == 0 && p.xd_out) p.xd_out[m * nblk + b] = d;
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-  // per-chunk activation sums: Q4_0 8 * (sum of the block's 32 values); TQ2_0 sum of the chunk's 64 values
-  for (int idx = tt; idx < M * C; idx += T) {
-    const int m = idx / C, c = idx - m * C;
-    const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * K);
-    int sum = 0;
-#pragma unroll
-    for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
-      const uint4 v = col[j * C + c];
-      sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
-    }
-    xsum[idx] = (FMT == 0) ? 8 * sum : sum;
-  }
-  __syncthreads();
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// Integer block dots of one chunk: weight word w (4 words of 16 bytes) against the activation fields of column m.
-// ------------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
-  return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
-}
-
-template <int FMT, bool BYTES>
-__device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
-  if (!BYTES) {
-    if (FMT == 0) {
-      int lo = 0, hi = 0;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t wk = word_of(w, k);
-        lo = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(x[0], k), lo);
-        hi = dp4a_us(wk & 0xF0F0F0F0u, (int)word_of(x[1], k), hi);
-      }
-      return lo + (hi >> 4) - xsum;
-    } else {
-      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t wk = word_of(w, k);
-        a0 = dp4a_us(wk & 0x03030303u, (int)word_of(x[0], k), a0);
-        a1 = dp4a_us(wk & 0x0C0C0C0Cu, (int)word_of(x[1], k), a1);
-        a2 = dp4a_us(wk & 0x30303030u, (int)word_of(x[2], k), a2);
-        a3 = dp4a_us(wk & 0xC0C0C0C0u, (int)word_of(x[3], k), a3);
-      }
-      return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - xsum;
-    }
-  } else {
-    // byte-wise variant (the reference's MODE 0): every value unpacked to an int32, no offset correction needed
-    int s = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t wk = word_of(w, k);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int wb = (int)((wk >> (8 * t)) & 0xffu);
-#pragma unroll
-        for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
-          const int xb = (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
-          const int val = (FMT == 0) ? ((wb >> (4 * j)) & 15) - 8 : ((wb >> (2 * j)) & 3) - 1;
-          s += val * xb;
-        }
-      }
-    }
-    return s;
-  }
-}
-
-// One chunk c of R rows (weights w[r], scales dw[r]) against all columns: block dots, S store, f32 accumulation.
-template <int FMT, int R, int MC, bool BYTES>
-__device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, int c, bool valid, const uint4 (&w)[R],
-                                              const float (&dw)[R], const uint8_t* xs, const int* xsum,
-                                              const float* xscale, float (&acc)[R][MC]) {
-  const int C = p.C, M = p.M;
-  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const int blk = c >> Fmt<FMT>::kChunkShift;
-#pragma unroll
-  for (int m = 0; m < MC; ++m) {
-    if (m < M) {
-      uint4 x[4];
-      int xs_sum = 0;
-      float dx = 0.f;
-      if (valid) {
-        const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * p.K);
-#pragma unroll
-        for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = col[j * C + c];
-        xs_sum = xsum[m * C + c];
-        dx = xscale[m * nblk + blk];
-      } else {
-#pragma unroll
-        for (int j = 0; j < Fmt<FMT>::kFields; ++j) x[j] = make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        int s = chunk_dot<FMT, BYTES>(w[r], x, xs_sum);
-        if (FMT == 1) {  // a TQ2_0 block spans 4 adjacent threads: exact int32 sum of the 4 partial dots
-          s += __shfl_xor_sync(0xffffffffu, s, 1);
-          s += __shfl_xor_sync(0xffffffffu, s, 2);
-        }
-        const bool lead = valid && (FMT == 0 || (c & 3) == 0);
-        const int64_t row = g * R + r;
-        if (lead && row < p.N) {
-          if (p.s) p.s[((int64_t)m * p.N + row) * nblk + blk] = s;
-          if (FMT == 0)
-            acc[r][m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), dx, acc[r][m]);
-          else
-            acc[r][m] = __fmaf_rn(__fmul_rn(dx, dw[r]), (float)s, acc[r][m]);
-        }
-      }
-    }
-  }
-}
-
-// Group reduction: warp shuffles, cross-warp sum in fixed order, store of R x M outputs. Contains __syncthreads.
-template <int R, int MC>
-__device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, float (&acc)[R][MC], float* red,
-                                             int buf) {
-  const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      float v = acc[r][m];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[(buf * nwarps + warp) * (R * MC) + r * MC + m] = v;
-      acc[r][m] = 0.f;
-    }
-  __syncthreads();
-  if ((int)threadIdx.x < R * MC) {
-    const int r = threadIdx.x / MC, m = threadIdx.x - (threadIdx.x / MC) * MC;
-    const int64_t row = g * R + r;
-    if (m < p.M && row < p.N) {
-      float v = 0.f;
-      for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * (R * MC) + threadIdx.x];
-      p.y[(int64_t)m * p.ldy + p.row0 + row] = v;
-    }
-  }
-}
-
-// Fused all-gather epilogue: copies this CTA's rows of Y to every peer, then the last CTA runs the flag barrier.
-__device__ void allgather_epilogue(const GemvParams& p, int64_t g_begin, int64_t g_end, int R) {
-  __syncthreads();
-  const int64_t r_begin = g_begin * R, r_end = min(g_end * R, p.N);
-  for (int m = 0; m < p.M; ++m) {
-    const int64_t base = (int64_t)m * p.ldy + p.row0;
-    for (int64_t row = r_begin + threadIdx.x; row < r_end; row += blockDim.x) {
-      const float v = p.y[base + row];
-      for (int q = 0; q < p.nranks; ++q)
-        if (q != p.rank) p.y_peers[q][base + row] = v;
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t* own = p.flags_peers[p.rank];
-    const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
-    if (arrived == gridDim.x - 1) {
-      own[p.nranks] = 0u;  // reset the arrival counter for the next call
-      __threadfence_system();
-      for (int q = 0; q < p.nranks; ++q) {
-        uint32_t* f = p.flags_peers[q] + p.rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
-      }
-      int err = 0;
-      for (int q = 0; q < p.nranks && !err; ++q) {
-        long long spins = 0;
-        uint32_t v;
-        for (;;) {
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
-          if ((int32_t)(v - p.epoch) >= 0) break;
-          if (++spins > p.spin_limit) {
-            err = 1 + q;
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-      if (err && p.status) *p.status = err;
-    }
-  }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// Register path: weights streamed straight into registers, double-buffered one unit (group, chunk round) ahead.
-// ------------------------------------------------------------------------------------------------------------------
-template <int R>
-struct WeightRegs {
-  uint4 w[R];
-  uint16_t sc[R];
-};
-
-template <int FMT, int R>
-__device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i, bool active, WeightRegs<R>& u) {
-  const int c = (int)threadIdx.x + i * (int)blockDim.x;
-  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int64_t row = g * R + r;
-    if (active && c < p.C && row < p.N) {
-      u.w[r] = ld_stream_v4(p.wq + row * p.ldwq + (int64_t)c * 16);
-      u.sc[r] = ld_stream_u16(p.ws + row * nblk + (c >> Fmt<FMT>::kChunkShift));
-    } else {
-      u.w[r] = make_uint4(0u, 0u, 0u, 0u);
-      u.sc[r] = 0;
-    }
-  }
-}
-
-template <int FMT, int R, int MC, bool BYTES>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int M = p.M, C = p.C;
-  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  uint8_t* xs = smem;                                                    // [M][K] permuted int8
-  int* xsum = reinterpret_cast<int*>(smem + (size_t)M * p.K);             // [M][C]
-  float* xscale = reinterpret_cast<float*>(xsum + M * C);                // [M][nblk]
-  float* red = xscale + M * nblk;                                        // [2][warps][R*MC]
-
-  const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
-  const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
-
-  WeightRegs<R> cur, nxt;
-  load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
-  stage_activations<FMT>(p, xs, xsum, xscale);
-
-  float acc[R][MC];
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int m = 0; m < MC; ++m) acc[r][m] = 0.f;
-
-  int buf = 0;
-  int64_t g = g_begin;
-  int i = 0;
-  while (g < g_end) {
-    int64_t gn = g;
-    int in = i + 1;
-    if (in == p.CPT) {
-      in = 0;
-      gn = g + 1;
-    }
-    load_unit<FMT, R>(p, gn, in, gn < g_end, nxt);
-
-    const int c = (int)threadIdx.x + i * (int)blockDim.x;
-    float dw[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) dw[r] = f16_bits_to_f32(cur.sc[r]);
-    compute_chunk<FMT, R, MC, BYTES>(p, g, c, c < C, cur.w, dw, xs, xsum, xscale, acc);
-    if (in == 0) {
-      reduce_store<R, MC>(p, g, acc, red, buf);
-      buf ^= 1;
-    }
-    cur = nxt;
-    g = gn;
-    i = in;
-  }
-  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// Ring path: TMA bulk copies of whole row groups into an S-stage shared-memory ring.
-// ------------------------------------------------------------------------------------------------------------------
-template <int FMT, int R>
-__device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint32_t stage, uint32_t bar,
-                                            uint64_t pol) {
-  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const uint32_t qrow = (uint32_t)p.C * 16u, srow = (uint32_t)nblk * 2u;
-  const int64_t r0 = g * R;
-  const int rows = (int)min((int64_t)R, p.N - r0);
-  mbar_expect_tx(bar, (uint32_t)rows * (qrow + srow));
-  if (p.dense) {
-    bulk_g2s(stage, p.wq + r0 * p.ldwq, (uint32_t)rows * qrow, bar, pol);
-  } else {
-    for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, p.wq + (r0 + r) * p.ldwq, qrow, bar, pol);
-  }
-  bulk_g2s(stage + R * qrow, p.ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
-}
-
-template <int FMT, int R, int MC>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_abort;
-  const int M = p.M, C = p.C, S = p.stages;
-  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
-  uint8_t* ring = smem;                                                          // [S][stage_bytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.stage_bytes);  // [S]
-  uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((S + 1) & ~1));               // 16-byte aligned
-  int* xsum = reinterpret_cast<int*>(xs + (size_t)M * p.K);
-  float* xscale = reinterpret_cast<float*>(xsum + M * C);
-  float* red = xscale + M * nblk;
-
-  const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
-  const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
-  const int64_t ngroups = g_end - g_begin;
-  const uint32_t ring_addr = smem_addr(ring), bar_addr = smem_addr(bars);
-  uint64_t pol = 0;
-
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int s = 0; s < S; ++s) mbar_init(bar_addr + 8 * s, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    pol = evict_first_policy();
-    for (int64_t j = 0; j < min((int64_t)(S - 1), ngroups); ++j)
-      issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
-  }
-  stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
-
-  float acc[R][MC];
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int m = 0; m < MC; ++m) acc[r][m] = 0.f;
-
-  int buf = 0;
-  int64_t j = 0;
-  for (; j < ngroups; ++j) {
-    const int s = (int)(j % S);
-    if (threadIdx.x == 0 && j + S - 1 < ngroups) {
-      // stage (j-1)%S was released by the previous group's __syncthreads
-      const int sn = (int)((j + S - 1) % S);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue_group<FMT, R>(p, g_begin + j + S - 1, ring_addr + (uint32_t)sn * p.stage_bytes, bar_addr + 8 * sn, pol);
-    }
-    if (!mbar_wait(bar_addr + 8 * s, (uint32_t)((j / S) & 1), kWaitLimit)) {
-      s_abort = 1;
-      atomicCAS(&g_device_error, 0, kErrTimeout);
-    }
-    const uint32_t stage = ring_addr + (uint32_t)s * p.stage_bytes;
-    const int64_t g = g_begin + j;
-    for (int i = 0; i < p.CPT; ++i) {
-      const int c = (int)threadIdx.x + i * (int)blockDim.x;
-      const bool valid = c < C;
-      const int blk = c >> Fmt<FMT>::kChunkShift;
-      uint4 w[R];
-      float dw[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        if (valid) {
-          w[r] = lds_v4(stage + r * qrow + (uint32_t)c * 16u);
-          dw[r] = f16_bits_to_f32(lds_u16(stage + R * qrow + r * srow + (uint32_t)blk * 2u));
-        } else {
-          w[r] = make_uint4(0u, 0u, 0u, 0u);
-          dw[r] = 0.f;
-        }
-      }
-      compute_chunk<FMT, R, MC, false>(p, g, c, valid, w, dw, xs, xsum, xscale, acc);
-    }
-    reduce_store<R, MC>(p, g, acc, red, buf);
-    buf ^= 1;
-    if (s_abort) break;  // uniform: read after the reduction's __syncthreads
-  }
-  if (s_abort) {
-    // drain: wait (bounded) for copies that were issued but not consumed, then leave
-    if (threadIdx.x == 0) {
-      for (int64_t jj = j; jj < min(ngroups, j + S); ++jj)
-        mbar_wait(bar_addr + 8 * (uint32_t)(jj % S), (uint32_t)((jj / S) & 1), kWaitLimit);
-    }
-    return;
-  }
-  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
-}
-
 // ------------------------------------------------------------------------------------------------------------------
 // Host side: planning and launch
 // ------------------------------------------------------------------------------------------------------------------
 
-using KernelFn = void (*)(const GemvParams);
-
-template <int FMT, bool BYTES>
-static KernelFn pick_reg(int R, int MC) {
-  if (MC == 1) {
-    if (R == 1) return gemv_reg_kernel<FMT, 1, 1, BYTES>;
-    if (R == 2) return gemv_reg_kernel<FMT, 2, 1, BYTES>;
-    return gemv_reg_kernel<FMT, 4, 1, BYTES>;
-  }
-  if (R == 1) return gemv_reg_kernel<FMT, 1, 4, BYTES>;
-  if (R == 2) return gemv_reg_kernel<FMT, 2, 4, BYTES>;
-  return gemv_reg_kernel<FMT, 4, 4, BYTES>;
-}
-
-template <int FMT>
-static KernelFn pick_ring(int R, int MC) {
-  if (MC == 1) {
-    if (R == 1) return gemv_ring_kernel<FMT, 1, 1>;
-    if (R == 2) return gemv_ring_kernel<FMT, 2, 1>;
-    return gemv_ring_kernel<FMT, 4, 1>;
-  }
-  if (R == 1) return gemv_ring_kernel<FMT, 1, 4>;
-  if (R == 2) return gemv_ring_kernel<FMT, 2, 4>;
-  return gemv_ring_kernel<FMT, 4, 4>;
-}
-
-static KernelFn kernel_for(int fmt, bool bytes, bool ring, int R, int MC) {
-  if (ring) return fmt == 0 ? pick_ring<0>(R, MC) : pick_ring<1>(R, MC);
-  if (fmt == 0) return bytes ? pick_reg<0, true>(R, MC) : pick_reg<0, false>(R, MC);
-  return bytes ? pick_reg<1, true>(R, MC) : pick_reg<1, false>(R, MC);
+static KernelFn kernel_for(int fmt, bool bytes, bool ring, int R, int MC, bool xreg) {
+  return ring ? ring_kernel_for(fmt, R, MC, xreg) : reg_kernel_for(fmt, bytes, R, MC, xreg);
 }
 
 struct OccKey {
@@ -741,11 +126,12 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
   if (g_tune_path == 1 && !use_ring) return fail(B2Q_EINVAL, "gemv: ring path forced but not applicable");
   Plan best{};
   double best_score = -1.0;
-  const int cand[3] = {4, 2, 1};
+  const int cand[4] = {8, 4, 2, 1};
+  const bool xreg = (M == 1) && CPT == 1;
   for (int pass = 0; pass < 2 && best_score < 0; ++pass) {
     const bool ring = use_ring && pass == 0;
     if (pass == 1 && g_tune_path == 1) break;
-    for (int ci = 0; ci < 3; ++ci) {
+    for (int ci = 0; ci < 4; ++ci) {
       const int R = cand[ci];
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
       const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T);
@@ -762,7 +148,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
         smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
       }
       if (smem > (size_t)di.max_smem_optin) continue;
-      KernelFn fn = kernel_for(fmt, bytes, ring, R, MC);
+      KernelFn fn = kernel_for(fmt, bytes, ring, R, MC, xreg);
       const int occ = occupancy(fn, T, smem, di.max_smem_optin);
       if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
       if (occ == 0) continue;
@@ -954,8 +340,8 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
 }
 
 int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
-  if (rows_per_group != 0 && rows_per_group != 1 && rows_per_group != 2 && rows_per_group != 4)
-    return fail(B2Q_EINVAL, "b2q_set_tuning: rows_per_group must be 0, 1, 2 or 4");
+  if (rows_per_group != 0 && rows_per_group != 1 && rows_per_group != 2 && rows_per_group != 4 && rows_per_group != 8)
+    return fail(B2Q_EINVAL, "b2q_set_tuning: rows_per_group must be 0, 1, 2, 4 or 8");
   if (chunks_per_thread < 0 || grid < 0) return fail(B2Q_EINVAL, "b2q_set_tuning: negative value");
   g_tune_rows = rows_per_group;
   g_tune_cpt = chunks_per_thread;
@@ -968,18 +354,6 @@ int b2q_set_pipeline(int path, int stages) {
   if (stages < 0 || stages == 1 || stages > 8) return fail(B2Q_EINVAL, "b2q_set_pipeline: stages must be 0 or 2..8");
   g_tune_path = path;
   g_tune_stages = stages;
-  return B2Q_OK;
-}
-
-int b2q_device_error(int* code, int clear) {
-  if (!code) return fail(B2Q_EINVAL, "b2q_device_error: null pointer");
-  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int));
-  if (e != cudaSuccess) return fail(B2Q_ECUDA, "b2q_device_error: %s", cudaGetErrorString(e));
-  if (clear && *code) {
-    const int zero = 0;
-    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
-    if (e != cudaSuccess) return fail(B2Q_ECUDA, "b2q_device_error: %s", cudaGetErrorString(e));
-  }
   return B2Q_OK;
 }
 
