@@ -266,6 +266,8 @@ def main():
     ap.add_argument("--m", type=int, default=1, help="activation columns")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -293,6 +295,11 @@ def main():
     lib = _lib.load()
     m = args.m
     layers_def = WORKLOADS[args.workload]
+    if args.layers:
+        keep = set(args.layers.split(","))
+        layers_def = [d for d in layers_def if d[3] in keep]
+        if not layers_def:
+            ap.error(f"--layers {args.layers}: no such layer in {args.workload}")
     total_bytes = sum(algo_bytes(f, n, k, m) for f, n, k, _ in layers_def)
     weights_total = sum(weight_bytes(f, n, k) for f, n, k, _ in layers_def)
     copies = max(1, -(-4 * L2_BYTES // max(1, weights_total))) if weights_total < 4 * L2_BYTES else 1
@@ -385,7 +392,7 @@ def main():
     traffic = profiled_traffic(tag)
 
     # ---- end to end through the public API: pinned host x -> device, quantize + gemv, Y -> host ----
-    e2e_steps = args.e2e_steps or args.steps
+    e2e_steps = 0 if args.no_e2e else (args.e2e_steps or args.steps)
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
     sharded = None
     if world > 1:
@@ -405,21 +412,23 @@ def main():
             y_host[i].copy_(y, non_blocking=True)
         stream.synchronize()  # the step's result is read on the host
 
-    for _ in range(3):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    e1.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_gbs = total_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9
+    e2e_gbs = None
+    if e2e_steps:
+        for _ in range(3):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        e1.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_gbs = round(total_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9, 3)
     h2d = sum(L.x_host.numel() * 4 for L in layers)
     d2h = sum(L.n * m * 4 for L in layers)
 
@@ -452,7 +461,7 @@ def main():
                          "kernel": f"gemv {tag} (quant prologue fused)", "peak_source": f"{peak_kind} hbm_gbs",
                          "us_per_launch": round(dom_ms * 1e3, 3), "algorithmic_bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "api": "comp_b200.host.quantize + gemv" if world == 1 else
                     "comp_b200.dist.RowShardedGemv"},
             "gpu_launches": launches,

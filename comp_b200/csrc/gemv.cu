@@ -108,9 +108,6 @@ static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
   return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
 }
 
-// Bytes of weights a CTA keeps in flight; the planner aims at kInflightTarget per SM.
-constexpr double kInflightTarget = 96.0 * 1024;
-
 static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out) {
   DeviceInfo di;
   int rc = device_info(&di);
@@ -140,11 +137,10 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       uint32_t sb = 0;
       size_t smem = xb;
       if (ring) {
+        // Measured on B200 (weight-streaming sweeps over the BASELINE layer shapes): two stages -- one group in
+        // flight while one is computed -- with the most CTAs per SM beats deeper rings at lower occupancy.
         sb = ring_stage_bytes(fmt, K, C, R);
-        // smallest ring with enough bytes in flight for one CTA, at least double-buffered
-        stages = (int)std::min<double>(8.0, std::max(2.0, 1.0 + std::ceil(kInflightTarget / 2 / sb)));
-        if (g_tune_stages > 0) stages = g_tune_stages;
-        while (stages > 2 && (size_t)stages * sb + 16 * (stages + 1) + xb > (size_t)di.max_smem_optin) --stages;
+        stages = g_tune_stages > 0 ? g_tune_stages : 2;
         smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
       }
       if (smem > (size_t)di.max_smem_optin) continue;
@@ -157,11 +153,8 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
       const int64_t per = (groups + grid - 1) / grid;
       const double balance = (double)groups / (double)(per * grid);
-      // memory-level parallelism per SM relative to the target
-      double inflight = ring ? (double)std::min<int64_t>(occ, (grid + di.sms - 1) / di.sms) * (stages - 1) * sb
-                             : (double)std::min<int64_t>(occ, (grid + di.sms - 1) / di.sms) * T * R * 16 * 2;
-      const double mlp = std::min(1.0, inflight / kInflightTarget);
-      const double score = balance * (0.5 + 0.5 * mlp) + 0.002 * R;
+      // larger groups amortize the per-group reduction and barrier (measured: R = 8 fastest when it fits)
+      const double score = balance + 0.02 * std::log2((double)R);
       if (score > best_score) {
         best_score = score;
         best = Plan{R, T, CPT, (int)grid, stages, sb, smem, ring, fn};

@@ -255,7 +255,11 @@ def test_ring_and_register_paths_identical(cuda, fmt, n, k, m):
         for path, rows, stages in ((2, 0, 0), (1, 0, 0), (1, 1, 2), (1, 2, 3), (1, 4, 8), (1, 8, 4), (2, 1, 0), (2, 4, 0), (2, 8, 0)):
             _lib.call("b2q_set_tuning", rows, 0, 0)
             _lib.call("b2q_set_pipeline", path, stages)
-            y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+            try:
+                y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+            except ValueError as e:  # a forced schedule larger than shared memory is refused, not run
+                assert "does not fit" in str(e) or "not applicable" in str(e)
+                continue
             assert np.array_equal(s.cpu().numpy(), os_), (path, rows, stages)
             outs.append(y.cpu().numpy())
             yf = host.quant_gemv(fmt, twq, tws, tx, n, k)
