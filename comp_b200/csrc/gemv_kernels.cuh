@@ -356,30 +356,35 @@ __device__ __forceinline__ void load_xchunk(const GemvParams& p, const uint8_t* 
 }
 
 // One chunk c of R rows (weights w[r], scales dw[r]) against MC columns: block dots, S store, f32 accumulation into
-// acc[r*MC + m]. Columns m >= p.M are skipped (uniformly).
-template <int FMT, int R, int MC, bool BYTES>
+// acc[r*MC + m]. Columns m >= p.M are skipped (uniformly). No predicate guards the accumulation: a chunk past the row
+// end has zero weights, zero activations and zero scales, and rows past N are never stored.
+//   Q4_0 (one block per chunk): acc += f32(s) * dw * dx, the reference's per-block product (kernels.py:93).
+//   TQ2_0 (a block spans 4 chunks on 4 adjacent threads): each thread adds its own chunk's exact partial dot,
+//     acc += (dx * dw) * f32(s_chunk) (the reference's dx * dw * s order, kernels.py:141, applied per quarter block),
+//     so the 4 threads need no exchange; with STORE the exact block dot is assembled with two xor-shuffles for S.
+template <int FMT, int R, int MC, bool BYTES, bool STORE>
 __device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, int c, bool valid, const uint4 (&w)[R],
                                               const float (&dw)[R], const XChunk (&xc)[MC], float (&acc)[R * MC]) {
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   const int blk = c >> Fmt<FMT>::kChunkShift;
-  const bool lead = valid && (FMT == 0 || (c & 3) == 0);
 #pragma unroll
   for (int m = 0; m < MC; ++m) {
     if (MC == 1 || m < p.M) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        int s = chunk_dot<FMT, BYTES>(w[r], xc[m].x, xc[m].sum);
-        if (FMT == 1) {  // a TQ2_0 block spans 4 adjacent threads: exact int32 sum of the 4 partial dots
-          s += __shfl_xor_sync(0xffffffffu, s, 1);
-          s += __shfl_xor_sync(0xffffffffu, s, 2);
-        }
-        const int64_t row = g * R + r;
-        if (lead && row < p.N) {
-          if (p.s) p.s[((int64_t)m * p.N + row) * nblk + blk] = s;
-          if (FMT == 0)
-            acc[r * MC + m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), xc[m].dx, acc[r * MC + m]);
-          else
-            acc[r * MC + m] = __fmaf_rn(__fmul_rn(xc[m].dx, dw[r]), (float)s, acc[r * MC + m]);
+        const int s = chunk_dot<FMT, BYTES>(w[r], xc[m].x, xc[m].sum);
+        if (FMT == 0)
+          acc[r * MC + m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), xc[m].dx, acc[r * MC + m]);
+        else
+          acc[r * MC + m] = __fmaf_rn(__fmul_rn(xc[m].dx, dw[r]), (float)s, acc[r * MC + m]);
+        if (STORE) {
+          int sb = s;
+          if (FMT == 1) {
+            sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+            sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+          }
+          const int64_t row = g * R + r;
+          if (valid && (FMT == 0 || (c & 3) == 0) && row < p.N) p.s[((int64_t)m * p.N + row) * nblk + blk] = sb;
         }
       }
     }
@@ -560,7 +565,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
     for (int r = 0; r < R; ++r) dw[r] = f16_bits_to_f32(cur.sc[r]);
     XChunk xc[MC];
     get_x<FMT, MC, XREG>(p, xs, xsum, xscale, xr, c, valid, xc);
-    compute_chunk<FMT, R, MC, BYTES>(p, g, c, valid, cur.w, dw, xc, acc);
+    if (p.s)
+      compute_chunk<FMT, R, MC, BYTES, true>(p, g, c, valid, cur.w, dw, xc, acc);
+    else
+      compute_chunk<FMT, R, MC, BYTES, false>(p, g, c, valid, cur.w, dw, xc, acc);
     if (in == 0) {
       reduce_store<R, MC>(p, g, acc, red, buf);
       buf ^= 1;
@@ -662,7 +670,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
       }
       XChunk xc[MC];
       get_x<FMT, MC, XREG>(p, xs, xsum, xscale, xr, c, valid, xc);
-      compute_chunk<FMT, R, MC, false>(p, g, c, valid, w, dw, xc, acc);
+      if (p.s)
+        compute_chunk<FMT, R, MC, false, true>(p, g, c, valid, w, dw, xc, acc);
+      else
+        compute_chunk<FMT, R, MC, false, false>(p, g, c, valid, w, dw, xc, acc);
     }
     reduce_store<R, MC>(p, g, acc, red, buf);
     buf ^= 1;
