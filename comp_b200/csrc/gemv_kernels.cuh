@@ -285,26 +285,30 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
   if (!BYTES) {
+    // Signed dp4a only, every weight byte kept below 128: fields at the same power-of-two scale share one
+    // accumulator, and the scale is removed by an exact arithmetic shift at the end.
     if (FMT == 0) {
-      int lo = 0, hi = 0;
+      // low nibbles (values i) and high nibbles shifted down (values 16+i) both at 1x: one accumulator
+      int acc = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t wk = word_of(w, k);
-        lo = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(x[0], k), lo);
-        hi = dp4a_us(wk & 0xF0F0F0F0u, (int)word_of(x[1], k), hi);
+        acc = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(x[0], k), acc);
+        acc = dp4a_ss((int)((wk >> 4) & 0x0F0F0F0Fu), (int)word_of(x[1], k), acc);
       }
-      return lo + (hi >> 4) - xsum;
+      return acc - xsum;
     } else {
-      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+      // crumbs 0 and 1 at 1x (w and w>>2 masked with 0x03), crumbs 2 and 3 at 16x (masked with 0x30)
+      int a01 = 0, a23 = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint32_t wk = word_of(w, k);
-        a0 = dp4a_us(wk & 0x03030303u, (int)word_of(x[0], k), a0);
-        a1 = dp4a_us(wk & 0x0C0C0C0Cu, (int)word_of(x[1], k), a1);
-        a2 = dp4a_us(wk & 0x30303030u, (int)word_of(x[2], k), a2);
-        a3 = dp4a_us(wk & 0xC0C0C0C0u, (int)word_of(x[3], k), a3);
+        const uint32_t wk = word_of(w, k), wh = wk >> 2;
+        a01 = dp4a_ss((int)(wk & 0x03030303u), (int)word_of(x[0], k), a01);
+        a01 = dp4a_ss((int)(wh & 0x03030303u), (int)word_of(x[1], k), a01);
+        a23 = dp4a_ss((int)(wk & 0x30303030u), (int)word_of(x[2], k), a23);
+        a23 = dp4a_ss((int)(wh & 0x30303030u), (int)word_of(x[3], k), a23);
       }
-      return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - xsum;
+      return a01 + (a23 >> 4) - xsum;
     }
   } else {
     // byte-wise variant (the reference's MODE 0): every value unpacked to an int32, no offset correction needed
