@@ -285,6 +285,29 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
   if (!BYTES) {
+#ifdef B2Q_DP4A_MIXED
+    if (FMT == 0) {
+      int lo = 0, hi = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wk = word_of(w, k);
+        lo = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(x[0], k), lo);
+        hi = dp4a_us(wk & 0xF0F0F0F0u, (int)word_of(x[1], k), hi);
+      }
+      return lo + (hi >> 4) - xsum;
+    } else {
+      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wk = word_of(w, k);
+        a0 = dp4a_us(wk & 0x03030303u, (int)word_of(x[0], k), a0);
+        a1 = dp4a_us(wk & 0x0C0C0C0Cu, (int)word_of(x[1], k), a1);
+        a2 = dp4a_us(wk & 0x30303030u, (int)word_of(x[2], k), a2);
+        a3 = dp4a_us(wk & 0xC0C0C0C0u, (int)word_of(x[3], k), a3);
+      }
+      return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - xsum;
+    }
+#else
     // Signed dp4a only, every weight byte kept below 128: fields at the same power-of-two scale share one
     // accumulator, and the scale is removed by an exact arithmetic shift at the end.
     if (FMT == 0) {
@@ -310,6 +333,7 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
       }
       return a01 + (a23 >> 4) - xsum;
     }
+#endif
   } else {
     // byte-wise variant (the reference's MODE 0): every value unpacked to an int32, no offset correction needed
     int s = 0;
@@ -528,7 +552,7 @@ __device__ __forceinline__ void get_x(const GemvParams& p, const uint8_t* xs, co
 
 template <int FMT, int R, int MC, bool BYTES, bool XREG>
 __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   const int M = p.M, C = p.C;
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   uint8_t* xs = smem;                                                    // [M][K] permuted int8
@@ -640,17 +664,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
 #pragma unroll
   for (int k = 0; k < R * MC; ++k) acc[k] = 0.f;
 
+  // Stage bookkeeping without divisions: group j sits in stage j % S with mbarrier phase parity (j / S) & 1; the
+  // producer refills stage (j - 1) % S with group j + S - 1.
   int buf = 0;
+  int s = 0;            // stage of group j
+  uint32_t parity = 0;  // phase parity of group j's stage
   int64_t j = 0;
   for (; j < ngroups; ++j) {
-    const int s = (int)(j % S);
     if (threadIdx.x == 0 && j + S - 1 < ngroups) {
       // stage (j-1)%S was released by the previous group's __syncthreads
-      const int sn = (int)((j + S - 1) % S);
+      const int sn = (s == 0) ? S - 1 : s - 1;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue_group<FMT, R>(p, g_begin + j + S - 1, ring_addr + (uint32_t)sn * p.stage_bytes, bar_addr + 8 * sn, pol);
     }
-    if (!mbar_wait(bar_addr + 8 * s, (uint32_t)((j / S) & 1), kWaitLimit)) {
+    if (!mbar_wait(bar_addr + 8 * s, parity, kWaitLimit)) {
       s_abort = 1;
       atomicCAS(&g_device_error, 0, kErrTimeout);
     }
@@ -681,10 +708,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
     }
     reduce_store<R, MC>(p, g, acc, red, buf);
     buf ^= 1;
+    if (++s == S) {
+      s = 0;
+      parity ^= 1u;
+    }
     if (s_abort) break;  // uniform: read after the reduction's __syncthreads
   }
   if (s_abort) {
-    // drain: wait (bounded) for copies that were issued but not consumed, then leave
+    // drain: wait (bounded) for copies that were issued but not consumed (groups j .. j+S-1), then leave
     if (threadIdx.x == 0) {
       for (int64_t jj = j; jj < min(ngroups, j + S); ++jj)
         mbar_wait(bar_addr + 8 * (uint32_t)(jj % S), (uint32_t)((jj / S) & 1), kWaitLimit);
