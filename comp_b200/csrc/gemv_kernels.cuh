@@ -285,7 +285,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
   if (!BYTES) {
-#ifdef B2Q_DP4A_MIXED
+#ifndef B2Q_DP4A_SIGNED_ONLY
     if (FMT == 0) {
       int lo = 0, hi = 0;
 #pragma unroll
@@ -308,7 +308,7 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
       return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6) - xsum;
     }
 #else
-    // Signed dp4a only, every weight byte kept below 128: fields at the same power-of-two scale share one
+    // Alternative (B2Q_DP4A_SIGNED_ONLY): signed dp4a only, every weight byte kept below 128: fields at the same power-of-two scale share one
     // accumulator, and the scale is removed by an exact arithmetic shift at the end.
     if (FMT == 0) {
       // low nibbles (values i) and high nibbles shifted down (values 16+i) both at 1x: one accumulator
