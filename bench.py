@@ -237,8 +237,10 @@ def run_reference_arm(args, rank):
     step_bytes = sum(algo_bytes(f, r, k, m) for f, r, k in meta)
     sec, threads = cpu_reference_run(layers, args.steps, args.warmup)
     gbs = step_bytes / sec / 1e9
-    sample = (f"first {rows} rows of each layer ({', '.join(f'{f} {r}x{k}' for f, r, k in meta)}), M={m}; "
-              f"quantize + GEMV + f64 reference dot per layer")
+    full_rows = all(r == n for (f, r, k), (_, n, _, _) in zip(meta, full))
+    what = "full layers" if full_rows else f"first {rows} rows of each layer"
+    sample = (f"{what} ({', '.join(f'{f} {r}x{k}' for f, r, k in meta)}), M={m}; quantize + GEMV + f64 reference dot "
+              f"per layer, each step")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3 * full_bytes / step_bytes, 3),
