@@ -270,6 +270,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -288,7 +289,7 @@ def main():
     import torch.distributed as dist
 
     from comp_b200 import _lib, host
-    from comp_b200.dist import partition, slice_rows
+    from comp_b200.dist import RowShardedGemv, partition
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -304,7 +305,9 @@ def main():
             ap.error(f"--layers {args.layers}: no such layer in {args.workload}")
     total_bytes = sum(algo_bytes(f, n, k, m) for f, n, k, _ in layers_def)
     weights_total = sum(weight_bytes(f, n, k) for f, n, k, _ in layers_def)
-    copies = max(1, -(-4 * L2_BYTES // max(1, weights_total))) if weights_total < 4 * L2_BYTES else 1
+    # every step must stream its weights from HBM: keep >= 4x L2 of distinct weights per GPU, rotating copies
+    per_gpu = max(1, weights_total // world)
+    copies = 1 if per_gpu >= 4 * L2_BYTES else -(-4 * L2_BYTES // per_gpu)
 
     class Layer:
         pass
@@ -314,55 +317,66 @@ def main():
         L = Layer()
         L.fmt, L.n, L.k, L.name = fmt, n, k, name
         L.row0, L.rows = partition(n, world)[rank]
-        L.per = slice_rows(n, world)
-        L.w = [make_layer_gpu(fmt, n, k, 100 + i, dev, rows=(L.row0, L.rows)) for _ in range(copies)]
+        L.w = [make_layer_gpu(fmt, n, k, 100 + i + 1000 * c, dev, rows=(L.row0, L.rows)) for c in range(copies)]
         L.x_host = torch.from_numpy(make_x(k, m, 200 + i)).pin_memory()
         L.x = L.x_host.to(dev)
-        L.part = torch.zeros((m, L.per), dtype=torch.float32, device=dev)
-        L.full = torch.empty((world, m, L.per), dtype=torch.float32, device=dev)
+        L.y = torch.empty((m, n), dtype=torch.float32, device=dev)
         L.fid = 0 if fmt == "q4_0" else 1
+        if world > 1:
+            L.objs = [RowShardedGemv(fmt, wq, ws, n, k, exchange=args.exchange) for wq, ws in L.w]
         layers.append(L)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     dominant = max(range(len(layers)), key=lambda i: weight_bytes(layers[i].fmt, layers[i].n, layers[i].k))
+    exchange_name = None if world == 1 else layers[0].objs[0].exchange
 
     def launch(L, c):
+        """N = 1: one fused quantize + GEMV launch straight through the C ABI."""
         wq, ws = L.w[c]
-        if L.rows == 0:
-            return
-        # M == 1: the slice buffer row is contiguous, so the kernel writes straight into it
-        y = L.part if m == 1 else torch.empty((m, L.rows), dtype=torch.float32, device=dev)
         rc = lib.b2q_quant_gemv(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x.data_ptr(), L.x.stride(0),
-                                None, None, y.data_ptr(), L.rows, L.k, m, sptr)
+                                None, None, L.y.data_ptr(), L.rows, L.k, m, sptr)
         if rc != 0:
             raise RuntimeError(_lib.last_error())
-        if m != 1:
-            L.part[:, : L.rows].copy_(y)
-
-    def exchange(L):
-        if world > 1:
-            dist.all_gather_into_tensor(L.full, L.part)
 
     def step(c, ev=None):
         for i, L in enumerate(layers):
             if ev is not None and i == dominant:
                 ev[0].record(stream)
+            if world == 1:
                 launch(L, c)
-                ev[1].record(stream)
             else:
-                launch(L, c)
-            exchange(L)
+                L.objs[c](L.x)
+            if ev is not None and i == dominant:
+                ev[1].record(stream)
 
     for w in range(args.warmup):
         step(w % copies)
     torch.cuda.synchronize()
+
+    # N > 1: the step is captured once per weight copy as a CUDA graph (three fused GEMV + all-gather launches, or
+    # GEMV + NCCL all-gather), so host launch time does not bound the multi-GPU step
+    graphs = []
+    launches_per_graph = 0
     if world > 1:
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            n0 = _lib.launch_count()
+            with torch.cuda.stream(cs), torch.cuda.graph(g, stream=cs):
+                step(c)
+            launches_per_graph = _lib.launch_count() - n0
+            graphs.append(g)
+        stream.wait_stream(cs)
+        for c in range(copies):
+            graphs[c].replay()
+        torch.cuda.synchronize()
         dist.barrier()
 
     # ---- device-timed region: inputs resident in HBM ----
     dom_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
+                  for _ in range(args.steps if world == 1 else 0)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _lib.launch_count()
     with ClockSampler(dev) as clocks:
@@ -371,13 +385,16 @@ def main():
             dist.barrier()
         start.record(stream)
         for s in range(args.steps):
-            step(s % copies, dom_events[s])
+            if world == 1:
+                step(s % copies, dom_events[s])
+            else:
+                graphs[s % copies].replay()
         end.record(stream)
         end.synchronize()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    launches = _lib.launch_count() - launches0
+    launches = _lib.launch_count() - launches0 if world == 1 else launches_per_graph * args.steps
     ms = start.elapsed_time(end)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -386,7 +403,40 @@ def main():
     sec = ms / 1e3
     value = total_bytes * args.steps / sec / 1e9
     dom = layers[dominant]
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_events)
+    if world == 1:
+        dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_events)
+        dom_note = "mean CUDA-event duration of its launches inside the timed steps"
+    else:
+        # the dominant layer alone (its fused GEMV + all-gather), graph-replayed, event-timed on its stream
+        dg = []
+        cs2 = torch.cuda.Stream(dev)
+        cs2.wait_stream(stream)
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cs2), torch.cuda.graph(g, stream=cs2):
+                dom.objs[c](dom.x)
+            dg.append(g)
+        stream.wait_stream(cs2)
+        reps = max(20, min(400, args.steps))
+        for r in range(4):
+            dg[r % copies].replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for r in range(reps):
+            dg[r % copies].replay()
+        d1.record(stream)
+        d1.synchronize()
+        td = torch.tensor([d0.elapsed_time(d1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(td, op=dist.ReduceOp.MAX)
+        dom_ms = float(td.item())
+        dom_note = f"dominant layer alone, {reps} graph replays after the timed steps, max over ranks"
+        del dg
+        for L in layers:
+            for o in L.objs:
+                if o.status_code() != 0:
+                    raise RuntimeError(f"rank {rank}: all-gather barrier timed out ({o.status_code()})")
     dom_bytes = algo_bytes(dom.fmt, dom.rows, dom.k, m)
     peak, peak_kind = peaks()
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
@@ -396,21 +446,16 @@ def main():
     # ---- end to end through the public API: pinned host x -> device, quantize + gemv, Y -> host ----
     e2e_steps = 0 if args.no_e2e else (args.e2e_steps or args.steps)
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
-    sharded = None
-    if world > 1:
-        from comp_b200.dist import RowShardedGemv
-
-        sharded = [RowShardedGemv(L.fmt, L.w[0][0], L.w[0][1], L.n, L.k) for L in layers]
 
     def e2e_step():
         for i, L in enumerate(layers):
             x = L.x_host.to(dev, non_blocking=True)
-            if sharded is None:
+            if world == 1:
                 wq, ws = L.w[0]
                 xq, xd = host.quantize(L.fmt, x)
                 y, _ = host.gemv(L.fmt, wq, ws, xq, xd, L.n, L.k, mode=2)
             else:
-                y = sharded[i](x)
+                y = L.objs[0](x)
             y_host[i].copy_(y, non_blocking=True)
         stream.synchronize()  # the step's result is read on the host
 
@@ -433,6 +478,12 @@ def main():
         e2e_gbs = round(total_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9, 3)
     h2d = sum(L.x_host.numel() * 4 for L in layers)
     d2h = sum(L.n * m * 4 for L in layers)
+    del graphs
+    torch.cuda.synchronize()
+    if world > 1:
+        for L in layers:
+            for o in L.objs:
+                o.close()
 
     # ---- CPU baseline (rank 0, N = 1): bounded sample of the same workload ----
     cpu = None
@@ -454,18 +505,22 @@ def main():
             "data": "synthetic (BASELINE distributions, seeded, random-init weights)",
             "config": {"workload": args.workload, "layers": [f"{f} {n}x{k} ({nm})" for f, n, k, nm in layers_def],
                        "m": m, "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
-                       "exchange": "nccl all_gather_into_tensor" if world > 1 else None,
-                       "l2": f"weights {weights_total / 2**20:.0f} MiB x {copies} copies > L2 (no flush needed)"},
+                       "exchange": {None: None, "p2p": "fused P2P stores + flag barrier in the GEMV kernel",
+                                    "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
+                       "graph": world > 1,
+                       "l2": f"weights {per_gpu / 2**20:.0f} MiB per GPU x {copies} rotating copies >= 4x L2 "
+                             f"(no flush needed)"},
             "us_per_gemv": round(ms * 1e3 / args.steps / len(layers), 3),
             "hbm_frac": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"gemv {tag} (quant prologue fused)", "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": f"gemv {tag} (quant prologue fused{', all-gather fused' if world > 1 else ''})",
+                         "timing": dom_note, "peak_source": f"{peak_kind} hbm_gbs",
                          "us_per_launch": round(dom_ms * 1e3, 3), "algorithmic_bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "api": "comp_b200.host.quantize + gemv" if world == 1 else
-                    "comp_b200.dist.RowShardedGemv"},
+                    f"comp_b200.dist.RowShardedGemv ({exchange_name})"},
             "gpu_launches": launches,
             "clocks": cs,
         }

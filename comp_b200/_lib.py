@@ -27,12 +27,12 @@ SIGNATURES = {
     "b2q_gemv_q4_0": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
     "b2q_gemv_tq2_0": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
     "b2q_quant_gemv": (INT, [INT, P, I64, P, P, I64, P, P, P, I64, I64, I64, P]),
-    "b2q_gemv_allgather": (INT, [INT, P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, INT, ctypes.c_uint32,
+    "b2q_gemv_allgather": (INT, [INT, P, I64, P, P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, INT, INT,
                                  ctypes.c_longlong, P]),
     "b2q_set_tuning": (INT, [INT, INT, INT]),
     "b2q_set_pipeline": (INT, [INT, INT]),
     "b2q_device_error": (INT, [ctypes.POINTER(ctypes.c_int), INT]),
-    "b2q_ipc_get_handle": (INT, [P, P]),
+    "b2q_ipc_get_handle": (INT, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
     "b2q_ipc_open_handle": (INT, [P, ctypes.POINTER(ctypes.c_void_p)]),
     "b2q_ipc_close_handle": (INT, [P]),
     "b2q_probe_dp4a": (INT, [P, P, P, P, I64, P]),

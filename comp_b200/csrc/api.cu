@@ -64,13 +64,30 @@ int b2q_last_error(char* buf, size_t len) {
 
 long long b2q_launch_count(void) { return b2q::g_launches.load(std::memory_order_relaxed); }
 
-int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64) {
-  if (!dev_ptr || !handle_out64) return b2q::fail(B2Q_EINVAL, "b2q_ipc_get_handle: null pointer");
+// cuMemGetAddressRange through the runtime's driver entry-point lookup (no link-time dependency on libcuda).
+typedef int (*MemGetAddressRangeFn)(unsigned long long* base, size_t* size, unsigned long long ptr);
+
+int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64, uint64_t* offset_out) {
+  if (!dev_ptr || !handle_out64 || !offset_out) return b2q::fail(B2Q_EINVAL, "b2q_ipc_get_handle: null pointer");
+  static MemGetAddressRangeFn range_fn = nullptr;
+  if (!range_fn) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return b2q::fail(B2Q_ECUDA, "b2q_ipc_get_handle: cuMemGetAddressRange not available");
+    range_fn = reinterpret_cast<MemGetAddressRangeFn>(fn);
+  }
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<unsigned long long>(dev_ptr)) != 0)
+    return b2q::fail(B2Q_ECUDA, "b2q_ipc_get_handle: cuMemGetAddressRange failed");
   cudaIpcMemHandle_t h;
-  cudaError_t e = cudaIpcGetMemHandle(&h, dev_ptr);
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
   if (e != cudaSuccess) return b2q::fail(B2Q_ECUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
   static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
   memcpy(handle_out64, &h, 64);
+  *offset_out = reinterpret_cast<unsigned long long>(dev_ptr) - base;
   return B2Q_OK;
 }
 

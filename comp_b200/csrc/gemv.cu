@@ -208,10 +208,10 @@ struct LaunchArgs {
   int64_t row0;
   int32_t* s;
   float* const* y_peers;
+  uint32_t* flags;
   uint32_t* const* flags_peers;
   int32_t* status;
   int rank, nranks;
-  uint32_t epoch;
   long long spin_limit;
   int64_t N, K, M;
 };
@@ -250,11 +250,11 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.row0 = a.row0;
     p.s = a.s ? a.s + m0 * a.N * nblk : nullptr;
     p.y_peers = a.y_peers;  // the exchange path is limited to one column group (M <= kMaxColumns) by its entry point
+    p.flags = a.flags;
     p.flags_peers = a.flags_peers;
     p.status = a.status;
     p.rank = a.rank;
     p.nranks = a.nranks;
-    p.epoch = a.epoch;
     p.spin_limit = a.spin_limit;
     p.N = a.N;
     p.K = a.K;
@@ -323,14 +323,31 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
   return launch_gemv(a, (cudaStream_t)stream);
 }
 
-int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq,
-                       const float* xd, float* const* y_peers, uint32_t* const* flags_peers, int32_t* status,
-                       int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M, int rank, int nranks,
-                       uint32_t epoch, long long spin_limit, b2q_stream_t stream) {
-  (void)fmt, (void)wq, (void)ldwq, (void)ws, (void)xq, (void)xd, (void)y_peers, (void)flags_peers, (void)status;
-  (void)row0, (void)n_local, (void)N_total, (void)K, (void)M, (void)rank, (void)nranks, (void)epoch;
-  (void)spin_limit, (void)stream;
-  return fail(B2Q_EINVAL, "b2q_gemv_allgather: not enabled in this build");
+int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                       float* y, float* const* y_peers, uint32_t* flags, uint32_t* const* flags_peers,
+                       int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
+                       int rank, int nranks, long long spin_limit, b2q_stream_t stream) {
+  const char* who = "b2q_gemv_allgather";
+  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0) or TQ2_0 (1)", who, fmt);
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(B2Q_EINVAL, "%s: rank %d of %d", who, rank, nranks);
+  if (M < 1 || M > kMaxColumns) return fail(B2Q_ERANGE, "%s: M=%lld, 1..%d supported", who, (long long)M, kMaxColumns);
+  if (K < 1 || n_local < 1 || row0 < 0 || row0 + n_local > N_total)
+    return fail(B2Q_EINVAL, "%s: rows [%lld, %lld) not inside [0, %lld), or K=%lld", who, (long long)row0,
+                (long long)(row0 + n_local), (long long)N_total, (long long)K);
+  if (!y || !y_peers || !flags || !flags_peers || !status) return fail(B2Q_EINVAL, "%s: null pointer", who);
+  if (spin_limit < 1) return fail(B2Q_EINVAL, "%s: spin_limit must be positive", who);
+  int rc = check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, n_local, K, M, true);
+  if (rc) return rc;
+  if (ldx < K || (ldx % 4)) return fail(B2Q_EALIGN, "%s: ldx must be >= K and a multiple of 4", who);
+  if (!aligned(flags, 4) || !aligned(status, 4)) return fail(B2Q_EALIGN, "%s: flags/status must be 4-byte aligned", who);
+  LaunchArgs a{};
+  a.fmt = fmt;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx;
+  a.y = y, a.ldy = N_total, a.row0 = row0;
+  a.y_peers = y_peers, a.flags = flags, a.flags_peers = flags_peers, a.status = status;
+  a.rank = rank, a.nranks = nranks, a.spin_limit = spin_limit;
+  a.N = n_local, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
 }
 
 int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {

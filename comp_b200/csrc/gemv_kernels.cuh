@@ -59,10 +59,10 @@ struct GemvParams {
   int32_t* s;             // [M][N][nblk] int32 block dots (nullable)
   // fused all-gather epilogue (multi-GPU): y is this rank's copy; every CTA also copies its rows to the peers
   float* const* y_peers;  // device array [nranks] or null
+  uint32_t* flags;        // this rank's flag array [nranks + 2] (peer epochs, CTA arrival counter, own epoch)
   uint32_t* const* flags_peers;  // device array [nranks] of flag arrays (each [nranks + 1] uint32) or null
   int32_t* status;
   int rank, nranks;
-  uint32_t epoch;
   long long spin_limit;
   int64_t N;              // rows in this launch
   int64_t K;
@@ -132,7 +132,8 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return pol;
 }
 
-// Global -> shared bulk copy (no multicast), completion counted in bytes on `bar`. dst, src, bytes: multiples of 16.
+// Global -> shared bulk copy into this CTA's own shared memory, completion counted in bytes on `bar`; dst, src and
+// bytes are multiples of 16. The source is always this GPU's own memory (local weights).
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
@@ -481,14 +482,16 @@ __device__ __forceinline__ void allgather_epilogue(const GemvParams& p, int64_t 
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    uint32_t* own = p.flags_peers[p.rank];
+    // flags: [0, nranks) latest epoch seen from each rank, [nranks] CTA arrival counter, [nranks+1] own epoch
+    uint32_t* own = p.flags;
     const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
     if (arrived == gridDim.x - 1) {
       own[p.nranks] = 0u;  // reset the arrival counter for the next call
+      const uint32_t epoch = own[p.nranks + 1] + 1u;
       __threadfence_system();
       for (int q = 0; q < p.nranks; ++q) {
         uint32_t* f = p.flags_peers[q] + p.rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.epoch) : "memory");
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
       }
       int err = 0;
       for (int q = 0; q < p.nranks && !err; ++q) {
@@ -496,7 +499,7 @@ __device__ __forceinline__ void allgather_epilogue(const GemvParams& p, int64_t 
         uint32_t v;
         for (;;) {
           asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
-          if ((int32_t)(v - p.epoch) >= 0) break;
+          if ((int32_t)(v - epoch) >= 0) break;
           if (++spins > p.spin_limit) {
             err = 1 + q;
             break;
@@ -504,11 +507,11 @@ __device__ __forceinline__ void allgather_epilogue(const GemvParams& p, int64_t 
           __nanosleep(64);
         }
       }
+      own[p.nranks + 1] = epoch;
       if (err && p.status) *p.status = err;
     }
   }
 }
-
 
 // ------------------------------------------------------------------------------------------------------------------
 // Register path: weights streamed straight into registers, double-buffered one unit (group, chunk round) ahead.

@@ -4,27 +4,33 @@ The reference has no multi-GPU path. Output rows are independent (src/komp/kerne
 are partitioned across ranks: rank r holds rows [row0_r, row0_r + rows_r) of WQ/WS, resident in its HBM. Every rank
 holds the same f32 activations (the decode hidden state is replicated) and quantizes them locally -- quantization is
 deterministic, so every rank gets the same q8 bytes and no activation broadcast is needed. After the local GEMV the
-output slices are all-gathered so every rank holds the full Y [M][N], ready to be the next layer's input.
+output slices are all-gathered so every rank holds the full Y [M][N], ready to be the next layer's input. A row's
+result does not depend on which rank computes it: the sharded Y is bit-identical to the single-GPU Y.
 
 Exchange paths:
-  "nccl"  torch.distributed.all_gather_into_tensor of equal-size padded slices (NCCL over NVLink/NVSwitch).
-  "p2p"   fused in the GEMV kernel: each CTA stores its output rows straight into every peer's Y (CUDA IPC
-          mappings over NVLink), and the last CTA runs a flag barrier with bounded waits (b2q_gemv_allgather).
+  "p2p"   fused into the GEMV kernel (b2q_gemv_allgather): each CTA stores its rows straight into every peer's Y
+          through CUDA IPC mappings over NVLink, and the last CTA runs a flag barrier with bounded waits. One launch
+          per layer, graph-capturable. Y is double-buffered: the tensor returned by call t stays valid until this
+          rank issues call t+2 (consume it before then, e.g. as the next layer's input).
+  "nccl"  host.quant_gemv, then torch.distributed.all_gather_into_tensor of equal-size padded slices.
 """
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
-from . import host
+from . import _lib, host
+
+SPIN_LIMIT = 1 << 24  # flag polls per peer (with a 64 ns back-off) before the barrier reports a timeout
 
 
 def partition(n, nranks, align=4):
-    """[(row0, rows)] per rank: equal slices of ceil(n / nranks) rows rounded up to `align`, the last one shorter
-    (possibly empty). Slice starts are multiples of `align`."""
+    """[(row0, rows)] per rank: equal slices of ceil(n / nranks) rows rounded up to `align`, the last ones shorter
+    (possibly empty). Non-empty slices start at rank * slice_rows(n, nranks)."""
     if nranks < 1:
         raise ValueError("nranks must be >= 1")
-    per = -(-n // nranks)
-    per = -(-per // align) * align
+    per = slice_rows(n, nranks, align)
     out = []
     for r in range(nranks):
         a = min(n, r * per)
@@ -39,17 +45,55 @@ def slice_rows(n, nranks, align=4):
     return -(-per // align) * align
 
 
+def assemble(gathered, world, m, per, n):
+    """[world*m][per] slices as all-gathered (rank-major) -> Y [m][n]."""
+    return gathered.view(world, m, per).permute(1, 0, 2).reshape(m, world * per)[:, :n]
+
+
+class _PeerMapped:
+    """A device buffer of this rank plus the peer-mapped pointers of the same buffer on every rank (CUDA IPC)."""
+
+    def __init__(self, t, group):
+        lib = _lib.load()
+        self.t = t
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _lib.call("b2q_ipc_get_handle", t.data_ptr(), handle, ctypes.byref(off))
+        mine = (bytes(handle.raw), int(off.value))
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        allh = [None] * world
+        dist.all_gather_object(allh, mine, group=group)
+        self.ptrs, self.opened = [], []
+        for q, (h, o) in enumerate(allh):
+            if q == rank:
+                self.ptrs.append(t.data_ptr())
+                continue
+            base = ctypes.c_void_p()
+            rc = lib.b2q_ipc_open_handle(ctypes.create_string_buffer(h, 64), ctypes.byref(base))
+            if rc != 0:
+                raise _lib.B2QError(rc, _lib.last_error())
+            self.opened.append(base.value)
+            self.ptrs.append(base.value + o)
+
+    def close(self):
+        for b in self.opened:
+            _lib.load().b2q_ipc_close_handle(b)
+        self.opened = []
+
+
 class RowShardedGemv:
     """One quantized layer, row-sharded over `group` (default: the world group).
 
-    wq/ws: this rank's rows of the split planes (CUDA tensors), n/k: the full layer's shape.
-    __call__(x f32 [M][K]) -> Y f32 [M][N] (the full output, on every rank).
+    wq/ws: this rank's rows of the split planes (CUDA tensors; rows given by partition(n, world)[rank]), n/k: the
+    full layer's shape. __call__(x f32 [M][K], M <= 4 for "p2p") -> Y f32 [M][N], the full output, on every rank.
+    Every rank must make the same calls in the same order.
     """
 
-    def __init__(self, fmt, wq, ws, n, k, group=None, exchange="nccl"):
-        if exchange not in ("nccl",):
-            raise ValueError(f"exchange {exchange!r} is not available (expected 'nccl')")
-        self.fmt, self.n, self.k, self.group, self.exchange = fmt, n, k, group, exchange
+    def __init__(self, fmt, wq, ws, n, k, group=None, exchange="p2p", max_m=4):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange {exchange!r}: expected 'p2p' or 'nccl'")
+        self.fmt, self.n, self.k, self.group, self.max_m = fmt, n, k, group, max_m
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.row0, self.rows = partition(n, self.world)[self.rank]
@@ -58,17 +102,75 @@ class RowShardedGemv:
                              f"{wq.shape[0]}/{ws.shape[0]}")
         self.wq, self.ws = wq, ws
         self.per = slice_rows(n, self.world)
+        self.dev = wq.device
+        # the fused exchange needs every rank to own rows (it runs the barrier); tiny layers use NCCL
+        if exchange == "p2p" and (self.world == 1 or any(r == 0 for _, r in partition(n, self.world))):
+            exchange = "nccl"
+        self.exchange = exchange
+        self._calls = 0
+        if exchange == "p2p":
+            self._init_p2p()
 
+    # ---- fused P2P exchange ----
+    def _init_p2p(self):
+        dev = self.dev
+        with torch.cuda.device(dev):
+            self.y = torch.zeros((2, self.max_m, self.n), dtype=torch.float32, device=dev)  # double-buffered
+            self.flags = torch.zeros(self.world + 2, dtype=torch.int32, device=dev)
+            self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+            torch.cuda.synchronize(dev)
+            self._ymap = _PeerMapped(self.y, self.group)
+            self._fmap = _PeerMapped(self.flags, self.group)
+            nbuf = self.max_m * self.n * 4
+            self._ypeers = [torch.tensor([p + b * nbuf for p in self._ymap.ptrs], dtype=torch.int64, device=dev)
+                            for b in range(2)]
+            self._fpeers = torch.tensor(self._fmap.ptrs, dtype=torch.int64, device=dev)
+        dist.barrier(group=self.group)
+
+    def _p2p(self, x):
+        m = x.shape[0]
+        if m > self.max_m:
+            raise ValueError(f"p2p exchange: M={m} > max_m={self.max_m}")
+        b = self._calls & 1
+        self._calls += 1
+        y = self.y[b]
+        with torch.cuda.device(self.dev):
+            _lib.call("b2q_gemv_allgather", host.FMT_ID[self.fmt], self.wq.data_ptr(), self.wq.stride(0),
+                      self.ws.data_ptr(), x.data_ptr(), x.stride(0), y.data_ptr(), self._ypeers[b].data_ptr(),
+                      self.flags.data_ptr(), self._fpeers.data_ptr(), self.status.data_ptr(), self.row0, self.rows,
+                      self.n, self.k, m, self.rank, self.world, SPIN_LIMIT,
+                      torch.cuda.current_stream(self.dev).cuda_stream)
+        return y[:m]
+
+    def status_code(self):
+        """0, or 1 + the rank a flag barrier timed out waiting for (synchronizes)."""
+        return int(self.status.item()) if self.exchange == "p2p" else 0
+
+    # ---- NCCL exchange ----
     def local(self, x):
         """This rank's output slice [M][rows] (no exchange)."""
         return host.quant_gemv(self.fmt, self.wq, self.ws, x, self.rows, self.k)
 
-    def __call__(self, x):
+    def _nccl(self, x):
         m = x.shape[0]
-        dev = x.device
-        part = torch.zeros((m, self.per), dtype=torch.float32, device=dev)
+        part = torch.zeros((m, self.per), dtype=torch.float32, device=x.device)
         if self.rows:
             part[:, : self.rows] = self.local(x)
-        gathered = torch.empty((self.world, m, self.per), dtype=torch.float32, device=dev)
+        gathered = torch.empty((self.world * m, self.per), dtype=torch.float32, device=x.device)
         dist.all_gather_into_tensor(gathered, part, group=self.group)
-        return gathered.permute(1, 0, 2).reshape(m, self.world * self.per)[:, : self.n]
+        return assemble(gathered, self.world, m, self.per, self.n)
+
+    def __call__(self, x):
+        if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.k:
+            raise ValueError(f"x must be float32 [M][{self.k}], got {x.dtype} {tuple(x.shape)}")
+        x = host._rows_aligned(x)
+        return self._p2p(x) if self.exchange == "p2p" else self._nccl(x)
+
+    def close(self):
+        """Unmaps the peers' buffers (collective: every rank calls it, after its last use of the layer)."""
+        if self.exchange == "p2p" and getattr(self, "_ymap", None) is not None:
+            torch.cuda.synchronize(self.dev)
+            dist.barrier(group=self.group)
+            self._ymap.close()
+            self._fmap.close()
+            self._ymap = self._fmap = None

@@ -109,19 +109,26 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream);
 
 /*
- * Row-sharded GEMV with the output all-gather fused into the epilogue (multi-GPU, one process per GPU).
- * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows.
- * Every output value is stored to y_peers[p] + m*N_total + row0 + r for every rank p (P2P stores over NVLink),
- * then the ranks meet at a flag barrier: rank r writes `epoch` into flags_peers[p][r] for every p and waits,
- * for at most `spin_limit` polls per peer, until its own flags[q] >= epoch for every q.
- * y_peers / flags_peers are device arrays (length nranks) of peer-mapped pointers (CUDA IPC), flags are uint32.
- * Returns B2Q_ETIMEOUT if a peer never arrived (the device writes a nonzero code to *status, a device int32).
- * No reference counterpart (the reference has no multi-GPU path); replaces an NCCL all-gather after host.gemv.
+ * Row-sharded GEMV with the output all-gather fused into the kernel (multi-GPU, one process per GPU).
+ * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows. The kernel
+ * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows, stores
+ * them into its own full output y [M][N_total] and, with plain peer stores over NVLink, into every other rank's
+ * full output (y_peers[q], the peer-mapped base of rank q's y). The last CTA to finish then runs a flag barrier:
+ * with e = flags[nranks+1] + 1 it writes e into flags_peers[q][rank] of every rank q (system-scope release), waits
+ * for at most spin_limit polls per rank until every flags[q] of its own >= e (acquire), and stores e back into
+ * flags[nranks+1]. When the kernel completes, y holds every rank's rows. The epoch lives in device memory, so the
+ * launch can be captured in a CUDA graph and replayed. On a timeout the last CTA writes 1 + (the rank it waited for)
+ * to *status (device int32) and the output must be treated as invalid; the call itself returns B2Q_OK once launched.
+ *   flags:  this rank's uint32 [nranks + 2], zeroed once before the first call (slot nranks: CTA arrival counter,
+ *           reset by the kernel; slot nranks+1: this rank's epoch); flags_peers: device array [nranks] of
+ *           peer-mapped flag arrays (flags_peers[rank] == flags).
+ *   Every rank must make the same sequence of calls. M <= 4.
+ * No reference counterpart (the reference has no multi-GPU path); replaces host.gemv + an NCCL all-gather.
  */
-int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq,
-                       const float* xd, float* const* y_peers, uint32_t* const* flags_peers, int32_t* status,
-                       int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M, int rank, int nranks,
-                       uint32_t epoch, long long spin_limit, b2q_stream_t stream);
+int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                       float* y, float* const* y_peers, uint32_t* flags, uint32_t* const* flags_peers,
+                       int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
+                       int rank, int nranks, long long spin_limit, b2q_stream_t stream);
 
 /* Benchmark/tuning hook (process-wide): force rows per group (1, 2, 4), chunks per thread and grid size of the
  * GEMV schedule; 0 restores the planner's choice. Results do not depend on it (except the f32 summation order). */
@@ -135,8 +142,10 @@ int b2q_set_pipeline(int path, int stages);
  * mbarrier gave up (the kernel then returned early; its outputs are invalid). Synchronizes with the device. */
 int b2q_device_error(int* code, int clear);
 
-/* CUDA IPC helpers for the multi-GPU path: export a device allocation as a 64-byte handle, open a peer's handle. */
-int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64);
+/* CUDA IPC helpers for the multi-GPU path. b2q_ipc_get_handle exports the allocation containing dev_ptr as a 64-byte
+ * handle and returns dev_ptr's byte offset inside it; b2q_ipc_open_handle maps a peer's allocation (with peer access
+ * enabled) and returns its base, to which the peer's offset is added; b2q_ipc_close_handle unmaps that base. */
+int b2q_ipc_get_handle(void* dev_ptr, void* handle_out64, uint64_t* offset_out);
 int b2q_ipc_open_handle(const void* handle64, void** dev_ptr_out);
 int b2q_ipc_close_handle(void* dev_ptr);
 

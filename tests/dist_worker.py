@@ -1,0 +1,81 @@
+"""Worker for tests/test_gpu_dist.py (run by torch.distributed.run, one process per GPU): row-sharded GEMVs with the
+fused P2P all-gather and with NCCL, checked bit-for-bit against the unsharded GEMV of the same layer on this GPU,
+over repeated calls and CUDA-graph replays. Prints one line `RESULT <rank> ok|FAIL <details>`."""
+
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from comp_b200 import host  # noqa: E402
+from comp_b200.dist import RowShardedGemv, partition  # noqa: E402
+
+
+def layer(fmt, n, k, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    nb = k // (32 if fmt == "q4_0" else 256)
+    if fmt == "q4_0":
+        wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    else:
+        t = torch.randint(0, 81, (n, k // 4), dtype=torch.uint8, device=dev, generator=g)
+        wq = (t % 3) | (((t // 3) % 3) << 2) | (((t // 9) % 3) << 4) | (((t // 27) % 3) << 6)
+    ws = (torch.randn((n, nb), device=dev, generator=g) * 0.03).abs().half().view(torch.int16)
+    return wq.contiguous(), ws.contiguous()
+
+
+def main():
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
+    fails = []
+    cases = [("q4_0", 4100, 4096, 1), ("tq2_0", 8192, 8192, 3), ("q4_0", 1000, 14336, 2), ("tq2_0", 64 * world, 2048, 1)]
+    for ci, (fmt, n, k, m) in enumerate(cases):
+        wq, ws = layer(fmt, n, k, dev, 100 + ci)
+        g = torch.Generator(device=dev)
+        g.manual_seed(200 + ci)
+        x = torch.randn((m, k), device=dev, generator=g)
+        want = host.quant_gemv(fmt, wq, ws, x, n, k)
+        row0, rows = partition(n, world)[rank]
+        shard = (wq[row0 : row0 + rows].contiguous(), ws[row0 : row0 + rows].contiguous())
+        for exchange in ("p2p", "nccl"):
+            L = RowShardedGemv(fmt, *shard, n, k, exchange=exchange)
+            for t in range(3):
+                y = L(x).clone()
+                if not torch.equal(y.view(torch.int32), want.view(torch.int32)):
+                    fails.append(f"{fmt} {n}x{k} m={m} {exchange} call {t}: max diff {(y - want).abs().max().item()}")
+            if L.exchange == "p2p":
+                # capture two calls (both output buffers) in a graph and replay it
+                s = torch.cuda.Stream(dev)
+                s.wait_stream(torch.cuda.current_stream(dev))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(s):
+                    with torch.cuda.graph(graph, stream=s):
+                        ya = L(x)
+                        yb = L(x)
+                torch.cuda.current_stream(dev).wait_stream(s)
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize(dev)
+                for name, yy in (("graph a", ya), ("graph b", yb)):
+                    if not torch.equal(yy.view(torch.int32), want.view(torch.int32)):
+                        fails.append(f"{fmt} {n}x{k} {name}: mismatch")
+                del graph
+                if L.status_code() != 0:
+                    fails.append(f"{fmt} {n}x{k} barrier status {L.status_code()}")
+            L.close()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    print(f"RESULT {rank} {'ok' if not fails else 'FAIL ' + '; '.join(fails)}", flush=True)
+    dist.destroy_process_group()
+    sys.exit(1 if fails else 0)
+
+
+if __name__ == "__main__":
+    main()

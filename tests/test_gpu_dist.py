@@ -1,0 +1,33 @@
+"""Row-sharded GEMV on 2+ GPUs of one box (one process per GPU through torch.distributed.run): the fused P2P
+all-gather and the NCCL exchange both reproduce the unsharded output bit for bit (tests/dist_worker.py)."""
+
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_row_sharded_gemv_matches_single_gpu_on_2_gpus():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "dist_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT")]
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert len(lines) == 2 and all(ln.endswith(" ok") for ln in lines), lines

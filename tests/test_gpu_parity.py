@@ -273,3 +273,30 @@ def test_ring_and_register_paths_identical(cuda, fmt, n, k, m):
     code = ctypes.c_int(-1)
     _lib.call("b2q_device_error", ctypes.byref(code), 1)
     assert code.value == 0
+
+
+def test_allgather_barrier_times_out_and_reports(cuda):
+    """The fused all-gather's flag barrier is bounded: with a 'peer' that never runs (its flag is never set), the
+    kernel gives up after spin_limit polls, reports 1 + that rank in the status word, and the context stays usable.
+    Everything lives on this GPU: the peer's Y and flags are plain local buffers, so no GPU waits on another."""
+    n_total, k, rows = 64, 512, 32
+    wq, ws, x, twq, tws, tx = _layer("q4_0", rows, k, 1, 21, cuda)
+    y = torch.zeros((1, n_total), device=cuda)
+    y_peer = torch.zeros((1, n_total), device=cuda)
+    flags = torch.zeros(4, dtype=torch.int32, device=cuda)
+    flags_peer = torch.zeros(4, dtype=torch.int32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ypeers = torch.tensor([y.data_ptr(), y_peer.data_ptr()], dtype=torch.int64, device=cuda)
+    fpeers = torch.tensor([flags.data_ptr(), flags_peer.data_ptr()], dtype=torch.int64, device=cuda)
+    _lib.call("b2q_gemv_allgather", 0, twq.data_ptr(), twq.stride(0), tws.data_ptr(), tx.data_ptr(), k, y.data_ptr(),
+              ypeers.data_ptr(), flags.data_ptr(), fpeers.data_ptr(), status.data_ptr(), 0, rows, n_total, k, 1, 0, 2,
+              2000, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 2                      # waited for rank 1, which never arrived
+    want = host.quant_gemv("q4_0", twq, tws, tx, rows, k).cpu().numpy()
+    assert _same_f32(y[:, :rows].cpu().numpy(), want)    # own rows computed
+    assert _same_f32(y_peer[:, :rows].cpu().numpy(), want)  # and stored into the 'peer' copy
+    f, fp = flags.cpu().tolist(), flags_peer.cpu().tolist()
+    assert fp[0] == 1 and f[0] == 1 and f[2] == 0 and f[3] == 1  # signalled, arrival counter reset, epoch 1 kept
+    # the context is still usable
+    assert _same_f32(host.quant_gemv("q4_0", twq, tws, tx, rows, k).cpu().numpy(), want)
