@@ -271,6 +271,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
+    ap.add_argument("--pdl", default="on", choices=["on", "off"], help="programmatic dependent launch of the GEMVs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -296,6 +297,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lib = _lib.load()
+    if args.pdl == "off":
+        _lib.call("b2q_set_pipeline", 4, 0)
     m = args.m
     layers_def = WORKLOADS[args.workload]
     if args.layers:
@@ -362,12 +365,11 @@ def main():
         cs = torch.cuda.Stream(dev)
         cs.wait_stream(stream)
         for c in range(copies):
-            g = torch.cuda.CUDAGraph()
+            graphs.append(torch.cuda.CUDAGraph())
             n0 = _lib.launch_count()
-            with torch.cuda.stream(cs), torch.cuda.graph(g, stream=cs):
+            with torch.cuda.stream(cs), torch.cuda.graph(graphs[-1], stream=cs):
                 step(c)
             launches_per_graph = _lib.launch_count() - n0
-            graphs.append(g)
         stream.wait_stream(cs)
         for c in range(copies):
             graphs[c].replay()
@@ -412,10 +414,9 @@ def main():
         cs2 = torch.cuda.Stream(dev)
         cs2.wait_stream(stream)
         for c in range(copies):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(cs2), torch.cuda.graph(g, stream=cs2):
+            dg.append(torch.cuda.CUDAGraph())
+            with torch.cuda.stream(cs2), torch.cuda.graph(dg[-1], stream=cs2):
                 dom.objs[c](dom.x)
-            dg.append(g)
         stream.wait_stream(cs2)
         reps = max(20, min(400, args.steps))
         for r in range(4):
@@ -432,6 +433,7 @@ def main():
         dist.all_reduce(td, op=dist.ReduceOp.MAX)
         dom_ms = float(td.item())
         dom_note = f"dominant layer alone, {reps} graph replays after the timed steps, max over ranks"
+        dg.clear()
         del dg
         for L in layers:
             for o in L.objs:
@@ -478,6 +480,8 @@ def main():
         e2e_gbs = round(total_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9, 3)
     h2d = sum(L.x_host.numel() * 4 for L in layers)
     d2h = sum(L.n * m * 4 for L in layers)
+    # graphs that hold NCCL calls must be released before the process group is destroyed
+    graphs.clear()
     del graphs
     torch.cuda.synchronize()
     if world > 1:
@@ -507,7 +511,7 @@ def main():
                        "m": m, "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
                        "exchange": {None: None, "p2p": "fused P2P stores + flag barrier in the GEMV kernel",
                                     "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
-                       "graph": world > 1,
+                       "graph": world > 1, "pdl": args.pdl,
                        "l2": f"weights {per_gpu / 2**20:.0f} MiB per GPU x {copies} rotating copies >= 4x L2 "
                              f"(no flush needed)"},
             "us_per_gemv": round(ms * 1e3 / args.steps / len(layers), 3),

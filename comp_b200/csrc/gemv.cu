@@ -86,6 +86,9 @@ static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) 
   return blocks;
 }
 
+// Programmatic dependent launch of the GEMV kernels (on by default; b2q_set_pipeline path 3/4 toggles it).
+static int g_pdl = 1;
+
 // Tuning overrides (benchmark hook): 0 = planner's choice.
 static int g_tune_rows = 0, g_tune_cpt = 0, g_tune_grid = 0, g_tune_stages = 0, g_tune_path = 0;
 
@@ -265,7 +268,22 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.stages = pl.stages;
     p.stage_bytes = pl.stage_bytes;
     p.dense = (a.ldwq == (int64_t)C * 16) ? 1 : 0;
-    pl.fn<<<pl.grid, pl.T, pl.smem, stream>>>(p);
+    // programmatic stream serialization: the kernel's weight prefetch may overlap the preceding kernel's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)pl.grid);
+    cfg.blockDim = dim3((unsigned)pl.T);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&cfg, pl.fn, p);
+    if (le != cudaSuccess) {
+      cudaGetLastError();
+      return fail(B2Q_ECUDA, "gemv: launch failed: %s", cudaGetErrorString(le));
+    }
     rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
     if (rc) return rc;
   }
@@ -361,6 +379,10 @@ int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
 }
 
 int b2q_set_pipeline(int path, int stages) {
+  if (path == 3 || path == 4) {  // 3: programmatic dependent launch on, 4: off
+    g_pdl = path == 3 ? 1 : 0;
+    return B2Q_OK;
+  }
   if (path < 0 || path > 2) return fail(B2Q_EINVAL, "b2q_set_pipeline: path must be 0 (auto), 1 (ring), 2 (registers)");
   if (stages < 0 || stages == 1 || stages > 8) return fail(B2Q_EINVAL, "b2q_set_pipeline: stages must be 0 or 2..8");
   g_tune_path = path;

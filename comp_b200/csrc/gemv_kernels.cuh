@@ -142,6 +142,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// Programmatic dependent launch: wait until the preceding grid on the stream has completed and its writes are
+// visible, then let the next grid launch (its CTAs start prefetching their own weights while this grid finishes).
+// Only immutable inputs (weights) may be read before this point; activations, outputs and flags only after it.
+// Without a programmatic dependency both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait_then_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -462,23 +471,19 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
     if (m < p.M && row < p.N) {
       float v = 0.f;
       for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * V + threadIdx.x];
-      p.y[(int64_t)m * p.ldy + p.row0 + row] = v;
+      const int64_t idx = (int64_t)m * p.ldy + p.row0 + row;
+      p.y[idx] = v;
+      if (p.y_peers != nullptr) {  // fused all-gather: the same value into every other rank's copy of Y
+        for (int q = 0; q < p.nranks; ++q)
+          if (q != p.rank) p.y_peers[q][idx] = v;
+      }
     }
   }
 }
 
-// Fused all-gather epilogue: copies this CTA's rows of Y to every peer, then the last CTA runs the flag barrier.
-__device__ __forceinline__ void allgather_epilogue(const GemvParams& p, int64_t g_begin, int64_t g_end, int R) {
-  __syncthreads();
-  const int64_t r_begin = g_begin * R, r_end = min(g_end * R, p.N);
-  for (int m = 0; m < p.M; ++m) {
-    const int64_t base = (int64_t)m * p.ldy + p.row0;
-    for (int64_t row = r_begin + threadIdx.x; row < r_end; row += blockDim.x) {
-      const float v = p.y[base + row];
-      for (int q = 0; q < p.nranks; ++q)
-        if (q != p.rank) p.y_peers[q][base + row] = v;
-    }
-  }
+// Fused all-gather epilogue: the CTA's rows were already stored into every peer's Y group by group (reduce_store);
+// every thread makes its own peer stores visible system-wide, then the last CTA of the grid runs the flag barrier.
+__device__ __forceinline__ void allgather_epilogue(const GemvParams& p) {
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -568,6 +573,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
 
   WeightRegs<R> cur, nxt;
   load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
+  pdl_wait_then_trigger();
   stage_activations<FMT>(p, xs, xsum, xscale);
 
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
@@ -608,7 +614,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
     g = gn;
     i = in;
   }
-  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
+  if (p.y_peers != nullptr) allgather_epilogue(p);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -658,6 +664,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
     for (int64_t j = 0; j < min((int64_t)(S - 1), ngroups); ++j)
       issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
   }
+  pdl_wait_then_trigger();
   stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
 
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
@@ -725,7 +732,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
     }
     return;
   }
-  if (p.y_peers != nullptr) allgather_epilogue(p, g_begin, g_end, R);
+  if (p.y_peers != nullptr) allgather_epilogue(p);
 }
 
 using KernelFn = void (*)(const GemvParams);

@@ -66,13 +66,13 @@ def main():
                 for name, yy in (("graph a", ya), ("graph b", yb)):
                     if not torch.equal(yy.view(torch.int32), want.view(torch.int32)):
                         fails.append(f"{fmt} {n}x{k} {name}: mismatch")
-                del graph
+                del graph, ya, yb
                 if L.status_code() != 0:
                     fails.append(f"{fmt} {n}x{k} barrier status {L.status_code()}")
             L.close()
     torch.cuda.synchronize(dev)
     dist.barrier()
-    print(f"RESULT {rank} {'ok' if not fails else 'FAIL ' + '; '.join(fails)}", flush=True)
+    print(f"\nRESULT {rank} {'ok' if not fails else 'FAIL ' + '; '.join(fails)}", flush=True)
     dist.destroy_process_group()
     sys.exit(1 if fails else 0)
 
