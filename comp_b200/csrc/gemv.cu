@@ -100,9 +100,11 @@ struct Plan {
   KernelFn fn;
 };
 
-static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T) {
+// Shared memory besides the ring: staged activations (none when they live in registers) and the reduction partials.
+static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T, bool xreg) {
   const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
-  return (size_t)M * K + (size_t)M * C * 4 + (size_t)M * nblk * 4 + (size_t)2 * (T / 32) * R * MC * 4;
+  const int Mx = xreg ? 0 : M;
+  return (size_t)Mx * K + (size_t)Mx * C * 4 + (size_t)Mx * nblk * 4 + (size_t)2 * (T / 32) * R * MC * 4;
 }
 
 static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
@@ -134,7 +136,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
     for (int ci = 0; ci < 4; ++ci) {
       const int R = cand[ci];
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
-      const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T);
+      const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T, xreg);
       const int64_t groups = (N + R - 1) / R;
       int stages = 0;
       uint32_t sb = 0;

@@ -482,11 +482,12 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
 }
 
 // Fused all-gather epilogue: the CTA's rows were already stored into every peer's Y group by group (reduce_store);
-// every thread makes its own peer stores visible system-wide, then the last CTA of the grid runs the flag barrier.
+// after a CTA barrier, one thread fences at system scope (cumulative over the CTA's stores) and counts the CTA in;
+// the last CTA of the grid runs the flag barrier.
 __device__ __forceinline__ void allgather_epilogue(const GemvParams& p) {
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // every peer store of this CTA happens before thread 0's system-scope fence and release below
   if (threadIdx.x == 0) {
+    __threadfence_system();
     // flags: [0, nranks) latest epoch seen from each rank, [nranks] CTA arrival counter, [nranks+1] own epoch
     uint32_t* own = p.flags;
     const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
@@ -546,6 +547,149 @@ __device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i,
   }
 }
 
+// XREG prologue: this thread's activation chunk straight from global memory into registers -- no shared memory and
+// no CTA barrier. int8 input: the chunk's q8 bytes, offset sum and scale. f32 input: the chunk is quantized here with
+// the math of b2q_quant_q8_0 / b2q_quant_q8_K: a Q4_0 chunk is a whole q8_0 block (one thread); a TQ2_0 chunk is a
+// quarter of a q8_K block, whose largest magnitude, its first index and its signed value are combined over the 4
+// threads of the block by xor-shuffles (all lanes of the warp take part; chunks past the row end are zero).
+// CTA 0 also stores the quantized activations when xq_out is given.
+template <int FMT>
+__device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool valid, XChunk& o) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o.x[j] = make_uint4(0u, 0u, 0u, 0u);
+  o.sum = 0;
+  o.dx = 0.f;
+  const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr) && valid;
+  if (p.x_f32 == nullptr) {
+    if (!valid) return;
+    if (FMT == 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.xq + (int64_t)c * 32);
+      o.x[0] = src[0];
+      o.x[1] = src[1];
+      o.dx = p.xd[c];
+    } else {
+      const int b = c >> 2, cc = c & 3;
+      const int8_t* base = p.xq + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o.x[j] = *reinterpret_cast<const uint4*>(base + j * 32);
+      o.dx = p.xd[b];
+    }
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < Fmt<FMT>::kFields; ++j)
+      sum += bytesum(o.x[j].x) + bytesum(o.x[j].y) + bytesum(o.x[j].z) + bytesum(o.x[j].w);
+    o.sum = (FMT == 0) ? 8 * sum : sum;
+    return;
+  }
+  if (FMT == 0) {
+    if (!valid) return;
+    const float4* src = reinterpret_cast<const float4*>(p.x_f32 + (int64_t)c * 32);
+    float4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = src[i];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q0 = (int)roundf(__fmul_rn(v[i].x, id)), q1 = (int)roundf(__fmul_rn(v[i].y, id));
+      const int q2 = (int)roundf(__fmul_rn(v[i].z, id)), q3 = (int)roundf(__fmul_rn(v[i].w, id));
+      w[i] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+             ((uint32_t)(q3 & 0xff) << 24);
+      sum += q0 + q1 + q2 + q3;
+    }
+    o.x[0] = make_uint4(w[0], w[1], w[2], w[3]);  // values 0..15 (low-nibble field)
+    o.x[1] = make_uint4(w[4], w[5], w[6], w[7]);  // values 16..31 (high-nibble field)
+    o.sum = 8 * sum;
+    o.dx = q8_0_stored_scale(d);
+    if (writer) {
+      uint4* dst = reinterpret_cast<uint4*>(p.xq_out + (int64_t)c * 32);
+      dst[0] = o.x[0];
+      dst[1] = o.x[1];
+      if (p.xd_out) p.xd_out[c] = o.dx;
+    }
+    return;
+  }
+  // TQ2_0 / q8_K: field j of chunk c holds block values (cc/2)*128 + j*32 + (cc%2)*16 + t, t = 0..15
+  const int b = c >> 2, cc = c & 3;
+  const int vbase = (cc >> 1) * 128 + (cc & 1) * 16;
+  float v[4][16];
+  if (valid) {
+    const float* base = p.x_f32 + (int64_t)b * 256 + vbase;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int t4 = 0; t4 < 4; ++t4) {
+        const float4 f = *reinterpret_cast<const float4*>(base + j * 32 + t4 * 4);
+        v[j][t4 * 4 + 0] = f.x, v[j][t4 * 4 + 1] = f.y, v[j][t4 * 4 + 2] = f.z, v[j][t4 * 4 + 3] = f.w;
+      }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int t = 0; t < 16; ++t) v[j][t] = 0.f;
+  }
+  // local largest magnitude, its lowest value index, and its signed value (values visited in increasing index)
+  float amax = 0.f, cand = 0.f;
+  int first = 256;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const float a = fabsf(v[j][t]);
+      if (a > amax) {
+        amax = a;
+        first = vbase + j * 32 + t;
+        cand = v[j][t];
+      }
+    }
+  // combine over the 4 threads of the block: larger magnitude wins, equal magnitudes keep the lower index
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+    const int of = __shfl_xor_sync(0xffffffffu, first, off);
+    const float oc = __shfl_xor_sync(0xffffffffu, cand, off);
+    if (oa > amax || (oa == amax && of < first)) {
+      amax = oa;
+      first = of;
+      cand = oc;
+    }
+  }
+  const bool nz = amax != 0.0f;
+  const float iscale = __fdiv_rn(-127.0f, nz ? cand : 1.0f);
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int q = (int)fminf(rintf(__fmul_rn(iscale, v[j][k * 4 + e])), 127.0f);
+        q = nz ? q : 0;
+        sum += q;
+        word |= (uint32_t)(q & 0xff) << (8 * e);
+      }
+      w[k] = word;
+    }
+    o.x[j] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  o.sum = sum;
+  o.dx = nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
+  if (writer) {
+    int8_t* dst = p.xq_out + (int64_t)b * 256 + vbase;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + j * 32) = o.x[j];
+    if (cc == 0 && p.xd_out) p.xd_out[b] = o.dx;
+  }
+}
+
 template <int FMT, int MC, bool XREG>
 __device__ __forceinline__ void get_x(const GemvParams& p, const uint8_t* xs, const int* xsum, const float* xscale,
                                       const XChunk& xr, int c, bool valid, XChunk (&xc)[MC]) {
@@ -561,12 +705,13 @@ __device__ __forceinline__ void get_x(const GemvParams& p, const uint8_t* xs, co
 template <int FMT, int R, int MC, bool BYTES, bool XREG>
 __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int M = p.M, C = p.C;
+  const int C = p.C;
+  const int Mx = XREG ? 0 : p.M;  // XREG: activations never touch shared memory
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  uint8_t* xs = smem;                                                    // [M][K] permuted int8
-  int* xsum = reinterpret_cast<int*>(smem + (size_t)M * p.K);             // [M][C]
-  float* xscale = reinterpret_cast<float*>(xsum + M * C);                // [M][nblk]
-  float* red = xscale + M * nblk;                                        // [2][warps][R*MC]
+  uint8_t* xs = smem;                                                    // [Mx][K] permuted int8
+  int* xsum = reinterpret_cast<int*>(smem + (size_t)Mx * p.K);            // [Mx][C]
+  float* xscale = reinterpret_cast<float*>(xsum + Mx * C);               // [Mx][nblk]
+  float* red = xscale + Mx * nblk;                                       // [2][warps][R*MC]
 
   const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
   const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
@@ -574,10 +719,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
   WeightRegs<R> cur, nxt;
   load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
   pdl_wait_then_trigger();
-  stage_activations<FMT>(p, xs, xsum, xscale);
-
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
-  if (XREG) load_xchunk<FMT>(p, xs, xsum, xscale, 0, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+  if (XREG)
+    load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+  else
+    stage_activations<FMT>(p, xs, xsum, xscale);
 
   float acc[R * MC];
 #pragma unroll
@@ -640,15 +786,16 @@ template <int FMT, int R, int MC, bool XREG>
 __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
-  const int M = p.M, C = p.C, S = p.stages;
+  const int C = p.C, S = p.stages;
+  const int Mx = XREG ? 0 : p.M;  // XREG: activations never touch shared memory
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
   uint8_t* ring = smem;                                                          // [S][stage_bytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.stage_bytes);  // [S]
   uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((S + 1) & ~1));               // 16-byte aligned
-  int* xsum = reinterpret_cast<int*>(xs + (size_t)M * p.K);
-  float* xscale = reinterpret_cast<float*>(xsum + M * C);
-  float* red = xscale + M * nblk;
+  int* xsum = reinterpret_cast<int*>(xs + (size_t)Mx * p.K);
+  float* xscale = reinterpret_cast<float*>(xsum + Mx * C);
+  float* red = xscale + Mx * nblk;
 
   const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
   const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
@@ -665,10 +812,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
       issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
   }
   pdl_wait_then_trigger();
-  stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
-
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
-  if (XREG) load_xchunk<FMT>(p, xs, xsum, xscale, 0, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+  if (XREG) {
+    load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+    __syncthreads();  // publishes the barrier init and s_abort
+  } else {
+    stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
+  }
 
   float acc[R * MC];
 #pragma unroll
