@@ -212,9 +212,10 @@ struct LaunchArgs {
   int64_t ldy;
   int64_t row0;
   int32_t* s;
-  float* const* y_peers;
-  uint32_t* flags;
-  uint32_t* const* flags_peers;
+  uint2* const* rx_peers;
+  uint2* rx;
+  int64_t rx_stride;
+  unsigned long long* done;
   int32_t* status;
   int rank, nranks;
   long long spin_limit;
@@ -254,9 +255,11 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.ldy = a.ldy;
     p.row0 = a.row0;
     p.s = a.s ? a.s + m0 * a.N * nblk : nullptr;
-    p.y_peers = a.y_peers;  // the exchange path is limited to one column group (M <= kMaxColumns) by its entry point
-    p.flags = a.flags;
-    p.flags_peers = a.flags_peers;
+    p.rx_peers = a.rx_peers;  // the exchange path is limited to one column group (M <= kMaxColumns) by its entry point
+    p.rx = a.rx;
+    p.rx_stride = a.rx_stride;
+    p.done = a.done;
+    p.N_total = a.rx_peers ? a.ldy : a.N;
     p.status = a.status;
     p.rank = a.rank;
     p.nranks = a.nranks;
@@ -344,7 +347,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 }
 
 int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
-                       float* y, float* const* y_peers, uint32_t* flags, uint32_t* const* flags_peers,
+                       float* y, void* rx, void* const* rx_peers, int64_t rx_stride, unsigned long long* done,
                        int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
                        int rank, int nranks, long long spin_limit, b2q_stream_t stream) {
   const char* who = "b2q_gemv_allgather";
@@ -354,17 +357,20 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
   if (K < 1 || n_local < 1 || row0 < 0 || row0 + n_local > N_total)
     return fail(B2Q_EINVAL, "%s: rows [%lld, %lld) not inside [0, %lld), or K=%lld", who, (long long)row0,
                 (long long)(row0 + n_local), (long long)N_total, (long long)K);
-  if (!y || !y_peers || !flags || !flags_peers || !status) return fail(B2Q_EINVAL, "%s: null pointer", who);
+  if (!y || !rx || !rx_peers || !done || !status) return fail(B2Q_EINVAL, "%s: null pointer", who);
+  if (rx_stride < M * N_total) return fail(B2Q_EINVAL, "%s: rx_stride %lld < M*N_total", who, (long long)rx_stride);
   if (spin_limit < 1) return fail(B2Q_EINVAL, "%s: spin_limit must be positive", who);
   int rc = check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, n_local, K, M, true);
   if (rc) return rc;
   if (ldx < K || (ldx % 4)) return fail(B2Q_EALIGN, "%s: ldx must be >= K and a multiple of 4", who);
-  if (!aligned(flags, 4) || !aligned(status, 4)) return fail(B2Q_EALIGN, "%s: flags/status must be 4-byte aligned", who);
+  if (!aligned(rx, 8) || !aligned(done, 8) || !aligned(status, 4))
+    return fail(B2Q_EALIGN, "%s: rx/done must be 8-byte aligned, status 4-byte aligned", who);
   LaunchArgs a{};
   a.fmt = fmt;
   a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx;
   a.y = y, a.ldy = N_total, a.row0 = row0;
-  a.y_peers = y_peers, a.flags = flags, a.flags_peers = flags_peers, a.status = status;
+  a.rx = reinterpret_cast<uint2*>(rx), a.rx_peers = reinterpret_cast<uint2* const*>(rx_peers);
+  a.rx_stride = rx_stride, a.done = done, a.status = status;
   a.rank = rank, a.nranks = nranks, a.spin_limit = spin_limit;
   a.N = n_local, a.K = K, a.M = M;
   return launch_gemv(a, (cudaStream_t)stream);

@@ -57,10 +57,13 @@ struct GemvParams {
   int64_t ldy;
   int64_t row0;
   int32_t* s;             // [M][N][nblk] int32 block dots (nullable)
-  // fused all-gather epilogue (multi-GPU): y is this rank's copy; every CTA also copies its rows to the peers
-  float* const* y_peers;  // device array [nranks] or null
-  uint32_t* flags;        // this rank's flag array [nranks + 2] (peer epochs, CTA arrival counter, own epoch)
-  uint32_t* const* flags_peers;  // device array [nranks] of flag arrays (each [nranks + 1] uint32) or null
+  // fused all-gather (multi-GPU): own rows go to y; every output value is also sent to each peer's receive buffer as
+  // one 8-byte (value, flag) store; each CTA then collects its slice of the peers' rows from its own receive buffer
+  uint2* const* rx_peers; // device array [nranks] of the ranks' receive buffers (peer-mapped), or null
+  uint2* rx;              // this rank's receive buffer: 2 parities x rx_stride entries ((m, row) -> m*ldy + row)
+  int64_t rx_stride;      // entries per parity
+  unsigned long long* done;  // CTAs completed over all calls of this layer (call index = done / gridDim.x)
+  int64_t N_total;
   int32_t* status;
   int rank, nranks;
   long long spin_limit;
@@ -457,7 +460,7 @@ __device__ __forceinline__ float warp_sum_scatter(float (&v)[V], int lane) {
 // __syncthreads. red is double-buffered so the next group's writes never race this group's reads.
 template <int R, int MC>
 __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, float (&acc)[R * MC], float* red,
-                                             int buf) {
+                                             int buf, int parity) {
   constexpr int V = R * MC;
   const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float s = warp_sum_scatter<V>(acc, lane);
@@ -473,50 +476,60 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
       for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * V + threadIdx.x];
       const int64_t idx = (int64_t)m * p.ldy + p.row0 + row;
       p.y[idx] = v;
-      if (p.y_peers != nullptr) {  // fused all-gather: the same value into every other rank's copy of Y
+      if (p.rx_peers != nullptr) {  // fused all-gather: (value, flag 1) into every other rank's receive buffer
+        const int64_t off = (int64_t)parity * p.rx_stride + idx;
         for (int q = 0; q < p.nranks; ++q)
-          if (q != p.rank) p.y_peers[q][idx] = v;
+          if (q != p.rank) {
+            uint2* dst = p.rx_peers[q] + off;
+            asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(__float_as_uint(v)), "r"(1u)
+                         : "memory");
+          }
       }
     }
   }
 }
 
-// Fused all-gather epilogue: the CTA's rows were already stored into every peer's Y group by group (reduce_store);
-// after a CTA barrier, one thread fences at system scope (cumulative over the CTA's stores) and counts the CTA in;
-// the last CTA of the grid runs the flag barrier.
-__device__ __forceinline__ void allgather_epilogue(const GemvParams& p) {
-  __syncthreads();  // every peer store of this CTA happens before thread 0's system-scope fence and release below
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    // flags: [0, nranks) latest epoch seen from each rank, [nranks] CTA arrival counter, [nranks+1] own epoch
-    uint32_t* own = p.flags;
-    const uint32_t arrived = atomicAdd(own + p.nranks, 1u);
-    if (arrived == gridDim.x - 1) {
-      own[p.nranks] = 0u;  // reset the arrival counter for the next call
-      const uint32_t epoch = own[p.nranks + 1] + 1u;
-      __threadfence_system();
-      for (int q = 0; q < p.nranks; ++q) {
-        uint32_t* f = p.flags_peers[q] + p.rank;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+// Fused all-gather, receive side. Every value a peer sends is one 8-byte (value, flag) store, single-copy atomic, so
+// the value is visible together with its flag and no fence is needed. Each CTA collects a contiguous slice of the
+// entries of the peers' rows: it polls each entry (bounded) until the flag is set, copies the value into y and clears
+// the flag for the call after next. The receive buffer alternates between two parities per call, so a fast peer's
+// next call never overwrites entries of this call that are still unread: a rank starts call t+2 only after it has
+// received every rank's rows of call t+1, which each rank sends after finishing call t.
+// Call index (and so the parity) of this launch: every CTA of a call reads done / gridDim.x at its start, which is
+// exact because only CTAs of this call can have incremented it since the previous call completed.
+__device__ __forceinline__ int call_parity(const GemvParams& p) {
+  if (p.rx_peers == nullptr) return 0;
+  const unsigned long long d = *reinterpret_cast<volatile unsigned long long*>(p.done);
+  return (int)((d / gridDim.x) & 1ull);
+}
+
+__device__ __forceinline__ void allgather_collect(const GemvParams& p, int parity) {
+  const int64_t peer_rows = p.N_total - p.N;
+  const int64_t total = (int64_t)p.M * peer_rows;
+  const int64_t e_begin = (total * blockIdx.x) / gridDim.x, e_end = (total * (blockIdx.x + 1)) / gridDim.x;
+  uint2* rx = p.rx + (int64_t)parity * p.rx_stride;
+  int err = 0;
+  for (int64_t e = e_begin + threadIdx.x; e < e_end && !err; e += blockDim.x) {
+    const int64_t m = e / peer_rows, r = e - m * peer_rows;
+    const int64_t row = r < p.row0 ? r : r + p.N;
+    const int64_t idx = m * p.ldy + row;
+    uint2* src = rx + idx;
+    uint32_t val, flag;
+    long long spins = 0;
+    for (;;) {
+      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(val), "=r"(flag) : "l"(src) : "memory");
+      if (flag != 0u) break;
+      if (++spins > p.spin_limit) {
+        err = 1;
+        break;
       }
-      int err = 0;
-      for (int q = 0; q < p.nranks && !err; ++q) {
-        long long spins = 0;
-        uint32_t v;
-        for (;;) {
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + q) : "memory");
-          if ((int32_t)(v - epoch) >= 0) break;
-          if (++spins > p.spin_limit) {
-            err = 1 + q;
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-      own[p.nranks + 1] = epoch;
-      if (err && p.status) *p.status = err;
     }
+    p.y[idx] = __uint_as_float(val);
+    asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(&src->y), "r"(0u) : "memory");
   }
+  if (err && p.status) atomicExch(p.status, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(p.done, 1ull);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -719,6 +732,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
   WeightRegs<R> cur, nxt;
   load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
   pdl_wait_then_trigger();
+  const int parity = call_parity(p);
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
   if (XREG)
     load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
@@ -753,14 +767,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
     else
       compute_chunk<FMT, R, MC, BYTES, false>(p, g, c, valid, cur.w, dw, xc, acc);
     if (in == 0) {
-      reduce_store<R, MC>(p, g, acc, red, buf);
+      reduce_store<R, MC>(p, g, acc, red, buf, parity);
       buf ^= 1;
     }
     cur = nxt;
     g = gn;
     i = in;
   }
-  if (p.y_peers != nullptr) allgather_epilogue(p);
+  if (p.rx_peers != nullptr) allgather_collect(p, parity);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -812,6 +826,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
       issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
   }
   pdl_wait_then_trigger();
+  const int rx_parity = call_parity(p);
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
   if (XREG) {
     load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
@@ -866,7 +881,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
       else
         compute_chunk<FMT, R, MC, false, false>(p, g, c, valid, w, dw, xc, acc);
     }
-    reduce_store<R, MC>(p, g, acc, red, buf);
+    reduce_store<R, MC>(p, g, acc, red, buf, rx_parity);
     buf ^= 1;
     if (++s == S) {
       s = 0;
@@ -882,7 +897,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvPar
     }
     return;
   }
-  if (p.y_peers != nullptr) allgather_epilogue(p);
+  if (p.rx_peers != nullptr) allgather_collect(p, rx_parity);
 }
 
 using KernelFn = void (*)(const GemvParams);

@@ -8,10 +8,11 @@ output slices are all-gathered so every rank holds the full Y [M][N], ready to b
 result does not depend on which rank computes it: the sharded Y is bit-identical to the single-GPU Y.
 
 Exchange paths:
-  "p2p"   fused into the GEMV kernel (b2q_gemv_allgather): each CTA stores its rows straight into every peer's Y
-          through CUDA IPC mappings over NVLink, and the last CTA runs a flag barrier with bounded waits. One launch
-          per layer, graph-capturable. Y is double-buffered: the tensor returned by call t stays valid until this
-          rank issues call t+2 (consume it before then, e.g. as the next layer's input).
+  "p2p"   fused into the GEMV kernel (b2q_gemv_allgather): every output value is sent to each peer as one 8-byte
+          (value, flag) store into its receive buffer (CUDA IPC mappings over NVLink), and each CTA collects its
+          slice of the peers' rows with bounded polls -- no fences, no grid-wide barrier. One launch per layer,
+          graph-capturable. The returned Y is this layer's output buffer: call t's result stays valid until the
+          layer's next call.
   "nccl"  host.quant_gemv, then torch.distributed.all_gather_into_tensor of equal-size padded slices.
 """
 
@@ -22,7 +23,7 @@ import torch.distributed as dist
 
 from . import _lib, host
 
-SPIN_LIMIT = 1 << 24  # flag polls per peer (with a 64 ns back-off) before the barrier reports a timeout
+SPIN_LIMIT = 1 << 26  # polls of one receive entry (~1-3 s) before the kernel reports a timeout
 
 
 def partition(n, nranks, align=4):
@@ -115,35 +116,31 @@ class RowShardedGemv:
     def _init_p2p(self):
         dev = self.dev
         with torch.cuda.device(dev):
-            self.y = torch.zeros((2, self.max_m, self.n), dtype=torch.float32, device=dev)  # double-buffered
-            self.flags = torch.zeros(self.world + 2, dtype=torch.int32, device=dev)
+            self.y = torch.zeros((self.max_m, self.n), dtype=torch.float32, device=dev)
+            self.rx_stride = self.max_m * self.n
+            self.rx = torch.zeros((2, self.rx_stride, 2), dtype=torch.int32, device=dev)  # (value bits, flag)
+            self.done = torch.zeros(1, dtype=torch.int64, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
             torch.cuda.synchronize(dev)
-            self._ymap = _PeerMapped(self.y, self.group)
-            self._fmap = _PeerMapped(self.flags, self.group)
-            nbuf = self.max_m * self.n * 4
-            self._ypeers = [torch.tensor([p + b * nbuf for p in self._ymap.ptrs], dtype=torch.int64, device=dev)
-                            for b in range(2)]
-            self._fpeers = torch.tensor(self._fmap.ptrs, dtype=torch.int64, device=dev)
+            self._rxmap = _PeerMapped(self.rx, self.group)
+            self._rxpeers = torch.tensor(self._rxmap.ptrs, dtype=torch.int64, device=dev)
         dist.barrier(group=self.group)
 
     def _p2p(self, x):
         m = x.shape[0]
         if m > self.max_m:
             raise ValueError(f"p2p exchange: M={m} > max_m={self.max_m}")
-        b = self._calls & 1
         self._calls += 1
-        y = self.y[b]
         with torch.cuda.device(self.dev):
             _lib.call("b2q_gemv_allgather", host.FMT_ID[self.fmt], self.wq.data_ptr(), self.wq.stride(0),
-                      self.ws.data_ptr(), x.data_ptr(), x.stride(0), y.data_ptr(), self._ypeers[b].data_ptr(),
-                      self.flags.data_ptr(), self._fpeers.data_ptr(), self.status.data_ptr(), self.row0, self.rows,
-                      self.n, self.k, m, self.rank, self.world, SPIN_LIMIT,
+                      self.ws.data_ptr(), x.data_ptr(), x.stride(0), self.y.data_ptr(), self.rx.data_ptr(),
+                      self._rxpeers.data_ptr(), self.rx_stride, self.done.data_ptr(), self.status.data_ptr(),
+                      self.row0, self.rows, self.n, self.k, m, self.rank, self.world, SPIN_LIMIT,
                       torch.cuda.current_stream(self.dev).cuda_stream)
-        return y[:m]
+        return self.y[:m]
 
     def status_code(self):
-        """0, or 1 + the rank a flag barrier timed out waiting for (synchronizes)."""
+        """0, or 1 if a receive poll timed out (synchronizes)."""
         return int(self.status.item()) if self.exchange == "p2p" else 0
 
     # ---- NCCL exchange ----
@@ -168,9 +165,8 @@ class RowShardedGemv:
 
     def close(self):
         """Unmaps the peers' buffers (collective: every rank calls it, after its last use of the layer)."""
-        if self.exchange == "p2p" and getattr(self, "_ymap", None) is not None:
+        if self.exchange == "p2p" and getattr(self, "_rxmap", None) is not None:
             torch.cuda.synchronize(self.dev)
             dist.barrier(group=self.group)
-            self._ymap.close()
-            self._fmap.close()
-            self._ymap = self._fmap = None
+            self._rxmap.close()
+            self._rxmap = None

@@ -111,22 +111,23 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 /*
  * Row-sharded GEMV with the output all-gather fused into the kernel (multi-GPU, one process per GPU).
  * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows. The kernel
- * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows, stores
- * them into its own full output y [M][N_total] and, with plain peer stores over NVLink, into every other rank's
- * full output (y_peers[q], the peer-mapped base of rank q's y). The last CTA to finish then runs a flag barrier:
- * with e = flags[nranks+1] + 1 it writes e into flags_peers[q][rank] of every rank q (system-scope release), waits
- * for at most spin_limit polls per rank until every flags[q] of its own >= e (acquire), and stores e back into
- * flags[nranks+1]. When the kernel completes, y holds every rank's rows. The epoch lives in device memory, so the
- * launch can be captured in a CUDA graph and replayed. On a timeout the last CTA writes 1 + (the rank it waited for)
- * to *status (device int32) and the output must be treated as invalid; the call itself returns B2Q_OK once launched.
- *   flags:  this rank's uint32 [nranks + 2], zeroed once before the first call (slot nranks: CTA arrival counter,
- *           reset by the kernel; slot nranks+1: this rank's epoch); flags_peers: device array [nranks] of
- *           peer-mapped flag arrays (flags_peers[rank] == flags).
- *   Every rank must make the same sequence of calls. M <= 4.
+ * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows into
+ * y [M][N_total], and sends every value to every other rank as one 8-byte (value bits, flag 1) store into that
+ * rank's receive buffer (rx_peers[q], peer-mapped). Each CTA then collects a slice of the other ranks' rows from its
+ * own rx: it polls each entry (at most spin_limit times) until its flag is set, copies the value into y and clears
+ * the flag. When the kernel completes, y holds all N_total rows. No fences and no grid-wide barrier are needed.
+ *   rx:        this rank's receive buffer, 2 x rx_stride entries of 8 bytes (uint32 value bits, uint32 flag),
+ *              zeroed once before the first call; entry (m, row) of a call sits at parity * rx_stride + m*N_total + row.
+ *   rx_peers:  device array [nranks] of the ranks' rx base pointers (rx_peers[rank] == rx).
+ *   done:      uint64 counter of completed CTAs, zeroed once; the call index is done / grid, its parity selects
+ *              the half of rx, so consecutive calls (also as CUDA-graph replays) alternate halves.
+ *   status:    device int32 set to 1 if a poll gave up (the output is then invalid); the call returns B2Q_OK once
+ *              launched.
+ *   Every rank must make the same sequence of calls with the same shapes. M <= 4.
  * No reference counterpart (the reference has no multi-GPU path); replaces host.gemv + an NCCL all-gather.
  */
 int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
-                       float* y, float* const* y_peers, uint32_t* flags, uint32_t* const* flags_peers,
+                       float* y, void* rx, void* const* rx_peers, int64_t rx_stride, unsigned long long* done,
                        int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
                        int rank, int nranks, long long spin_limit, b2q_stream_t stream);
 
