@@ -796,8 +796,13 @@ __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint
   bulk_g2s(stage + R * qrow, p.ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
 }
 
+#ifdef B2Q_RING_MAXNREG
+#define B2Q_RING_BOUNDS __maxnreg__(B2Q_RING_MAXNREG)
+#else
+#define B2Q_RING_BOUNDS __launch_bounds__(kMaxThreads, 1)
+#endif
 template <int FMT, int R, int MC, bool XREG>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_ring_kernel(const GemvParams p) {
+__global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
   const int C = p.C, S = p.stages;
