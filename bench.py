@@ -325,6 +325,8 @@ def main():
         L.x = L.x_host.to(dev)
         L.y = torch.empty((m, n), dtype=torch.float32, device=dev)
         L.fid = 0 if fmt == "q4_0" else 1
+        L.wsb = host.workspace_size(fmt, n, k, m) if world == 1 else 0
+        L.work = torch.empty(max(16, L.wsb), dtype=torch.uint8, device=dev)
         if world > 1:
             L.objs = [RowShardedGemv(fmt, wq, ws, n, k, exchange=args.exchange) for wq, ws in L.w]
         layers.append(L)
@@ -335,10 +337,10 @@ def main():
     exchange_name = None if world == 1 else layers[0].objs[0].exchange
 
     def launch(L, c):
-        """N = 1: one fused quantize + GEMV launch straight through the C ABI."""
+        """N = 1: fused quantize + GEMV straight through the C ABI (tall-K layers: split-K, two launches)."""
         wq, ws = L.w[c]
-        rc = lib.b2q_quant_gemv(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x.data_ptr(), L.x.stride(0),
-                                None, None, L.y.data_ptr(), L.rows, L.k, m, sptr)
+        rc = lib.b2q_quant_gemv_ws(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x.data_ptr(), L.x.stride(0),
+                                   None, None, L.y.data_ptr(), L.rows, L.k, m, L.work.data_ptr(), L.wsb, sptr)
         if rc != 0:
             raise RuntimeError(_lib.last_error())
 

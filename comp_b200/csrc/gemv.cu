@@ -41,6 +41,21 @@ namespace b2q {
 // Host side: planning and launch
 // ------------------------------------------------------------------------------------------------------------------
 
+// Split-K combine: y[m][n] = sum over s of partial[s][m][n], splits summed in order 0, 1, ... (deterministic).
+// Launched with programmatic stream serialization after the split GEMV; reads the partials only after the wait.
+__global__ void __launch_bounds__(256) splitk_sum_kernel(const float* __restrict__ partial, float* __restrict__ y,
+                                                         int64_t M, int64_t N, int64_t ldy, int splits) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = partial[i];
+    for (int s = 1; s < splits; ++s) v += partial[(int64_t)s * total + i];
+    const int64_t m = i / N, n = i - m * N;
+    y[m * ldy + n] = v;
+  }
+}
+
 static KernelFn kernel_for(int fmt, bool bytes, bool ring, int R, int MC, bool xreg) {
   return ring ? ring_kernel_for(fmt, R, MC, xreg) : reg_kernel_for(fmt, bytes, R, MC, xreg);
 }
@@ -113,7 +128,8 @@ static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
   return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
 }
 
-static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out) {
+// K is the per-split K; `splits` CTAs rows share the SMs (the grid is splits x grid_x).
+static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out, int splits = 1) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -153,7 +169,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       const int occ = occupancy(fn, T, smem, di.max_smem_optin);
       if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
       if (occ == 0) continue;
-      int64_t grid = std::min<int64_t>(groups, (int64_t)occ * di.sms);
+      int64_t grid = std::min<int64_t>(groups, std::max<int64_t>(1, (int64_t)occ * di.sms / splits));
       if (g_tune_grid > 0) grid = std::min<int64_t>(groups, g_tune_grid);
       // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
       const int64_t per = (groups + grid - 1) / grid;
@@ -172,6 +188,24 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
                 (long long)K, M, di.max_smem_optin);
   *out = best;
   return B2Q_OK;
+}
+
+// K splits the split-K schedule uses for a layer (1 = none): tall-K layers whose rows would need CTAs of more than
+// 256 threads are split until each split's row fits 256 threads (measured on B200: smaller CTAs with the same bytes
+// in flight stream faster). Every split keeps 16-byte aligned whole scale rows (ring path) and whole quads of TQ2_0
+// chunks. Only for one column group (M <= 4).
+static int choose_splits(int fmt, int64_t K, int64_t M) {
+  if (M < 1 || M > kMaxColumns || K == 0) return 1;
+  const int blk = fmt == 0 ? 32 : 256;
+  const int64_t nblk = K / blk, C = K / (fmt == 0 ? 32 : 64);
+  if (C <= 256) return 1;
+  for (int s = 2; s <= 16; s *= 2) {
+    if (nblk % s) continue;
+    const int64_t nblk_s = nblk / s;
+    if ((nblk_s * 2) % 16) continue;
+    if (C / s <= 256) return s;
+  }
+  return 1;
 }
 
 static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws,
@@ -220,6 +254,8 @@ struct LaunchArgs {
   int rank, nranks;
   long long spin_limit;
   int64_t N, K, M;
+  float* workspace;  // split-K partial sums (null: no split)
+  size_t workspace_bytes;
 };
 
 static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
@@ -233,27 +269,45 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   }
   const int blk = a.fmt == 0 ? 32 : 256;
   const int64_t nblk = a.K / blk;
-  const int C = (int)(a.K / (a.fmt == 0 ? 32 : 64));
+  // split-K when a workspace for the partial sums is given and the layer is tall (one column group only)
+  int splits = 1;
+  if (a.workspace && !a.s && !a.rx_peers && a.M <= kMaxColumns) {
+    const int sp = choose_splits(a.fmt, a.K, a.M);
+    if (sp > 1 && (size_t)sp * a.M * a.N * sizeof(float) <= a.workspace_bytes) splits = sp;
+  }
+  const int64_t Ks = a.K / splits, nblk_s = nblk / splits;
+  const int C = (int)(Ks / (a.fmt == 0 ? 32 : 64));
   // ring path: every row's scale bytes (and so every group's) must be a whole number of 16-byte units, 16-aligned
-  const bool ring_ok = ((nblk * 2) % 16 == 0) && aligned(a.ws, 16);
+  const bool ring_ok = ((nblk * 2) % 16 == 0) && ((nblk_s * 2) % 16 == 0) && aligned(a.ws, 16);
   for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
     const int Mc = (int)std::min<int64_t>(kMaxColumns, a.M - m0);
     Plan pl;
-    int rc = make_plan(a.fmt, a.bytes, ring_ok, a.N, a.K, Mc, &pl);
+    int rc = make_plan(a.fmt, a.bytes, ring_ok, a.N, Ks, Mc, &pl, splits);
     if (rc) return rc;
     GemvParams p{};
     p.wq = a.wq;
     p.ldwq = a.ldwq;
     p.ws = a.ws;
+    p.ldws = nblk;
     p.xq = a.xq ? a.xq + m0 * a.K : nullptr;
+    p.ldxq = a.K;
     p.xd = a.xd ? a.xd + m0 * nblk : nullptr;
+    p.ldxd = nblk;
     p.x_f32 = a.x_f32 ? a.x_f32 + m0 * a.ldx : nullptr;
     p.ldx = a.ldx;
     p.xq_out = a.xq_out ? a.xq_out + m0 * a.K : nullptr;
     p.xd_out = a.xd_out ? a.xd_out + m0 * nblk : nullptr;
-    p.y = a.y + m0 * a.ldy;
-    p.ldy = a.ldy;
-    p.row0 = a.row0;
+    if (splits > 1) {  // partial sums [splits][Mc][N] in the workspace, combined below
+      p.y = a.workspace;
+      p.ldy = a.N;
+      p.row0 = 0;
+      p.y_split = (int64_t)Mc * a.N;
+    } else {
+      p.y = a.y + m0 * a.ldy;
+      p.ldy = a.ldy;
+      p.row0 = a.row0;
+      p.y_split = 0;
+    }
     p.s = a.s ? a.s + m0 * a.N * nblk : nullptr;
     p.rx_peers = a.rx_peers;  // the exchange path is limited to one column group (M <= kMaxColumns) by its entry point
     p.rx = a.rx;
@@ -265,17 +319,17 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.nranks = a.nranks;
     p.spin_limit = a.spin_limit;
     p.N = a.N;
-    p.K = a.K;
+    p.K = Ks;
     p.M = Mc;
     p.C = C;
     p.CPT = pl.CPT;
     p.groups = (a.N + pl.R - 1) / pl.R;
     p.stages = pl.stages;
     p.stage_bytes = pl.stage_bytes;
-    p.dense = (a.ldwq == (int64_t)C * 16) ? 1 : 0;
+    p.dense = (splits == 1 && a.ldwq == (int64_t)C * 16) ? 1 : 0;
     // programmatic stream serialization: the kernel's weight prefetch may overlap the preceding kernel's tail
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)pl.grid);
+    cfg.gridDim = dim3((unsigned)pl.grid, (unsigned)splits);
     cfg.blockDim = dim3((unsigned)pl.T);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
@@ -288,6 +342,27 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     if (le != cudaSuccess) {
       cudaGetLastError();
       return fail(B2Q_ECUDA, "gemv: launch failed: %s", cudaGetErrorString(le));
+    }
+    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
+    if (rc) return rc;
+    if (splits > 1) {
+      DeviceInfo di;
+      if ((rc = device_info(&di))) return rc;
+      const int64_t total = (int64_t)Mc * a.N;
+      cudaLaunchConfig_t c2 = {};
+      c2.gridDim = dim3((unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)di.sms * 4));
+      c2.blockDim = dim3(256);
+      c2.stream = stream;
+      c2.attrs = attr;
+      c2.numAttrs = 1;
+      le = cudaLaunchKernelEx(&c2, splitk_sum_kernel, (const float*)a.workspace, a.y + m0 * a.ldy + a.row0,
+                              (int64_t)Mc, a.N, a.ldy, splits);
+      if (le != cudaSuccess) {
+        cudaGetLastError();
+        return fail(B2Q_ECUDA, "gemv: split-K combine launch failed: %s", cudaGetErrorString(le));
+      }
+      rc = after_launch("splitk_sum");
+      if (rc) return rc;
     }
     rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
     if (rc) return rc;
@@ -343,6 +418,31 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
   a.fmt = fmt;
   a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx, a.xq_out = xq, a.xd_out = xd, a.y = y, a.ldy = N;
   a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
+size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
+  if ((fmt != 0 && fmt != 1) || N <= 0 || K <= 0 || M <= 0 || (K % (fmt == 0 ? 32 : 256))) return 0;
+  const int sp = choose_splits(fmt, K, M);
+  return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
+}
+
+int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                      int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, void* workspace,
+                      size_t workspace_bytes, b2q_stream_t stream) {
+  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: fmt %d is not Q4_0 (0) or TQ2_0 (1)", fmt);
+  int rc = check_gemv_args("b2q_quant_gemv_ws", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
+  if (rc) return rc;
+  if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
+    return fail(B2Q_EALIGN, "b2q_quant_gemv_ws: ldx must be >= K and a multiple of 4");
+  if ((xq == nullptr) != (xd == nullptr)) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: give both xq and xd, or neither");
+  if (xq && !aligned(xq, 16)) return fail(B2Q_EALIGN, "b2q_quant_gemv_ws: xq must be 16-byte aligned");
+  if (workspace && !aligned(workspace, 16)) return fail(B2Q_EALIGN, "b2q_quant_gemv_ws: workspace must be 16-byte aligned");
+  LaunchArgs a{};
+  a.fmt = fmt;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx, a.xq_out = xq, a.xd_out = xd, a.y = y, a.ldy = N;
+  a.N = N, a.K = K, a.M = M;
+  a.workspace = reinterpret_cast<float*>(workspace), a.workspace_bytes = workspace ? workspace_bytes : 0;
   return launch_gemv(a, (cudaStream_t)stream);
 }
 

@@ -73,6 +73,12 @@ struct GemvParams {
   int C;                  // 16-byte chunks per row
   int CPT;                // chunks per thread per row
   int64_t groups;         // ceil(N / R)
+  // split-K (gridDim.y = splits): split s handles K columns [s*K, (s+1)*K) of the full rows -- p.K, p.C are the
+  // per-split values -- and writes its partial sums to y + s*y_split; strides below refer to the full matrices
+  int64_t ldws;           // scale-plane row stride (elements)
+  int64_t ldxq;           // int8 activation row stride (bytes); also for xq_out
+  int64_t ldxd;           // activation scale row stride (elements); also for xd_out
+  int64_t y_split;        // elements between the partial outputs of consecutive splits
   int stages;             // ring path: shared-memory stages
   uint32_t stage_bytes;   // ring path: bytes per stage (R rows of quants, then R rows of scales, 16-byte padded)
   int dense;              // ring path: ldwq == C*16, so a group's quant rows are one contiguous copy
@@ -87,6 +93,30 @@ struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibb
 template <>
 struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
   static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4;
+};
+
+// Base pointers of this CTA's K split (blockIdx.y); with one split every offset is zero.
+template <int FMT>
+struct Split {
+  static __device__ __forceinline__ int64_t nblk(const GemvParams& p) { return p.K / Fmt<FMT>::kBlock; }
+  static __device__ __forceinline__ const uint8_t* wq(const GemvParams& p) {
+    return p.wq + (int64_t)blockIdx.y * (p.K / (FMT == 0 ? 2 : 4));
+  }
+  static __device__ __forceinline__ const int16_t* ws(const GemvParams& p) {
+    return p.ws + (int64_t)blockIdx.y * nblk(p);
+  }
+  static __device__ __forceinline__ const int8_t* xq(const GemvParams& p) { return p.xq + (int64_t)blockIdx.y * p.K; }
+  static __device__ __forceinline__ const float* xd(const GemvParams& p) { return p.xd + (int64_t)blockIdx.y * nblk(p); }
+  static __device__ __forceinline__ const float* xf(const GemvParams& p) {
+    return p.x_f32 + (int64_t)blockIdx.y * p.K;
+  }
+  static __device__ __forceinline__ int8_t* xq_out(const GemvParams& p) {
+    return p.xq_out + (int64_t)blockIdx.y * p.K;
+  }
+  static __device__ __forceinline__ float* xd_out(const GemvParams& p) {
+    return p.xd_out + (int64_t)blockIdx.y * nblk(p);
+  }
+  static __device__ __forceinline__ float* y(const GemvParams& p) { return p.y + (int64_t)blockIdx.y * p.y_split; }
 };
 
 // Position (in 16-byte units, within one activation column) of the q-th 16-byte piece of the natural int8 layout.
@@ -187,7 +217,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         const int idx = base + u * T;
         if (idx < total) {
           const int m = idx / units, q = idx - m * units;
-          v[u] = *reinterpret_cast<const uint4*>(p.xq + (int64_t)m * K + (int64_t)q * 16);
+          v[u] = *reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)m * p.ldxq + (int64_t)q * 16);
         }
       }
 #pragma unroll
@@ -199,7 +229,10 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         }
       }
     }
-    for (int idx = tt; idx < M * nblk; idx += T) xscale[idx] = p.xd[idx];
+    for (int idx = tt; idx < M * nblk; idx += T) {
+      const int m = idx / nblk, b = idx - m * nblk;
+      xscale[idx] = Split<FMT>::xd(p)[(int64_t)m * p.ldxd + b];
+    }
   } else if (FMT == 0) {
     // q8_0: 8 lanes per 32-value block (4 blocks per warp per slot); kUnroll slots of loads in flight per lane
     const int lane = tt & 31, sub = lane & 7, nw = T / 32;
@@ -213,7 +246,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (g < total) {
           const int m = g / nblk, b = g - m * nblk;
-          v[u] = *reinterpret_cast<const float4*>(p.x_f32 + (int64_t)m * p.ldx + b * 32 + sub * 4);
+          v[u] = *reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)m * p.ldx + b * 32 + sub * 4);
         }
       }
 #pragma unroll
@@ -227,8 +260,8 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
           const float ds = q8_0_stored_scale(d);
           if (sub == 0) xscale[m * nblk + b] = ds;
           if (writer) {
-            *reinterpret_cast<uint32_t*>(p.xq_out + (int64_t)m * K + b * 32 + sub * 4) = q;
-            if (sub == 0 && p.xd_out) p.xd_out[m * nblk + b] = ds;
+            *reinterpret_cast<uint32_t*>(Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq + b * 32 + sub * 4) = q;
+            if (sub == 0 && p.xd_out) Split<FMT>::xd_out(p)[(int64_t)m * p.ldxd + b] = ds;
           }
         }
       }
@@ -246,7 +279,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         va[u] = vb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (g < total) {
           const int m = g / nblk, b = g - m * nblk;
-          const float* src = p.x_f32 + (int64_t)m * p.ldx + b * 256 + lane * 8;
+          const float* src = Split<FMT>::xf(p) + (int64_t)m * p.ldx + b * 256 + lane * 8;
           va[u] = *reinterpret_cast<const float4*>(src);
           vb[u] = *reinterpret_cast<const float4*>(src + 4);
         }
@@ -265,8 +298,9 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
               make_uint2(qlo, qhi);
           if (lane == 0) xscale[m * nblk + b] = d;
           if (writer) {
-            *reinterpret_cast<uint2*>(p.xq_out + (int64_t)m * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
-            if (lane == 0 && p.xd_out) p.xd_out[m * nblk + b] = d;
+            *reinterpret_cast<uint2*>(Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq + b * 256 + lane * 8) =
+                make_uint2(qlo, qhi);
+            if (lane == 0 && p.xd_out) Split<FMT>::xd_out(p)[(int64_t)m * p.ldxd + b] = d;
           }
         }
       }
@@ -475,7 +509,7 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
       float v = 0.f;
       for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * V + threadIdx.x];
       const int64_t idx = (int64_t)m * p.ldy + p.row0 + row;
-      p.y[idx] = v;
+      p.y[idx + (int64_t)blockIdx.y * p.y_split] = v;
       if (p.rx_peers != nullptr) {  // fused all-gather: (value, flag 1) into every other rank's receive buffer
         const int64_t off = (int64_t)parity * p.rx_stride + idx;
         for (int q = 0; q < p.nranks; ++q)
@@ -551,8 +585,8 @@ __device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i,
   for (int r = 0; r < R; ++r) {
     const int64_t row = g * R + r;
     if (active && c < p.C && row < p.N) {
-      u.w[r] = ld_stream_v4(p.wq + row * p.ldwq + (int64_t)c * 16);
-      u.sc[r] = ld_stream_u16(p.ws + row * nblk + (c >> Fmt<FMT>::kChunkShift));
+      u.w[r] = ld_stream_v4(Split<FMT>::wq(p) + row * p.ldwq + (int64_t)c * 16);
+      u.sc[r] = ld_stream_u16(Split<FMT>::ws(p) + row * p.ldws + (c >> Fmt<FMT>::kChunkShift));
     } else {
       u.w[r] = make_uint4(0u, 0u, 0u, 0u);
       u.sc[r] = 0;
@@ -576,16 +610,16 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   if (p.x_f32 == nullptr) {
     if (!valid) return;
     if (FMT == 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.xq + (int64_t)c * 32);
+      const uint4* src = reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 32);
       o.x[0] = src[0];
       o.x[1] = src[1];
-      o.dx = p.xd[c];
+      o.dx = Split<FMT>::xd(p)[c];
     } else {
       const int b = c >> 2, cc = c & 3;
-      const int8_t* base = p.xq + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
+      const int8_t* base = Split<FMT>::xq(p) + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
 #pragma unroll
       for (int j = 0; j < 4; ++j) o.x[j] = *reinterpret_cast<const uint4*>(base + j * 32);
-      o.dx = p.xd[b];
+      o.dx = Split<FMT>::xd(p)[b];
     }
     int sum = 0;
 #pragma unroll
@@ -596,7 +630,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   }
   if (FMT == 0) {
     if (!valid) return;
-    const float4* src = reinterpret_cast<const float4*>(p.x_f32 + (int64_t)c * 32);
+    const float4* src = reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 32);
     float4 v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = src[i];
@@ -621,10 +655,10 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     o.sum = 8 * sum;
     o.dx = q8_0_stored_scale(d);
     if (writer) {
-      uint4* dst = reinterpret_cast<uint4*>(p.xq_out + (int64_t)c * 32);
+      uint4* dst = reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 32);
       dst[0] = o.x[0];
       dst[1] = o.x[1];
-      if (p.xd_out) p.xd_out[c] = o.dx;
+      if (p.xd_out) Split<FMT>::xd_out(p)[c] = o.dx;
     }
     return;
   }
@@ -633,7 +667,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   const int vbase = (cc >> 1) * 128 + (cc & 1) * 16;
   float v[4][16];
   if (valid) {
-    const float* base = p.x_f32 + (int64_t)b * 256 + vbase;
+    const float* base = Split<FMT>::xf(p) + (int64_t)b * 256 + vbase;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -696,10 +730,10 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   o.sum = sum;
   o.dx = nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
   if (writer) {
-    int8_t* dst = p.xq_out + (int64_t)b * 256 + vbase;
+    int8_t* dst = Split<FMT>::xq_out(p) + (int64_t)b * 256 + vbase;
 #pragma unroll
     for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + j * 32) = o.x[j];
-    if (cc == 0 && p.xd_out) p.xd_out[b] = o.dx;
+    if (cc == 0 && p.xd_out) Split<FMT>::xd_out(p)[b] = o.dx;
   }
 }
 
@@ -788,12 +822,18 @@ __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint
   const int64_t r0 = g * R;
   const int rows = (int)min((int64_t)R, p.N - r0);
   mbar_expect_tx(bar, (uint32_t)rows * (qrow + srow));
+  const uint8_t* wq = Split<FMT>::wq(p);
+  const int16_t* ws = Split<FMT>::ws(p);
   if (p.dense) {
-    bulk_g2s(stage, p.wq + r0 * p.ldwq, (uint32_t)rows * qrow, bar, pol);
+    bulk_g2s(stage, wq + r0 * p.ldwq, (uint32_t)rows * qrow, bar, pol);
   } else {
-    for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, p.wq + (r0 + r) * p.ldwq, qrow, bar, pol);
+    for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, wq + (r0 + r) * p.ldwq, qrow, bar, pol);
   }
-  bulk_g2s(stage + R * qrow, p.ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
+  if (p.ldws == nblk) {  // contiguous scale rows: one copy
+    bulk_g2s(stage + R * qrow, ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
+  } else {
+    for (int r = 0; r < rows; ++r) bulk_g2s(stage + R * qrow + r * srow, ws + (r0 + r) * p.ldws, srow, bar, pol);
+  }
 }
 
 #ifdef B2Q_RING_MAXNREG

@@ -211,10 +211,18 @@ def gemv(fmt, wq, ws, xq, xd, n, k, block_n=32, nb=4, mode=0, num_warps=4, store
     return y, s
 
 
-def quant_gemv(fmt, wq, ws, x, n, k, return_act=False):
-    """Fused quantize + gemv in one launch: f32 x [M][K] -> Y f32 [M][N] (and (XQ, XD) when return_act).
+def workspace_size(fmt, n, k, m):
+    """Bytes of split-K workspace quant_gemv uses for this shape (0: the layer is not split)."""
+    return int(_lib.load().b2q_workspace_size(FMT_ID[fmt], n, k, m))
 
-    Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule, same f32 order)."""
+
+def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=None):
+    """Fused quantize + gemv: f32 x [M][K] -> Y f32 [M][N] (and (XQ, XD) when return_act).
+
+    split=False: one launch; Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule,
+    same f32 order). split=True (default): tall-K layers run the split-K schedule with a workspace (allocated here
+    unless given; a CUDA byte tensor of at least workspace_size(...) bytes); Y then differs from the single-launch
+    result only by f32 rounding of the sum order, and is deterministic."""
     f = _fmt(fmt)
     dev = _need_cuda("quant_gemv", wq, ws, x)
     _check_weights(fmt, wq, ws, n, k)
@@ -227,8 +235,12 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False):
     if return_act:
         xq = torch.empty((m, k), dtype=torch.int8, device=dev)
         xd = torch.empty((m, k // f["block"]), dtype=torch.float32, device=dev)
+    wsb = workspace_size(fmt, n, k, m) if split else 0
+    if wsb and workspace is None:
+        workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        _lib.call("b2q_quant_gemv", FMT_ID[fmt], wq.data_ptr(), wq.stride(0), ws.data_ptr(), x.data_ptr(),
+        _lib.call("b2q_quant_gemv_ws", FMT_ID[fmt], wq.data_ptr(), wq.stride(0), ws.data_ptr(), x.data_ptr(),
                   x.stride(0), xq.data_ptr() if return_act else None, xd.data_ptr() if return_act else None,
-                  y.data_ptr(), n, k, m, _stream(dev))
+                  y.data_ptr(), n, k, m, workspace.data_ptr() if wsb else None,
+                  workspace.numel() * workspace.element_size() if wsb else 0, _stream(dev))
     return (y, xq, xd) if return_act else y

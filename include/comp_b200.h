@@ -109,6 +109,25 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream);
 
 /*
+ * Split-K workspace: bytes of scratch b2q_quant_gemv_ws uses for this layer shape (0 = the layer is not split).
+ * Tall-K layers (rows of more than 256 16-byte chunks, e.g. K = 14336 Q4_0 or K = 28672 TQ2_0) are split over K
+ * into 2-4 independent slices computed concurrently (blockIdx.y); each writes partial sums [splits][M][N] to the
+ * workspace and a second kernel sums them in split order (deterministic). Part of the north star's split-K schedule
+ * for tall-K layers; no reference counterpart (COMP loops over K inside one program, kernels.py:61).
+ */
+size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M);
+
+/*
+ * b2q_quant_gemv with a caller-provided workspace (device memory, 16-byte aligned): when workspace_bytes >=
+ * b2q_workspace_size(fmt, N, K, M) > 0 the split-K schedule runs; otherwise exactly b2q_quant_gemv. Two launches
+ * when split (GEMV, then the combine), one otherwise. Results match b2q_quant_gemv within f32 rounding (the split
+ * changes the summation order) and are deterministic. Fuses host.quantize + host.gemv (src/komp/host.py:63-85).
+ */
+int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                      int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, void* workspace,
+                      size_t workspace_bytes, b2q_stream_t stream);
+
+/*
  * Row-sharded GEMV with the output all-gather fused into the kernel (multi-GPU, one process per GPU).
  * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows. The kernel
  * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows into

@@ -119,7 +119,8 @@ def test_gemv_matches_reference(cuda, golden, cid):
     y, s = host.gemv(fmt, _t(wq, cuda), _t(ws, cuda), xq, xd, n, k, mode=2)
     assert s is None and _same_f32(y.cpu().numpy(), ys[2])
     # fused quantizer prologue: same activations, same Y
-    yf, fq, fd = host.quant_gemv(fmt, _t(wq, cuda), _t(ws, cuda), _t(g["x"], cuda), n, k, return_act=True)
+    yf, fq, fd = host.quant_gemv(fmt, _t(wq, cuda), _t(ws, cuda), _t(g["x"], cuda), n, k, return_act=True,
+                                 split=False)
     assert np.array_equal(fq.cpu().numpy(), g["xq"]) and _same_f32(fd.cpu().numpy(), g["xd"])
     assert _same_f32(yf.cpu().numpy(), ys[2])
 
@@ -262,7 +263,7 @@ def test_ring_and_register_paths_identical(cuda, fmt, n, k, m):
                 continue
             assert np.array_equal(s.cpu().numpy(), os_), (path, rows, stages)
             outs.append(y.cpu().numpy())
-            yf = host.quant_gemv(fmt, twq, tws, tx, n, k)
+            yf = host.quant_gemv(fmt, twq, tws, tx, n, k, split=False)
             assert _same_f32(yf.cpu().numpy(), outs[-1])
     finally:
         _lib.call("b2q_set_tuning", 0, 0, 0)
@@ -300,3 +301,26 @@ def test_allgather_receive_times_out_and_reports(cuda):
     assert int(done.item()) > 0                            # every CTA counted itself in
     # the context is still usable
     assert _same_f32(host.quant_gemv("q4_0", twq, tws, tx, rows, k).cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("tq2_0", 8192, 28672, 1), ("q4_0", 4100, 14336, 1), ("q4_0", 333, 28672, 3),
+                                       ("tq2_0", 37, 28672, 2)])
+def test_split_k_matches_oracle_and_is_deterministic(cuda, fmt, n, k, m):
+    """Tall-K layers through the split-K schedule (workspace of partial sums + ordered combine): same quantized
+    activations, Y within the rule of the exact reference, within f32 rounding of the single-launch Y, and repeatable."""
+    assert host.workspace_size(fmt, n, k, m) > 0
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 17, cuda)
+    before = _lib.launch_count()
+    ys, fq, fd = host.quant_gemv(fmt, twq, tws, tx, n, k, return_act=True)
+    assert _lib.launch_count() - before == 2  # split GEMV + combine
+    oq, od = ref.quantize(fmt, x)
+    assert np.array_equal(fq.cpu().numpy(), oq) and _same_f32(fd.cpu().numpy(), od)
+    r, _ = native.gemv(fmt, wq, ws, oq, od, k)
+    ys = ys.cpu().numpy()
+    assert ref.relerr(ys, r) <= TOL
+    y1 = host.quant_gemv(fmt, twq, tws, tx, n, k, split=False).cpu().numpy()
+    assert ref.relerr(ys, y1) <= 1e-6
+    assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy(), ys)
+    # too small a workspace: no split, exactly the single-launch result
+    tiny = torch.empty(16, dtype=torch.uint8, device=cuda)
+    assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, workspace=tiny).cpu().numpy(), y1)
