@@ -175,8 +175,8 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       const int64_t per = (groups + grid - 1) / grid;
       const double balance = (double)groups / (double)(per * grid);
       // larger groups amortize the per-group reduction and barrier (measured on B200: R = 8 fastest whenever it
-      // fits, even at 7% worse balance)
-      const double score = balance + 0.1 * std::log2((double)R);
+      // fits, even at 13% worse balance)
+      const double score = balance + 0.2 * std::log2((double)R);
       if (score > best_score) {
         best_score = score;
         best = Plan{R, T, CPT, (int)grid, stages, sb, smem, ring, fn};
@@ -190,12 +190,16 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
   return B2Q_OK;
 }
 
-// K splits the split-K schedule uses for a layer (1 = none): tall-K layers whose rows would need CTAs of more than
-// 256 threads are split until each split's row fits 256 threads (measured on B200: smaller CTAs with the same bytes
-// in flight stream faster). Every split keeps 16-byte aligned whole scale rows (ring path) and whole quads of TQ2_0
-// chunks. Only for one column group (M <= 4).
+// K splits the split-K schedule uses for a layer (1 = none). Off by default: on B200 the BASELINE tall-K layers ran
+// slower split (TQ2_0 8192x28672: 23.4 vs 19.0 us; Q4_0 4096x14336: 14.6 vs 11.9 us) -- the unsplit kernel already
+// keeps the HBM stream busy and the combine adds a launch. With b2q_set_splitk(1) tall-K layers whose rows would
+// need CTAs of more than 256 threads are split until each split's row fits 256 threads; b2q_set_splitk(n) forces n.
+// Every split keeps 16-byte aligned whole scale rows (ring path) and whole quads of TQ2_0 chunks. One column group
+// (M <= 4) only.
+static int g_splitk_mode = 0;  // 0: never split (default; measured slower on B200), 1: automatic rule, n>=2: force n
+
 static int choose_splits(int fmt, int64_t K, int64_t M) {
-  if (M < 1 || M > kMaxColumns || K == 0) return 1;
+  if (g_splitk_mode == 0 || M < 1 || M > kMaxColumns || K == 0) return 1;
   const int blk = fmt == 0 ? 32 : 256;
   const int64_t nblk = K / blk, C = K / (fmt == 0 ? 32 : 64);
   if (C <= 256) return 1;
@@ -203,7 +207,7 @@ static int choose_splits(int fmt, int64_t K, int64_t M) {
     if (nblk % s) continue;
     const int64_t nblk_s = nblk / s;
     if ((nblk_s * 2) % 16) continue;
-    if (C / s <= 256) return s;
+    if (g_splitk_mode >= 2 ? s == g_splitk_mode : C / s <= 256) return s;
   }
   return 1;
 }
@@ -364,8 +368,6 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       rc = after_launch("splitk_sum");
       if (rc) return rc;
     }
-    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
-    if (rc) return rc;
   }
   return B2Q_OK;
 }
@@ -483,6 +485,12 @@ int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
   g_tune_rows = rows_per_group;
   g_tune_cpt = chunks_per_thread;
   g_tune_grid = grid;
+  return B2Q_OK;
+}
+
+int b2q_set_splitk(int mode) {
+  if (mode < 0 || mode > 16) return fail(B2Q_EINVAL, "b2q_set_splitk: mode must be 0 (off), 1 (auto) or 2..16");
+  g_splitk_mode = mode;
   return B2Q_OK;
 }
 

@@ -109,13 +109,18 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream);
 
 /*
- * Split-K workspace: bytes of scratch b2q_quant_gemv_ws uses for this layer shape (0 = the layer is not split).
+ * Split-K workspace: bytes of scratch b2q_quant_gemv_ws uses for this layer shape under the current split-K mode
+ * (0 = the layer is not split; see b2q_set_splitk).
  * Tall-K layers (rows of more than 256 16-byte chunks, e.g. K = 14336 Q4_0 or K = 28672 TQ2_0) are split over K
  * into 2-4 independent slices computed concurrently (blockIdx.y); each writes partial sums [splits][M][N] to the
  * workspace and a second kernel sums them in split order (deterministic). Part of the north star's split-K schedule
  * for tall-K layers; no reference counterpart (COMP loops over K inside one program, kernels.py:61).
  */
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M);
+
+/* Split-K mode (process-wide): 0 = never split (default: on B200 the unsplit kernel measured faster on every
+ * BASELINE tall-K layer), 1 = split tall-K layers automatically, n >= 2 = n splits where the shape allows. */
+int b2q_set_splitk(int mode);
 
 /*
  * b2q_quant_gemv with a caller-provided workspace (device memory, 16-byte aligned): when workspace_bytes >=

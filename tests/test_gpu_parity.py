@@ -308,6 +308,15 @@ def test_allgather_receive_times_out_and_reports(cuda):
 def test_split_k_matches_oracle_and_is_deterministic(cuda, fmt, n, k, m):
     """Tall-K layers through the split-K schedule (workspace of partial sums + ordered combine): same quantized
     activations, Y within the rule of the exact reference, within f32 rounding of the single-launch Y, and repeatable."""
+    assert host.workspace_size(fmt, n, k, m) == 0  # off by default
+    _lib.call("b2q_set_splitk", 1)
+    try:
+        _split_k_checks(cuda, fmt, n, k, m)
+    finally:
+        _lib.call("b2q_set_splitk", 0)
+
+
+def _split_k_checks(cuda, fmt, n, k, m):
     assert host.workspace_size(fmt, n, k, m) > 0
     wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 17, cuda)
     before = _lib.launch_count()
