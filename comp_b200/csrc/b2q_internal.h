@@ -25,4 +25,9 @@ int device_info(DeviceInfo* out);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// Fused quantize + split-K GEMV with exactly `splits` K splits, partial sums in `workspace` (gemv.cu).
+int quant_gemv_forced_split(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                            float* y, int64_t N, int64_t K, int64_t M, int splits, float* workspace,
+                            size_t workspace_bytes, cudaStream_t stream);
+
 }  // namespace b2q

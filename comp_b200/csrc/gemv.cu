@@ -260,6 +260,7 @@ struct LaunchArgs {
   int64_t N, K, M;
   float* workspace;  // split-K partial sums (null: no split)
   size_t workspace_bytes;
+  int force_splits;  // > 1: run exactly this many K splits (validated by the caller)
 };
 
 static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
@@ -276,7 +277,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   // split-K when a workspace for the partial sums is given and the layer is tall (one column group only)
   int splits = 1;
   if (a.workspace && !a.s && !a.rx_peers && a.M <= kMaxColumns) {
-    const int sp = choose_splits(a.fmt, a.K, a.M);
+    const int sp = a.force_splits > 1 ? a.force_splits : choose_splits(a.fmt, a.K, a.M);
     if (sp > 1 && (size_t)sp * a.M * a.N * sizeof(float) <= a.workspace_bytes) splits = sp;
   }
   const int64_t Ks = a.K / splits, nblk_s = nblk / splits;
@@ -370,6 +371,33 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     }
   }
   return B2Q_OK;
+}
+
+// Fused quantize + split-K GEMV into a given workspace with exactly `splits` K splits (used by gemv_noalloc.cu).
+int quant_gemv_forced_split(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                            float* y, int64_t N, int64_t K, int64_t M, int splits, float* workspace,
+                            size_t workspace_bytes, cudaStream_t stream) {
+  const char* who = "b2q_quant_gemv_splitk_noalloc";
+  int rc = check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
+  if (rc) return rc;
+  if (M > kMaxColumns) return fail(B2Q_ERANGE, "%s: M=%lld, at most %d columns", who, (long long)M, kMaxColumns);
+  const int blk = fmt == 0 ? 32 : 256;
+  const int64_t nblk = K / blk;
+  if (splits < 2 || splits > 16 || nblk % splits)
+    return fail(B2Q_EINVAL, "%s: splits=%d must be 2..16 and divide the %lld blocks of a row", who, splits,
+                (long long)nblk);
+  if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
+    return fail(B2Q_EALIGN, "%s: ldx must be >= K and a multiple of 4", who);
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  if (need > workspace_bytes)
+    return fail(B2Q_ERANGE, "%s: %d splits x M=%lld x N=%lld partial sums need %zu bytes, the scratch holds %zu", who,
+                splits, (long long)M, (long long)N, need, workspace_bytes);
+  LaunchArgs a{};
+  a.fmt = fmt;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx, a.y = y, a.ldy = N;
+  a.N = N, a.K = K, a.M = M;
+  a.workspace = workspace, a.workspace_bytes = workspace_bytes, a.force_splits = splits;
+  return launch_gemv(a, stream);
 }
 
 }  // namespace b2q

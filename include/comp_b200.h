@@ -133,6 +133,22 @@ int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
                       size_t workspace_bytes, b2q_stream_t stream);
 
 /*
+ * Split-K fused quantize + GEMV that allocates nothing, for callers that cannot allocate device memory (an inference
+ * engine that reserves all GPU memory at start-up, or an FFI caller without a device allocator of its own). It is
+ * b2q_quant_gemv_ws with exactly `splits` K splits (2..16, dividing the blocks of a row) whose partial sums live in
+ * a fixed scratch array inside the library: b2q_noalloc_scratch_bytes() bytes (4 MiB) on every GPU that loads the
+ * library, held until the process exits. splits * M * N * 4 must fit in it (else B2Q_ERANGE), M <= 4.
+ * The first call on a device, with that device current, looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture. Every call shares the one array, which keeps the last call's
+ * partial sums (each call overwrites all the sums it reads, so nothing has to start at zero); calls whose work
+ * overlaps on the GPU (other streams, other host threads) race on it. No counterpart in the reference.
+ */
+size_t b2q_noalloc_scratch_bytes(void);
+int b2q_quant_gemv_splitk_noalloc(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x,
+                                  int64_t ldx, float* y, int64_t N, int64_t K, int64_t M, int splits,
+                                  b2q_stream_t stream);
+
+/*
  * Row-sharded GEMV with the output all-gather fused into the kernel (multi-GPU, one process per GPU).
  * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows. The kernel
  * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows into
