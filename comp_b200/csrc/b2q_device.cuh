@@ -123,4 +123,13 @@ __device__ __forceinline__ float q8_K_quant8(const float (&v)[8], int lane, uint
 // Sum of the four signed bytes of a word.
 __device__ __forceinline__ int bytesum(uint32_t w) { return __dp4a((int)w, 0x01010101, 0); }
 
+// Programmatic dependent launch: wait until the preceding grid on the stream has completed and its writes are
+// visible, then let the next grid launch (its CTAs start prefetching their own weights while this grid finishes).
+// Only immutable inputs (weights) may be read before this point; activations, outputs and flags only after it.
+// Without a programmatic dependency both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait_then_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace b2q

@@ -25,6 +25,26 @@ int device_info(DeviceInfo* out);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// Whether kernels launch with programmatic dependent launch (b2q_set_pipeline; on by default).
+bool pdl_enabled();
+
+// Launches `kernel` on `stream`, with the programmatic-stream-serialization attribute when PDL is enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Fused quantize + split-K GEMV with exactly `splits` K splits, partial sums in `workspace` (gemv.cu).
 int quant_gemv_forced_split(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                             float* y, int64_t N, int64_t K, int64_t M, int splits, float* workspace,

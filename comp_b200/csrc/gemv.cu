@@ -103,6 +103,7 @@ static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) 
 
 // Programmatic dependent launch of the GEMV kernels (on by default; b2q_set_pipeline path 3/4 toggles it).
 static int g_pdl = 1;
+bool pdl_enabled() { return g_pdl != 0; }
 
 // Tuning overrides (benchmark hook): 0 = planner's choice.
 static int g_tune_rows = 0, g_tune_cpt = 0, g_tune_grid = 0, g_tune_stages = 0, g_tune_path = 0;

@@ -175,14 +175,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
-// Programmatic dependent launch: wait until the preceding grid on the stream has completed and its writes are
-// visible, then let the next grid launch (its CTAs start prefetching their own weights while this grid finishes).
-// Only immutable inputs (weights) may be read before this point; activations, outputs and flags only after it.
-// Without a programmatic dependency both instructions are no-ops.
-__device__ __forceinline__ void pdl_wait_then_trigger() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   uint4 v;

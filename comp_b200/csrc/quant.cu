@@ -1,7 +1,9 @@
 // Standalone activation quantizers (q8_0, q8_K) and the test probes (dp4a, Q4_0/TQ2_0 decode).
 //
 // The quantizers are memory-trivial (a [4][14336] f32 activation is 229 KB): one pass, fully coalesced, grid-stride.
-// The same device functions quantize inside the fused GEMV prologue, so both paths give the same bytes.
+// The same device functions quantize inside the fused GEMV prologue, so both paths give the same bytes. They take part
+// in programmatic dependent launch: each waits for the preceding grid, then at once lets the next grid (a GEMV)
+// launch, whose CTAs start streaming weights while the activations are being quantized.
 #include "b2q_device.cuh"
 #include "b2q_internal.h"
 
@@ -11,6 +13,7 @@ namespace b2q {
 __global__ void __launch_bounds__(256) quant_q8_0_kernel(const float* __restrict__ x, int64_t ldx,
                                                          int8_t* __restrict__ xq, float* __restrict__ xd, int64_t M,
                                                          int64_t K) {
+  pdl_wait_then_trigger();
   const int64_t nblk = K / 32;
   const int64_t total = M * nblk;
   const int sub = threadIdx.x & 7;
@@ -36,6 +39,7 @@ __global__ void __launch_bounds__(256) quant_q8_0_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) quant_q8_K_kernel(const float* __restrict__ x, int64_t ldx,
                                                          int8_t* __restrict__ xq, float* __restrict__ xd,
                                                          int16_t* __restrict__ bsums, int64_t M, int64_t K) {
+  pdl_wait_then_trigger();
   const int64_t nblk = K / 256;
   const int64_t total = M * nblk;
   const int lane = threadIdx.x & 31;
@@ -119,7 +123,8 @@ int b2q_quant_q8_0(const float* x, int64_t ldx, int8_t* xq, float* xd, int64_t M
   if (rc) return rc;
   if (M == 0 || K == 0) return B2Q_OK;
   const int64_t blocks = M * (K / 32);
-  quant_q8_0_kernel<<<grid_for(blocks, 32), 256, 0, (cudaStream_t)stream>>>(x, ldx, xq, xd, M, K);
+  launch_maybe_pdl(quant_q8_0_kernel, dim3(grid_for(blocks, 32)), dim3(256), 0, (cudaStream_t)stream, x, ldx, xq, xd,
+                   M, K);
   return after_launch("quant_q8_0");
 }
 
@@ -130,7 +135,8 @@ int b2q_quant_q8_K(const float* x, int64_t ldx, int8_t* xq, float* xd, int16_t* 
   if (bsums && !aligned(bsums, 4)) return fail(B2Q_EALIGN, "b2q_quant_q8_K: bsums must be 4-byte aligned");
   if (M == 0 || K == 0) return B2Q_OK;
   const int64_t blocks = M * (K / 256);
-  quant_q8_K_kernel<<<grid_for(blocks, 8), 256, 0, (cudaStream_t)stream>>>(x, ldx, xq, xd, bsums, M, K);
+  launch_maybe_pdl(quant_q8_K_kernel, dim3(grid_for(blocks, 8)), dim3(256), 0, (cudaStream_t)stream, x, ldx, xq, xd,
+                   bsums, M, K);
   return after_launch("quant_q8_K");
 }
 
