@@ -191,6 +191,49 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
   return B2Q_OK;
 }
 
+// Warp-rows path (one column): W warps per CTA, one CTA per SM, each warp with its own S-stage ring of R-row groups.
+static int g_tune_warps = 0;
+
+static int make_warp_plan(int fmt, int64_t N, int64_t K, Plan* out) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int C = (int)(K / (fmt == 0 ? 32 : 64));
+  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  const size_t xbytes = (size_t)K + 4 * (size_t)C + 4 * (size_t)nblk;
+  const int rows[3] = {4, 2, 1}, stages[3] = {3, 2, 4};
+  double best_score = -1.0;
+  Plan best{};
+  for (int R : rows) {
+    if (g_tune_rows > 0 && R != g_tune_rows) continue;
+    const uint32_t sb = ring_stage_bytes(fmt, K, C, R);
+    for (int S : stages) {
+      if (g_tune_stages > 0 && S != g_tune_stages) continue;
+      for (int W = kMaxThreads / 32; W >= 4; --W) {
+        if (g_tune_warps > 0 && W != g_tune_warps) continue;
+        const size_t smem = (size_t)W * S * sb + 8 * (size_t)((W * S + 1) & ~1) + xbytes;
+        if (smem > (size_t)di.max_smem_optin) continue;
+        KernelFn fn = warp_kernel_for(fmt, R);
+        if (!fn) continue;
+        const int occ = occupancy(fn, 32 * W, smem, di.max_smem_optin);
+        if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
+        if (occ == 0) continue;
+        const int64_t groups = (N + R - 1) / R;
+        // more warps first (latency hiding), then larger groups (fewer reductions per row), then deeper rings
+        const double score = W * 100.0 + R * 10.0 + (S == 3 ? 2 : S == 2 ? 1 : 0);
+        if (score > best_score) {
+          best_score = score;
+          best = Plan{R, 32 * W, (C + 31) / 32, (int)std::min<int64_t>(groups, di.sms), S, sb, smem, true, fn};
+        }
+        break;  // the largest W that fits for this (R, S)
+      }
+    }
+  }
+  if (best_score < 0) return fail(B2Q_ERANGE, "gemv: K=%lld does not fit the warp-rows schedule", (long long)K);
+  *out = best;
+  return B2Q_OK;
+}
+
 // K splits the split-K schedule uses for a layer (1 = none). Off by default: on B200 the BASELINE tall-K layers ran
 // slower split (TQ2_0 8192x28672: 23.4 vs 19.0 us; Q4_0 4096x14336: 14.6 vs 11.9 us) -- the unsplit kernel already
 // keeps the HBM stream busy and the combine adds a launch. With b2q_set_splitk(1) tall-K layers whose rows would
@@ -288,7 +331,10 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
     const int Mc = (int)std::min<int64_t>(kMaxColumns, a.M - m0);
     Plan pl;
-    int rc = make_plan(a.fmt, a.bytes, ring_ok, a.N, Ks, Mc, &pl, splits);
+    const bool warp_ok = Mc == 1 && a.M == 1 && splits == 1 && !a.rx_peers && ring_ok && !a.bytes;
+    if (g_tune_path == 5 && !warp_ok) return fail(B2Q_EINVAL, "gemv: warp-rows path forced but not applicable");
+    int rc = (warp_ok && g_tune_path == 5) ? make_warp_plan(a.fmt, a.N, Ks, &pl)
+                                           : make_plan(a.fmt, a.bytes, ring_ok, a.N, Ks, Mc, &pl, splits);
     if (rc) return rc;
     GemvParams p{};
     p.wq = a.wq;
@@ -523,12 +569,20 @@ int b2q_set_splitk(int mode) {
   return B2Q_OK;
 }
 
+int b2q_set_warps(int warps) {
+  if (warps != 0 && (warps < 4 || warps > kMaxThreads / 32))
+    return fail(B2Q_EINVAL, "b2q_set_warps: warps must be 0 (auto) or 4..%d", kMaxThreads / 32);
+  g_tune_warps = warps;
+  return B2Q_OK;
+}
+
 int b2q_set_pipeline(int path, int stages) {
   if (path == 3 || path == 4) {  // 3: programmatic dependent launch on, 4: off
     g_pdl = path == 3 ? 1 : 0;
     return B2Q_OK;
   }
-  if (path < 0 || path > 2) return fail(B2Q_EINVAL, "b2q_set_pipeline: path must be 0 (auto), 1 (ring), 2 (registers)");
+  if (path < 0 || path > 5 || path == 3 || path == 4)
+    return fail(B2Q_EINVAL, "b2q_set_pipeline: path must be 0 (auto), 1 (ring), 2 (registers), 5 (warp rows)");
   if (stages < 0 || stages == 1 || stages > 8) return fail(B2Q_EINVAL, "b2q_set_pipeline: stages must be 0 or 2..8");
   g_tune_path = path;
   g_tune_stages = stages;

@@ -36,6 +36,7 @@ namespace b2q {
 
 constexpr int kMaxThreads = 512;
 constexpr int kMaxColumns = 4;  // columns per launch; more are processed in groups of 4 (weights re-read per group)
+constexpr int kMaxStages = 8;   // ring stages at most (b2q_set_pipeline)
 constexpr long long kWaitLimit = 1LL << 20;  // bounded mbarrier polls (each try_wait also suspends in hardware)
 constexpr int kErrTimeout = 1;
 
@@ -486,7 +487,7 @@ __device__ __forceinline__ float warp_sum_scatter(float (&v)[V], int lane) {
 // __syncthreads. red is double-buffered so the next group's writes never race this group's reads.
 template <int R, int MC>
 __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, float (&acc)[R * MC], float* red,
-                                             int buf, int parity) {
+                                             int buf, int parity, int sum_warp = 0) {
   constexpr int V = R * MC;
   const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float s = warp_sum_scatter<V>(acc, lane);
@@ -494,12 +495,12 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
   for (int k = 0; k < V; ++k) acc[k] = 0.f;
   if ((lane & (32 / V - 1)) == 0) red[(buf * nwarps + warp) * V + lane / (32 / V)] = s;
   __syncthreads();
-  if ((int)threadIdx.x < V) {
-    const int r = threadIdx.x / MC, m = threadIdx.x - r * MC;
+  if (warp == sum_warp && lane < V) {  // the cross-warp sum of this group is done by warp sum_warp
+    const int r = lane / MC, m = lane - r * MC;
     const int64_t row = g * R + r;
     if (m < p.M && row < p.N) {
       float v = 0.f;
-      for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * V + threadIdx.x];
+      for (int w = 0; w < nwarps; ++w) v += red[(buf * nwarps + w) * V + lane];
       const int64_t idx = (int64_t)m * p.ldy + p.row0 + row;
       p.y[idx + (int64_t)blockIdx.y * p.y_split] = v;
       if (p.rx_peers != nullptr) {  // fused all-gather: (value, flag 1) into every other rank's receive buffer
@@ -852,13 +853,12 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
   const int64_t ngroups = g_end - g_begin;
   const uint32_t ring_addr = smem_addr(ring), bar_addr = smem_addr(bars);
-  uint64_t pol = 0;
+  const uint64_t pol = evict_first_policy();
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < S; ++s) mbar_init(bar_addr + 8 * s, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    pol = evict_first_policy();
     for (int64_t j = 0; j < min((int64_t)(S - 1), ngroups); ++j)
       issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
   }
@@ -878,12 +878,16 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
 
   // Stage bookkeeping without divisions: group j sits in stage j % S with mbarrier phase parity (j / S) & 1; the
   // producer refills stage (j - 1) % S with group j + S - 1.
+  // The per-group extra work -- issuing the next copy and the cross-warp sum -- rotates over the warps (issuer warp
+  // j mod W, summing warp (j + W/2) mod W), so that no warp is the one the others wait for at every barrier.
+  const int nwarps = blockDim.x >> 5;
+  int iw = 0, fw = nwarps >> 1;
   int buf = 0;
   int s = 0;            // stage of group j
   uint32_t parity = 0;  // phase parity of group j's stage
   int64_t j = 0;
   for (; j < ngroups; ++j) {
-    if (threadIdx.x == 0 && j + S - 1 < ngroups) {
+    if (threadIdx.x == 32 * iw && j + S - 1 < ngroups) {
       // stage (j-1)%S was released by the previous group's __syncthreads
       const int sn = (s == 0) ? S - 1 : s - 1;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -918,12 +922,14 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
       else
         compute_chunk<FMT, R, MC, false, false>(p, g, c, valid, w, dw, xc, acc);
     }
-    reduce_store<R, MC>(p, g, acc, red, buf, rx_parity);
+    reduce_store<R, MC>(p, g, acc, red, buf, rx_parity, fw);
     buf ^= 1;
     if (++s == S) {
       s = 0;
       parity ^= 1u;
     }
+    if (++iw == nwarps) iw = 0;
+    if (++fw == nwarps) fw = 0;
     if (s_abort) break;  // uniform: read after the reduction's __syncthreads
   }
   if (s_abort) {
@@ -937,10 +943,131 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   if (p.rx_peers != nullptr) allgather_collect(p, rx_parity);
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// Warp-rows kernel (one activation column): every warp owns whole weight rows, so a row's sum never leaves its warp.
+// ------------------------------------------------------------------------------------------------------------------
+// One CTA per SM of W warps. The f32 activations are quantized once per CTA into shared memory (the same permuted
+// layout and bytes as the ring path's prologue). Each warp streams its own groups of R rows through its own S-stage
+// ring (TMA bulk copies issued by the warp's lane 0, one mbarrier per stage) and takes its next group from a CTA-wide
+// counter, so the warps finish together. Lane l computes chunks l, l+32, ... of every row of a group; the group's R
+// sums are reduced inside the warp once per group, so the per-group cost is spread over all of a lane's chunks and the
+// loop has no CTA-wide barrier. The whole ring (W x S groups) is requested before the activation prologue.
+// Shared memory: [W][S] stages, [W][S] mbarriers, activations (K bytes), chunk sums (C ints), block scales.
+template <int FMT, int R>
+__global__ void __launch_bounds__(kMaxThreads, 1) gemv_warp_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_next;                                    // next unassigned group of this CTA
+  __shared__ int s_abort;
+  __shared__ int s_group[kMaxThreads / 32][kMaxStages];    // CTA-local group held by each warp's stage, -1: none
+  const int C = p.C, S = p.stages, W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
+  uint8_t* ring = smem;                                                                   // [W][S][stage_bytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * p.stage_bytes);    // [W][S]
+  uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((W * S + 1) & ~1));                   // 16-byte aligned
+  int* xsum = reinterpret_cast<int*>(xs + (size_t)p.K);
+  float* xscale = reinterpret_cast<float*>(xsum + C);
+
+  const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
+  const int n = (int)((p.groups * (blockIdx.x + 1)) / gridDim.x - g_begin);
+  const uint32_t my_ring = smem_addr(ring) + (uint32_t)(warp * S) * p.stage_bytes;
+  const uint32_t my_bars = smem_addr(bars) + (uint32_t)(warp * S) * 8u;
+  const uint64_t pol = evict_first_policy();
+
+  // Initial fills (weights only, so before the dependency wait): warp w's stage k gets group k*W + w.
+  if (lane == 0) {
+    for (int k = 0; k < S; ++k) mbar_init(my_bars + 8 * k, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int k = 0; k < S; ++k) {
+      const int gl = k * W + warp;
+      if (gl < n) issue_group<FMT, R>(p, g_begin + gl, my_ring + (uint32_t)k * p.stage_bytes, my_bars + 8 * k, pol);
+      s_group[warp][k] = gl < n ? gl : -1;
+    }
+  }
+  if (threadIdx.x == 0) {
+    s_next = S * W;
+    s_abort = 0;
+  }
+  pdl_wait_then_trigger();
+  stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (publishes the inits above)
+
+  int s = 0;
+  uint32_t parity = 0;
+  while (true) {
+    const int gl = *reinterpret_cast<volatile int*>(&s_group[warp][s]);
+    if (gl < 0) break;  // warp-uniform: groups are handed out in increasing order, so the rest are empty too
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(my_bars + 8 * s, parity, kWaitLimit));
+    if (!ok || *reinterpret_cast<volatile int*>(&s_abort)) {
+      if (lane == 0) {
+        *reinterpret_cast<volatile int*>(&s_abort) = 1;
+        if (!ok) atomicCAS(&g_device_error, 0, kErrTimeout);
+        // drain (bounded): this warp's copies still in flight, in ring order from stage s
+        for (int k = 0; k < S; ++k) {
+          const int st = (s + k) % S;
+          if (*reinterpret_cast<volatile int*>(&s_group[warp][st]) >= 0)
+            mbar_wait(my_bars + 8 * st, parity ^ (st < s ? 1u : 0u), kWaitLimit);
+        }
+      }
+      break;
+    }
+    const uint32_t stage = my_ring + (uint32_t)s * p.stage_bytes;
+    const int64_t g = g_begin + gl;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int i = 0; i < p.CPT; ++i) {
+      const int c = lane + 32 * i;
+      const bool valid = c < C;
+      const int blk = c >> Fmt<FMT>::kChunkShift;
+      uint4 w[R];
+      float dw[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (valid) {
+          w[r] = lds_v4(stage + r * qrow + (uint32_t)c * 16u);
+          dw[r] = f16_bits_to_f32(lds_u16(stage + R * qrow + r * srow + (uint32_t)blk * 2u));
+        } else {
+          w[r] = make_uint4(0u, 0u, 0u, 0u);
+          dw[r] = 0.f;
+        }
+      }
+      XChunk xc[1];
+      load_xchunk<FMT>(p, xs, xsum, xscale, 0, c, valid, xc[0]);
+      if (p.s)
+        compute_chunk<FMT, R, 1, false, true>(p, g, c, valid, w, dw, xc, acc);
+      else
+        compute_chunk<FMT, R, 1, false, false>(p, g, c, valid, w, dw, xc, acc);
+    }
+    const float v = warp_sum_scatter<R>(acc, lane);
+    if ((lane & (32 / R - 1)) == 0) {
+      const int64_t row = g * R + lane / (32 / R);
+      if (row < p.N) p.y[p.row0 + row] = v;
+    }
+    __syncwarp();
+    if (lane == 0) {  // every lane's reads of this stage are done: refill it with the CTA's next group
+      const int nx = atomicAdd(&s_next, 1);
+      if (nx < n && !*reinterpret_cast<volatile int*>(&s_abort)) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue_group<FMT, R>(p, g_begin + nx, stage, my_bars + 8 * s, pol);
+        s_group[warp][s] = nx;
+      } else {
+        s_group[warp][s] = -1;
+      }
+    }
+    __syncwarp();
+    if (++s == S) {
+      s = 0;
+      parity ^= 1u;
+    }
+  }
+}
+
 using KernelFn = void (*)(const GemvParams);
 
 // Kernel selection, one per translation unit (instantiations live in gemv_reg.cu / gemv_ring.cu).
 KernelFn reg_kernel_for(int fmt, bool bytes, int R, int MC, bool xreg);
 KernelFn ring_kernel_for(int fmt, int R, int MC, bool xreg);
+KernelFn warp_kernel_for(int fmt, int R);
 
 }  // namespace b2q

@@ -1,0 +1,23 @@
+// Instantiations of the warp-rows GEMV kernel (one activation column): Q4_0 and TQ2_0, R = 1, 2, 4 rows per group.
+#include "gemv_kernels.cuh"
+
+namespace b2q {
+
+KernelFn warp_kernel_for(int fmt, int R) {
+  if (fmt == 0) {
+    switch (R) {
+      case 1: return gemv_warp_kernel<0, 1>;
+      case 2: return gemv_warp_kernel<0, 2>;
+      case 4: return gemv_warp_kernel<0, 4>;
+    }
+  } else {
+    switch (R) {
+      case 1: return gemv_warp_kernel<1, 1>;
+      case 2: return gemv_warp_kernel<1, 2>;
+      case 4: return gemv_warp_kernel<1, 4>;
+    }
+  }
+  return nullptr;
+}
+
+}  // namespace b2q

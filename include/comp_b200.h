@@ -176,9 +176,13 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
 int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid);
 
 /* Benchmark/tuning hook (process-wide): weight-streaming path 0 = planner's choice, 1 = TMA bulk-copy ring in shared
- * memory, 2 = streaming loads into registers; stages = ring depth (0 = planner, else 2..8). path 3 / 4 turns the
- * programmatic dependent launch of the GEMV kernels on (default) / off (stages ignored). Results do not change. */
+ * memory, 2 = streaming loads into registers, 5 = warp-rows schedule (one column: each warp owns whole rows and has its
+ * own TMA ring); stages = ring depth (0 = planner, else 2..8). path 3 / 4 turns the programmatic dependent launch of
+ * the GEMV kernels on (default) / off (stages ignored). Results do not change (except the f32 summation order). */
 int b2q_set_pipeline(int path, int stages);
+
+/* Benchmark/tuning hook (process-wide): warps per CTA of the warp-rows schedule (4..16; 0 = planner's choice). */
+int b2q_set_warps(int warps);
 
 /* Reads (and with clear != 0 resets) the library's device error word: nonzero if a kernel's bounded wait on an
  * mbarrier gave up (the kernel then returned early; its outputs are invalid). Synchronizes with the device. */

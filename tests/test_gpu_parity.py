@@ -333,3 +333,42 @@ def _split_k_checks(cuda, fmt, n, k, m):
     # too small a workspace: no split, exactly the single-launch result
     tiny = torch.empty(16, dtype=torch.uint8, device=cuda)
     assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, workspace=tiny).cpu().numpy(), y1)
+
+
+@pytest.mark.parametrize("fmt,n,k", [("tq2_0", 998, 8192), ("q4_0", 1001, 4096), ("tq2_0", 8192, 28672),
+                                     ("q4_0", 301, 28672), ("tq2_0", 37, 2048), ("tq2_0", 5, 4096)])
+def test_warp_rows_path_matches_oracle(cuda, fmt, n, k):
+    """The warp-rows schedule (each warp owns whole rows, own TMA ring, one column) for several warps / rows-per-group
+    / ring-depth settings: exact int32 dots, Y within the rule of the exact reference, the same Y from the fused
+    quantizer prologue as from pre-quantized activations, repeatable; the bounded waits never fire."""
+    import ctypes
+
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, 1, 31, cuda)
+    xq, xd = host.quantize(fmt, tx)
+    oq, od = ref.quantize(fmt, x)
+    r, os_ = native.gemv(fmt, wq, ws, oq, od, k, want_s=True)
+    ran = 0
+    try:
+        for warps, rows, stages in ((0, 0, 0), (16, 1, 2), (8, 2, 3), (4, 4, 2), (12, 1, 4), (6, 2, 2), (4, 1, 2)):
+            _lib.call("b2q_set_warps", warps)
+            _lib.call("b2q_set_tuning", rows, 0, 0)
+            _lib.call("b2q_set_pipeline", 5, stages)
+            try:
+                y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+            except ValueError as e:  # a forced schedule larger than shared memory is refused, not run
+                assert "does not fit" in str(e), str(e)
+                continue
+            ran += 1
+            assert np.array_equal(s.cpu().numpy(), os_), (warps, rows, stages)
+            y = y.cpu().numpy()
+            assert ref.relerr(y, r) <= TOL, (warps, rows, stages)
+            assert _same_f32(host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2)[0].cpu().numpy(), y)
+            assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, split=False).cpu().numpy(), y)
+    finally:
+        _lib.call("b2q_set_warps", 0)
+        _lib.call("b2q_set_tuning", 0, 0, 0)
+        _lib.call("b2q_set_pipeline", 0, 0)
+    assert ran >= 2  # the planner's choice and at least one forced setting
+    code = ctypes.c_int(-1)
+    _lib.call("b2q_device_error", ctypes.byref(code), 1)
+    assert code.value == 0
