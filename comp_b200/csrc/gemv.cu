@@ -26,7 +26,11 @@
 //     -1 for TQ2_0) are folded in with per-chunk activation sums precomputed in the prologue. TQ2_0 blocks span 4
 //     chunks (4 adjacent threads), whose partial dots are combined with two xor-shuffles before scaling.
 //   * Per-group reduction: warp shuffles, then a cross-warp sum in shared memory in fixed warp order. The summation
-//     order of a row depends only on (K, T, CPT), so Y is bit-identical across paths, variants, R and grid size.
+//     order of a row depends only on (K, T, CPT), so Y is bit-identical across paths, variants, R and grid size. On
+//     the ring path the issuing of the next copy and the cross-warp sum rotate over the warps group by group.
+//   * Opt-in schedules: split-K over gridDim.y with an ordered combine kernel (b2q_set_splitk), and the warp-rows
+//     schedule for one column (b2q_set_pipeline path 5: each warp owns whole rows and streams them through its own
+//     TMA ring, activations in shared memory). Both are slower on the B200 layer shapes measured so far.
 #include <algorithm>
 #include <cmath>
 #include <mutex>
