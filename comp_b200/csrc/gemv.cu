@@ -118,7 +118,35 @@ struct Plan {
   size_t smem;
   bool ring;
   KernelFn fn;
+  int cluster = 1;  // CTAs per thread-block cluster sharing the activation prologue (ring path, one column)
 };
+
+// CTAs per cluster for the shared activation prologue: 0 = planner, 1 = off, 2 / 4 / 8 = forced. The planner uses
+// pairs whenever every CTA slot of the grid can still be filled by whole clusters: measured on B200 (same box), pairs
+// are 4-5% faster on the TQ2_0 config4 layers and up to 14% on the 8-GPU slices, where the prologue weighs most;
+// clusters of 4 or 8 lose on the layers with several CTAs per SM.
+static int g_tune_cluster = 0;
+
+// Clusters of `cs` CTAs of this kernel and launch shape that can be resident at once on the device.
+static int max_active_clusters(KernelFn fn, int threads, size_t smem, int cs) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cs);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute a[1];
+  a[0].id = cudaLaunchAttributeClusterDimension;
+  a[0].val.clusterDim.x = (unsigned)cs;
+  a[0].val.clusterDim.y = 1;
+  a[0].val.clusterDim.z = 1;
+  cfg.attrs = a;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void*)fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
 
 // Shared memory besides the ring: staged activations (none when they live in registers) and the reduction partials.
 static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T, bool xreg) {
@@ -169,13 +197,35 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
         stages = g_tune_stages > 0 ? g_tune_stages : 2;
         smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
       }
+      int cs = 1;
+      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster : (g_tune_cluster == 0 ? 2 : 1);
+      const size_t slot = fmt == 0 ? cluster_slot_bytes<0>(C) : cluster_slot_bytes<1>(C);
+      if (cs > 1 && smem + slot > (size_t)di.max_smem_optin && g_tune_cluster == 0) cs = 1;
+      if (cs > 1) smem += slot;
       if (smem > (size_t)di.max_smem_optin) continue;
       KernelFn fn = kernel_for(fmt, bytes, ring, R, MC, xreg);
-      const int occ = occupancy(fn, T, smem, di.max_smem_optin);
+      int occ = occupancy(fn, T, smem, di.max_smem_optin);
       if (occ < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed: %s", cudaGetErrorString(cudaGetLastError()));
+      if (cs > 1 && g_tune_cluster == 0) {  // pairs only if they cost no resident CTA
+        const size_t smem1 = smem - slot;
+        const int occ1 = occupancy(fn, T, smem1, di.max_smem_optin);
+        const int ncl = occ > 0 ? max_active_clusters(fn, T, smem, cs) : 0;
+        if (occ1 < 0) return fail(B2Q_ECUDA, "gemv: occupancy query failed");
+        if (occ < occ1 || (int64_t)ncl * cs < (int64_t)occ * di.sms) {
+          cs = 1;
+          smem = smem1;
+          occ = occ1;
+        }
+      }
       if (occ == 0) continue;
       int64_t grid = std::min<int64_t>(groups, std::max<int64_t>(1, (int64_t)occ * di.sms / splits));
       if (g_tune_grid > 0) grid = std::min<int64_t>(groups, g_tune_grid);
+      if (cs > 1) {  // whole clusters, no more than can be resident at once (a member may own no group)
+        const int ncl = max_active_clusters(fn, T, smem, cs);
+        if (ncl <= 0) continue;
+        grid = std::min<int64_t>(grid, (int64_t)ncl * cs / splits);
+        grid = std::max<int64_t>(cs, grid / cs * cs);
+      }
       // balance: groups per CTA is floor or ceil of groups/grid; efficiency = mean / max
       const int64_t per = (groups + grid - 1) / grid;
       const double balance = (double)groups / (double)(per * grid);
@@ -184,7 +234,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       const double score = balance + 0.2 * std::log2((double)R);
       if (score > best_score) {
         best_score = score;
-        best = Plan{R, T, CPT, (int)grid, stages, sb, smem, ring, fn};
+        best = Plan{R, T, CPT, (int)grid, stages, sb, smem, ring, fn, cs};
       }
     }
   }
@@ -383,17 +433,22 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.stages = pl.stages;
     p.stage_bytes = pl.stage_bytes;
     p.dense = (splits == 1 && a.ldwq == (int64_t)C * 16) ? 1 : 0;
+    p.cluster = pl.cluster;
     // programmatic stream serialization: the kernel's weight prefetch may overlap the preceding kernel's tail
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)pl.grid, (unsigned)splits);
     cfg.blockDim = dim3((unsigned)pl.T);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)pl.cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pl.cluster > 1 ? 2 : 1;
     cudaError_t le = cudaLaunchKernelEx(&cfg, pl.fn, p);
     if (le != cudaSuccess) {
       cudaGetLastError();
@@ -570,6 +625,13 @@ int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
 int b2q_set_splitk(int mode) {
   if (mode < 0 || mode > 16) return fail(B2Q_EINVAL, "b2q_set_splitk: mode must be 0 (off), 1 (auto) or 2..16");
   g_splitk_mode = mode;
+  return B2Q_OK;
+}
+
+int b2q_set_cluster(int ctas) {
+  if (ctas != 0 && ctas != 1 && ctas != 2 && ctas != 4 && ctas != 8)
+    return fail(B2Q_EINVAL, "b2q_set_cluster: ctas must be 0 (auto), 1 (off), 2, 4 or 8");
+  g_tune_cluster = ctas;
   return B2Q_OK;
 }
 

@@ -83,6 +83,7 @@ struct GemvParams {
   int stages;             // ring path: shared-memory stages
   uint32_t stage_bytes;   // ring path: bytes per stage (R rows of quants, then R rows of scales, 16-byte padded)
   int dense;              // ring path: ldwq == C*16, so a group's quant rows are one contiguous copy
+  int cluster;            // ring path, activations in registers: CTAs per cluster sharing the activation prologue
 };
 
 template <int FMT>
@@ -599,7 +600,8 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   for (int j = 0; j < 4; ++j) o.x[j] = make_uint4(0u, 0u, 0u, 0u);
   o.sum = 0;
   o.dx = 0.f;
-  const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr) && valid;
+  // the first CTA (with clusters: the first cluster's CTAs, each for the chunks it quantizes) writes XQ/XD out
+  const bool writer = (blockIdx.x < (unsigned)max(1, p.cluster)) && (p.xq_out != nullptr) && valid;
   if (p.x_f32 == nullptr) {
     if (!valid) return;
     if (FMT == 0) {
@@ -730,6 +732,76 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   }
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// Cluster-shared activation prologue: the CTAs of a thread-block cluster split the activation chunks, each quantizes
+// its share once (the same load_x_direct arithmetic) and stores the q8 chunk into every member's shared memory
+// (distributed shared memory stores, no multicast loads), then every thread reads its own chunk back into registers.
+// Per SM this loads and quantizes 1/cluster of the activations instead of all of them.
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(local_addr), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared-memory bytes of the chunk slots: [kFields][C] 16-byte q8 pieces, then [C] (sum, scale bits).
+template <int FMT>
+__host__ __device__ constexpr uint32_t cluster_slot_bytes(int C) {
+  return (uint32_t)C * (16u * Fmt<FMT>::kFields + 8u);
+}
+
+template <int FMT>
+__device__ __forceinline__ void cluster_share_x(const GemvParams& p, uint32_t slots, XChunk& xr) {
+  const int C = p.C, cs = p.cluster;
+  const int per = (((C + cs - 1) / cs) + 31) & ~31;  // chunks per member, in whole warps (the quad shuffles)
+  const int c = (int)threadIdx.x;
+  const int wfirst = c & ~31;
+  if (wfirst < C && wfirst / per == (int)cluster_ctarank()) {  // warp-uniform
+    XChunk o;
+    load_x_direct<FMT>(p, c, c < C, o);
+    if (c < C) {
+      for (int q = 0; q < cs; ++q) {
+#pragma unroll
+        for (int j = 0; j < Fmt<FMT>::kFields; ++j)
+          st_cluster_v4(cluster_map(slots + (uint32_t)(j * C + c) * 16u, (uint32_t)q), o.x[j]);
+        st_cluster_v2(cluster_map(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u, (uint32_t)q),
+                      (uint32_t)o.sum, __float_as_uint(o.dx));
+      }
+    }
+  }
+  cluster_sync_all();  // every member's slots are complete (release / acquire at cluster scope)
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xr.x[j] = make_uint4(0u, 0u, 0u, 0u);
+  xr.sum = 0;
+  xr.dx = 0.f;
+  if (c < C) {
+#pragma unroll
+    for (int j = 0; j < Fmt<FMT>::kFields; ++j) xr.x[j] = lds_v4(slots + (uint32_t)(j * C + c) * 16u);
+    uint32_t a, b;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                 : "=r"(a), "=r"(b)
+                 : "r"(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u));
+    xr.sum = (int)a;
+    xr.dx = __uint_as_float(b);
+  }
+}
+
 template <int FMT, int MC, bool XREG>
 __device__ __forceinline__ void get_x(const GemvParams& p, const uint8_t* xs, const int* xsum, const float* xscale,
                                       const XChunk& xr, int c, bool valid, XChunk (&xc)[MC]) {
@@ -847,7 +919,8 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((S + 1) & ~1));               // 16-byte aligned
   int* xsum = reinterpret_cast<int*>(xs + (size_t)Mx * p.K);
   float* xscale = reinterpret_cast<float*>(xsum + Mx * C);
-  float* red = xscale + Mx * nblk;
+  uint8_t* slots = reinterpret_cast<uint8_t*>(xscale + Mx * nblk);  // XREG with clusters: shared chunk slots
+  float* red = reinterpret_cast<float*>(slots + ((XREG && p.cluster > 1) ? cluster_slot_bytes<FMT>(C) : 0u));
 
   const int64_t g_begin = (p.groups * blockIdx.x) / gridDim.x;
   const int64_t g_end = (p.groups * (blockIdx.x + 1)) / gridDim.x;
@@ -866,7 +939,10 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   const int rx_parity = call_parity(p);
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
   if (XREG) {
-    load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+    if (p.cluster > 1)
+      cluster_share_x<FMT>(p, smem_addr(slots), xr);
+    else
+      load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
     __syncthreads();  // publishes the barrier init and s_abort
   } else {
     stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)

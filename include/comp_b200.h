@@ -184,6 +184,11 @@ int b2q_set_pipeline(int path, int stages);
 /* Benchmark/tuning hook (process-wide): warps per CTA of the warp-rows schedule (4..16; 0 = planner's choice). */
 int b2q_set_warps(int warps);
 
+/* Benchmark/tuning hook (process-wide): ring path with one column -- the CTAs of a thread-block cluster of this size
+ * (2, 4 or 8) split the activation prologue, each quantizing its share once and storing it into every member's shared
+ * memory; 1 = off, 0 = planner's choice. Results do not change (identical bytes, identical summation order). */
+int b2q_set_cluster(int ctas);
+
 /* Reads (and with clear != 0 resets) the library's device error word: nonzero if a kernel's bounded wait on an
  * mbarrier gave up (the kernel then returned early; its outputs are invalid). Synchronizes with the device. */
 int b2q_device_error(int* code, int clear);

@@ -372,3 +372,30 @@ def test_warp_rows_path_matches_oracle(cuda, fmt, n, k):
     code = ctypes.c_int(-1)
     _lib.call("b2q_device_error", ctypes.byref(code), 1)
     assert code.value == 0
+
+
+@pytest.mark.parametrize("fmt,n,k", [("tq2_0", 998, 8192), ("tq2_0", 8192, 28672), ("q4_0", 1001, 4096),
+                                     ("q4_0", 300, 28672), ("tq2_0", 5, 4096), ("tq2_0", 64, 14336)])
+def test_cluster_shared_prologue_identical(cuda, fmt, n, k):
+    """No cluster, and clusters of 2, 4 and 8 CTAs splitting the fused activation prologue (each member quantizes its share and stores
+    it into every member's shared memory): the same quantized bytes written out, bit-identical Y, the bounded waits
+    never fire -- also when the layer has fewer row groups than the cluster has members."""
+    import ctypes
+
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, 1, 41, cuda)
+    y0, q0, d0 = host.quant_gemv(fmt, twq, tws, tx, n, k, return_act=True, split=False)
+    oq, od = ref.quantize(fmt, x)
+    assert np.array_equal(q0.cpu().numpy(), oq) and _same_f32(d0.cpu().numpy(), od)
+    y0 = y0.cpu().numpy()
+    try:
+        for cs in (1, 2, 4, 8):
+            _lib.call("b2q_set_cluster", cs)
+            y, q, d = host.quant_gemv(fmt, twq, tws, tx, n, k, return_act=True, split=False)
+            assert np.array_equal(q.cpu().numpy(), oq), cs
+            assert _same_f32(d.cpu().numpy(), od), cs
+            assert _same_f32(y.cpu().numpy(), y0), cs
+    finally:
+        _lib.call("b2q_set_cluster", 0)
+    code = ctypes.c_int(-1)
+    _lib.call("b2q_device_error", ctypes.byref(code), 1)
+    assert code.value == 0
