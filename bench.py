@@ -451,17 +451,24 @@ def main():
     e2e_steps = 0 if args.no_e2e else (args.e2e_steps or args.steps)
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
 
+    y_dev = [torch.empty((m, L.n), dtype=torch.float32, device=dev) for L in layers] if world == 1 else None
+
     def e2e_step():
+        # every step: the layers' inputs from pinned host memory, the GEMVs back to back through the public API (so
+        # each one's weight stream can start while the previous one finishes), every layer's output back to pinned
+        # host memory, then the host waits for all of it
+        xs = [L.x_host.to(dev, non_blocking=True) for L in layers]
+        ys = []
         for i, L in enumerate(layers):
-            x = L.x_host.to(dev, non_blocking=True)
             if world == 1:
                 wq, ws = L.w[0]
-                xq, xd = host.quantize(L.fmt, x)
-                y, _ = host.gemv(L.fmt, wq, ws, xq, xd, L.n, L.k, mode=2)
+                ys.append(host.quant_gemv(L.fmt, wq, ws, xs[i], L.n, L.k, out=y_dev[i]))
             else:
-                y = L.objs[0](x)
+                # the fused exchange reuses its output buffer on the layer's next call
+                ys.append(L.objs[0](xs[i]) if i + 1 == len(layers) else L.objs[0](xs[i]).clone())
+        for i, y in enumerate(ys):
             y_host[i].copy_(y, non_blocking=True)
-        stream.synchronize()  # the step's result is read on the host
+        stream.synchronize()  # the step's results are read on the host
 
     e2e_gbs = None
     if e2e_steps:
@@ -511,7 +518,7 @@ def main():
             "data": "synthetic (BASELINE distributions, seeded, random-init weights)",
             "config": {"workload": args.workload, "layers": [f"{f} {n}x{k} ({nm})" for f, n, k, nm in layers_def],
                        "m": m, "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
-                       "exchange": {None: None, "p2p": "fused P2P stores + flag barrier in the GEMV kernel",
+                       "exchange": {None: None, "p2p": "fused all-gather: (value, flag) peer stores from the GEMV epilogue",
                                     "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
                        "graph": world > 1, "pdl": args.pdl,
                        "l2": f"weights {per_gpu / 2**20:.0f} MiB per GPU x {copies} rotating copies >= 4x L2 "
@@ -525,7 +532,7 @@ def main():
                          "us_per_launch": round(dom_ms * 1e3, 3), "algorithmic_bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "api": "comp_b200.host.quantize + gemv" if world == 1 else
+                    "steps": e2e_steps, "api": "comp_b200.host.quant_gemv (fused quantize + GEMV, one launch per layer)" if world == 1 else
                     f"comp_b200.dist.RowShardedGemv ({exchange_name})"},
             "gpu_launches": launches,
             "clocks": cs,

@@ -131,7 +131,7 @@ class RowShardedGemv:
         if m > self.max_m:
             raise ValueError(f"p2p exchange: M={m} > max_m={self.max_m}")
         self._calls += 1
-        with torch.cuda.device(self.dev):
+        with host._on(self.dev):
             _lib.call("b2q_gemv_allgather", host.FMT_ID[self.fmt], self.wq.data_ptr(), self.wq.stride(0),
                       self.ws.data_ptr(), x.data_ptr(), x.stride(0), self.y.data_ptr(), self.rx.data_ptr(),
                       self._rxpeers.data_ptr(), self.rx_stride, self.done.data_ptr(), self.status.data_ptr(),

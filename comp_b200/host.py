@@ -9,6 +9,8 @@ schedule is planned from (N, K, M) by the library, and results do not depend on 
 0 = byte-wise unpack, 1 or 2 = packed-word dp4a; all variants give identical int32 block dots and identical Y.
 """
 
+import contextlib
+
 import numpy as np
 import torch
 
@@ -133,6 +135,11 @@ def _stream(dev):
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def _on(dev):
+    """Context making `dev` the current device (a no-op when it already is: the common single-GPU case)."""
+    return contextlib.nullcontext() if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
+
+
 def quantize(fmt, x, bb=4):
     """f32 [M][K] CUDA tensor -> (XQ int8 [M][K], XD f32 [M][K/block]) with the q8_0 / q8_K quantizer of `fmt`'s
     activation format (src/komp/host.py:63-73). Bytes equal ggml's reference quantizers."""
@@ -148,7 +155,7 @@ def quantize(fmt, x, bb=4):
     x = _rows_aligned(x)
     xq = torch.empty((m, k), dtype=torch.int8, device=dev)
     xd = torch.empty((m, k // blk), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         if act == "q8_0":
             _lib.call("b2q_quant_q8_0", x.data_ptr(), x.stride(0), xq.data_ptr(), xd.data_ptr(), m, k, _stream(dev))
         else:
@@ -167,7 +174,7 @@ def quantize_q8_K_bsums(x):
     xq = torch.empty((m, k), dtype=torch.int8, device=dev)
     xd = torch.empty((m, k // 256), dtype=torch.float32, device=dev)
     bs = torch.empty((m, k // 256, 16), dtype=torch.int16, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("b2q_quant_q8_K", x.data_ptr(), x.stride(0), xq.data_ptr(), xd.data_ptr(), bs.data_ptr(), m, k,
                   _stream(dev))
     return xq, xd, bs
@@ -205,7 +212,7 @@ def gemv(fmt, wq, ws, xq, xd, n, k, block_n=32, nb=4, mode=0, num_warps=4, store
     y = torch.empty((m, n), dtype=torch.float32, device=dev)
     s = torch.empty((m, n, k // f["block"]), dtype=torch.int32, device=dev) if store_s else None
     name = "b2q_gemv_q4_0" if fmt == "q4_0" else "b2q_gemv_tq2_0"
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call(name, wq.data_ptr(), wq.stride(0), ws.data_ptr(), xq.data_ptr(), xd.data_ptr(), y.data_ptr(),
                   s.data_ptr() if store_s else None, n, k, m, mode, _stream(dev))
     return y, s
@@ -216,8 +223,11 @@ def workspace_size(fmt, n, k, m):
     return int(_lib.load().b2q_workspace_size(FMT_ID[fmt], n, k, m))
 
 
-def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=None):
+def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=None, out=None):
     """Fused quantize + gemv: f32 x [M][K] -> Y f32 [M][N] (and (XQ, XD) when return_act).
+
+    out: optional preallocated contiguous f32 [M][N] CUDA tensor for Y (returned), e.g. to avoid an allocation per
+    decode step.
 
     split=False: one launch; Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule,
     same f32 order). split=True (default): tall-K layers run the split-K schedule with a workspace (allocated here
@@ -230,7 +240,12 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
         raise ValueError(f"quant_gemv: x must be float32 [M][{k}], got {x.dtype} {tuple(x.shape)}")
     m = x.shape[0]
     x = _rows_aligned(x)
-    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    if out is None:
+        y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    else:
+        if out.dtype != torch.float32 or tuple(out.shape) != (m, n) or out.device != dev or not out.is_contiguous():
+            raise ValueError(f"quant_gemv: out must be a contiguous float32 [{m}][{n}] tensor on {dev}")
+        y = out
     xq = xd = None
     if return_act:
         xq = torch.empty((m, k), dtype=torch.int8, device=dev)
@@ -238,7 +253,7 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
     wsb = workspace_size(fmt, n, k, m) if split else 0
     if wsb and workspace is None:
         workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("b2q_quant_gemv_ws", FMT_ID[fmt], wq.data_ptr(), wq.stride(0), ws.data_ptr(), x.data_ptr(),
                   x.stride(0), xq.data_ptr() if return_act else None, xd.data_ptr() if return_act else None,
                   y.data_ptr(), n, k, m, workspace.data_ptr() if wsb else None,

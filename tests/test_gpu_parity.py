@@ -399,3 +399,18 @@ def test_cluster_shared_prologue_identical(cuda, fmt, n, k):
     code = ctypes.c_int(-1)
     _lib.call("b2q_device_error", ctypes.byref(code), 1)
     assert code.value == 0
+
+
+def test_quant_gemv_into_given_output(cuda):
+    """quant_gemv(out=...) writes Y into the caller's buffer (no allocation), identical to the allocating call; a
+    buffer of the wrong shape, dtype or device is refused before any launch."""
+    wq, ws, x, twq, tws, tx = _layer("tq2_0", 300, 4096, 2, 51, cuda)
+    want = host.quant_gemv("tq2_0", twq, tws, tx, 300, 4096).cpu().numpy()
+    out = torch.full((2, 300), float("nan"), device=cuda)
+    got = host.quant_gemv("tq2_0", twq, tws, tx, 300, 4096, out=out)
+    assert got.data_ptr() == out.data_ptr()
+    assert _same_f32(out.cpu().numpy(), want)
+    for bad in (torch.empty((2, 299), device=cuda), torch.empty((2, 300), dtype=torch.float64, device=cuda),
+                torch.empty((300, 2), device=cuda).t()):
+        with pytest.raises(ValueError):
+            host.quant_gemv("tq2_0", twq, tws, tx, 300, 4096, out=bad)
