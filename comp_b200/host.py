@@ -57,6 +57,31 @@ def split_q4_0(W, n, k):
     return split("q4_0", W, n, k)
 
 
+def split_device(fmt, blocks, n, k, ldwq=None):
+    """split() on the GPU: ggml blocks as a CUDA uint8 tensor (n rows of k values, the bytes as stored in a GGUF
+    file) -> (WQ uint8 [n][ldwq], WS int16 [n][k/block]) CUDA tensors, byte-identical to split(). ldwq defaults to the
+    quant bytes per row (a multiple of 16 for every K the GEMVs take)."""
+    f = _fmt(fmt)
+    if k % f["block"]:
+        raise ValueError(f"k={k} is not a multiple of the {fmt} block ({f['block']})")
+    dev = _need_cuda("split_device", blocks)
+    nb = k // f["block"]
+    if blocks.dtype != torch.uint8 or blocks.numel() != n * nb * f["nbytes"]:
+        raise ValueError(f"split_device: expected {n * nb * f['nbytes']} uint8 bytes of {fmt} blocks, got "
+                         f"{blocks.dtype} x {blocks.numel()}")
+    blocks = blocks.reshape(-1)
+    if not blocks.is_contiguous() or blocks.data_ptr() % 16:
+        blocks = blocks.clone()
+    qb = nb * f["qbytes"]
+    ldwq = qb if ldwq is None else ldwq
+    wq = torch.empty((n, ldwq), dtype=torch.uint8, device=dev)
+    ws = torch.empty((n, nb), dtype=torch.int16, device=dev)
+    with _on(dev):
+        _lib.call("b2q_split_blocks", FMT_ID[fmt], blocks.data_ptr(), n, k, wq.data_ptr(), ldwq, ws.data_ptr(),
+                  _stream(dev))
+    return (wq if ldwq == qb else wq[:, :qb]), ws
+
+
 def tq2_0_qplane(W, nblk):
     """ggml tq2_0 blocks -> quant plane uint8 [nblk][64] (the f16 scale at byte 64 goes to the scale plane)."""
     return np.frombuffer(W, dtype=np.uint8).reshape(nblk, 66)[:, :64].copy()

@@ -133,6 +133,16 @@ int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
                       size_t workspace_bytes, b2q_stream_t stream);
 
 /*
+ * ggml blocks -> split planes on the device (model load path). blocks: n rows of k values as ggml Q4_0 (fmt 0,
+ * 18-byte blocks: f16 d, 16 quant bytes) or TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d), row-major,
+ * 16-byte aligned device memory (a GGUF tensor's bytes as stored). Writes WQ [n][ldwq] (ldwq >= quant bytes per row,
+ * multiple of 16) and WS [n][k/blk] int16 (f16 bits), exactly host.split's planes. Replaces the host-side numpy cut
+ * of src/komp/host.py:16-22 for weights already on the GPU.
+ */
+int b2q_split_blocks(int fmt, const uint8_t* blocks, int64_t n, int64_t k, uint8_t* wq, int64_t ldwq, int16_t* ws,
+                     b2q_stream_t stream);
+
+/*
  * Split-K fused quantize + GEMV that allocates nothing, for callers that cannot allocate device memory (an inference
  * engine that reserves all GPU memory at start-up, or an FFI caller without a device allocator of its own). It is
  * b2q_quant_gemv_ws with exactly `splits` K splits (2..16, dividing the blocks of a row) whose partial sums live in

@@ -414,3 +414,51 @@ def test_quant_gemv_into_given_output(cuda):
                 torch.empty((300, 2), device=cuda).t()):
         with pytest.raises(ValueError):
             host.quant_gemv("tq2_0", twq, tws, tx, 300, 4096, out=bad)
+
+
+@pytest.mark.parametrize("fmt,n,k", [("q4_0", 37, 416), ("tq2_0", 5, 768), ("q4_0", 4100, 4096), ("tq2_0", 999, 8192),
+                                     ("q4_0", 1, 32), ("tq2_0", 3, 28672)])
+def test_split_device_matches_host_split(cuda, fmt, n, k):
+    """The on-device cut of ggml blocks into WQ / WS (b2q_split_blocks) is byte-identical to host.split, also with a
+    padded row stride, an unaligned source and a partial last CTA."""
+    rng = np.random.default_rng(71)
+    raw = ref.weight_blocks(fmt, rng, n, k, extreme=(n % 2 == 1))
+    wq, ws = host.split(fmt, raw, n, k)
+    blocks = torch.from_numpy(np.frombuffer(raw, dtype=np.uint8).copy()).to(cuda)
+    dwq, dws = host.split_device(fmt, blocks, n, k)
+    assert np.array_equal(dwq.cpu().numpy(), wq) and np.array_equal(dws.cpu().numpy(), ws)
+    pad = wq.shape[1] + 16
+    dwq2, _ = host.split_device(fmt, blocks, n, k, ldwq=pad)
+    assert dwq2.stride(0) == pad and np.array_equal(dwq2.cpu().numpy(), wq)
+    shifted = torch.empty(blocks.numel() + 2, dtype=torch.uint8, device=cuda)[2:]  # 2-byte offset source
+    shifted.copy_(blocks)
+    dwq3, dws3 = host.split_device(fmt, shifted, n, k)
+    assert np.array_equal(dwq3.cpu().numpy(), wq) and np.array_equal(dws3.cpu().numpy(), ws)
+
+
+def test_gguf_file_to_gemv_matches_oracle(cuda, tmp_path):
+    """A GGUF file's Q4_0 and TQ2_0 tensors, uploaded as stored and split on the GPU, give the oracle's GEMV."""
+    gguf = pytest.importorskip("gguf")
+    from comp_b200 import gguf_io
+
+    rng = np.random.default_rng(72)
+    specs = [("blk.0.attn_output.weight", "q4_0", 300, 4096), ("blk.0.ffn_up.weight", "tq2_0", 200, 8192)]
+    w = gguf.GGUFWriter(str(tmp_path / "m.gguf"), "llama")
+    raws = {}
+    for name, fmt, n, k in specs:
+        raws[name] = ref.weight_blocks(fmt, rng, n, k)
+        w.add_tensor(name, np.frombuffer(raws[name], dtype=np.uint8).reshape(n, -1),
+                     raw_dtype=getattr(gguf.GGMLQuantizationType, fmt.upper()))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    for name, fmt, n, k in specs:
+        f, twq, tws, rn, rk = gguf_io.load_split(str(tmp_path / "m.gguf"), name, device=cuda)
+        assert (f, rn, rk) == (fmt, n, k)
+        x = rng.standard_normal((2, k)).astype(np.float32)
+        y = host.quant_gemv(fmt, twq, tws, _t(x, cuda), n, k).cpu().numpy()
+        wq, ws = host.split(fmt, raws[name], n, k)
+        oq, od = ref.quantize(fmt, x)
+        r, _ = native.gemv(fmt, wq, ws, oq, od, k)
+        assert ref.relerr(y, r) <= TOL
