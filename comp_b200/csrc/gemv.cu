@@ -361,6 +361,19 @@ struct LaunchArgs {
   int force_splits;  // > 1: run exactly this many K splits (validated by the caller)
 };
 
+// Tensor-core GEMM for many columns (gemm_tc.cu): pre-quantized activations, M >= the threshold below.
+int launch_gemm_tc(const GemvParams& base, int fmt, cudaStream_t stream, bool pdl);
+
+// Columns from which a layer runs on the tensor-core GEMM (0 = never). Below it the GEMV kernels, which re-read the
+// weights per group of 4 columns, are the better fit.
+static int g_tc_min_m = 8;
+
+// Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD.
+static size_t tc_act_bytes(int fmt, int64_t K, int64_t M) {
+  const int64_t nblk = K / (fmt == 0 ? 32 : 256);
+  return ((size_t)M * (size_t)K + 15) / 16 * 16 + (size_t)M * (size_t)nblk * sizeof(float);
+}
+
 static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   if (a.N == 0 || a.M == 0 || a.K == 0) {
     // empty reductions: Y = 0 (K == 0); nothing to do for N == 0 or M == 0
@@ -372,6 +385,52 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   }
   const int blk = a.fmt == 0 ? 32 : 256;
   const int64_t nblk = a.K / blk;
+  // many columns: the tensor-core GEMM, on pre-quantized activations (a fused call quantizes first into the caller's
+  // XQ / XD outputs or the workspace; without either it stays on the GEMV path)
+  // (only when its CTAs -- 128 rows x up to 128 columns each -- fill the GPU: on narrow layers the GEMV path is faster)
+  DeviceInfo tc_di;
+  const int tc_nt = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+  const bool tc_wide = device_info(&tc_di) == B2Q_OK &&
+                       ((a.N + 127) / 128) * ((a.M + tc_nt - 1) / tc_nt) >= (int64_t)tc_di.sms;
+  if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || g_tc_min_m < 8) && !a.rx_peers && aligned(a.wq, 16) &&
+      a.ldwq % 16 == 0) {
+    const int8_t* xq = a.xq;
+    const float* xd = a.xd;
+    if (a.x_f32) {
+      int8_t* qo = a.xq_out;
+      float* dq = a.xd_out;
+      if (!qo && a.workspace && a.workspace_bytes >= tc_act_bytes(a.fmt, a.K, a.M)) {
+        qo = reinterpret_cast<int8_t*>(a.workspace);
+        dq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + ((size_t)a.M * a.K + 15) / 16 * 16);
+      }
+      if (qo) {
+        const int rc = a.fmt == 0 ? b2q_quant_q8_0(a.x_f32, a.ldx, qo, dq, a.M, a.K, stream)
+                                  : b2q_quant_q8_K(a.x_f32, a.ldx, qo, dq, nullptr, a.M, a.K, stream);
+        if (rc) return rc;
+        xq = qo;
+        xd = dq;
+      }
+    }
+    if (xq) {
+      GemvParams p{};
+      p.wq = a.wq;
+      p.ldwq = a.ldwq;
+      p.ws = a.ws;
+      p.ldws = nblk;
+      p.xq = xq;
+      p.ldxq = a.K;
+      p.xd = xd;
+      p.ldxd = nblk;
+      p.y = a.y;
+      p.ldy = a.ldy;
+      p.row0 = a.row0;
+      p.s = a.s;
+      p.N = a.N;
+      p.K = a.K;
+      p.M = (int)a.M;
+      return launch_gemm_tc(p, a.fmt, stream, g_pdl != 0);
+    }
+  }
   // split-K when a workspace for the partial sums is given and the layer is tall (one column group only)
   int splits = 1;
   if (a.workspace && !a.s && !a.rx_peers && a.M <= kMaxColumns) {
@@ -559,6 +618,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if ((fmt != 0 && fmt != 1) || N <= 0 || K <= 0 || M <= 0 || (K % (fmt == 0 ? 32 : 256))) return 0;
+  if (g_tc_min_m > 0 && M >= g_tc_min_m) return tc_act_bytes(fmt, K, M);  // the GEMV path ignores it
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
 }
@@ -625,6 +685,12 @@ int b2q_set_tuning(int rows_per_group, int chunks_per_thread, int grid) {
 int b2q_set_splitk(int mode) {
   if (mode < 0 || mode > 16) return fail(B2Q_EINVAL, "b2q_set_splitk: mode must be 0 (off), 1 (auto) or 2..16");
   g_splitk_mode = mode;
+  return B2Q_OK;
+}
+
+int b2q_set_gemm_min_columns(int m) {
+  if (m < 0) return fail(B2Q_EINVAL, "b2q_set_gemm_min_columns: m must be >= 0 (0 = never)");
+  g_tc_min_m = m;
   return B2Q_OK;
 }
 

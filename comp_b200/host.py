@@ -254,8 +254,8 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
     out: optional preallocated contiguous f32 [M][N] CUDA tensor for Y (returned), e.g. to avoid an allocation per
     decode step.
 
-    split=False: one launch; Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule,
-    same f32 order). split=True (default): tall-K layers run the split-K schedule with a workspace (allocated here
+    split=False: Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule, same f32
+    order); one launch up to 4 columns, with more the quantizer and the tensor-core GEMM. split=True (default): tall-K layers run the split-K schedule with a workspace (allocated here
     unless given; a CUDA byte tensor of at least workspace_size(...) bytes); Y then differs from the single-launch
     result only by f32 rounding of the sum order, and is deterministic."""
     f = _fmt(fmt)
@@ -275,7 +275,9 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
     if return_act:
         xq = torch.empty((m, k), dtype=torch.int8, device=dev)
         xd = torch.empty((m, k // f["block"]), dtype=torch.float32, device=dev)
-    wsb = workspace_size(fmt, n, k, m) if split else 0
+    # the workspace enables split-K (split=True, at most 4 columns) or, with more columns, the scratch for the
+    # quantized activations of the tensor-core GEMM
+    wsb = workspace_size(fmt, n, k, m) if (split or m > 4) else 0
     if wsb and workspace is None:
         workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
     with _on(dev):

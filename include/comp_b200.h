@@ -194,6 +194,12 @@ int b2q_set_pipeline(int path, int stages);
 /* Benchmark/tuning hook (process-wide): warps per CTA of the warp-rows schedule (4..16; 0 = planner's choice). */
 int b2q_set_warps(int warps);
 
+/* Tuning hook (process-wide): layers with at least m activation columns run on the tensor-core GEMM (tcgen05 int8
+ * MMA, weights read once for all columns; default 8, 0 = never). Fused calls then quantize first into the caller's
+ * XQ / XD outputs or the workspace (b2q_workspace_size reports its size); int32 block dots are unchanged, Y differs
+ * from the GEMV path only by the f32 summation order. */
+int b2q_set_gemm_min_columns(int m);
+
 /* Benchmark/tuning hook (process-wide): ring path with one column -- the CTAs of a thread-block cluster of this size
  * (2, 4 or 8) split the activation prologue, each quantizing its share once and storing it into every member's shared
  * memory; 1 = off, 0 = planner's choice. Results do not change (identical bytes, identical summation order). */

@@ -462,3 +462,54 @@ def test_gguf_file_to_gemv_matches_oracle(cuda, tmp_path):
         oq, od = ref.quantize(fmt, x)
         r, _ = native.gemv(fmt, wq, ws, oq, od, k)
         assert ref.relerr(y, r) <= TOL
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 300, 4096, 8), ("q4_0", 1000, 4096, 16), ("q4_0", 128, 14336, 33),
+                                       ("tq2_0", 257, 8192, 8), ("tq2_0", 999, 4096, 64), ("tq2_0", 128, 2048, 130),
+                                       ("q4_0", 4100, 4096, 100), ("q4_0", 37, 416, 9), ("tq2_0", 5, 768, 12)])
+def test_tensor_core_gemm_matches_oracle(cuda, fmt, n, k, m):
+    """Many columns run on the tcgen05 int8 GEMM (weights read once for all columns): exact int32 block dots, Y within
+    the rule of the exact reference, the fused call (quantizer + GEMM, 2 launches) equal to the separate calls, and
+    repeatable; also below the threshold when forced (padded columns) and with the byte-wise variant."""
+    import ctypes
+
+    _lib.call("b2q_set_gemm_min_columns", 1)  # also on layers too narrow to fill the GPU (the planner's rule)
+    try:
+        _tensor_core_checks(cuda, fmt, n, k, m)
+    finally:
+        _lib.call("b2q_set_gemm_min_columns", 8)
+    code = ctypes.c_int(-1)
+    _lib.call("b2q_device_error", ctypes.byref(code), 1)
+    assert code.value == 0
+
+
+def _tensor_core_checks(cuda, fmt, n, k, m):
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 81, cuda)
+    xq, xd = host.quantize(fmt, tx)
+    oq, od = ref.quantize(fmt, x)
+    assert np.array_equal(xq.cpu().numpy(), oq) and _same_f32(xd.cpu().numpy(), od)
+    r, os_ = native.gemv(fmt, wq, ws, oq, od, k, want_s=True)
+    y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+    assert np.array_equal(s.cpu().numpy(), os_)
+    y = y.cpu().numpy()
+    assert ref.relerr(y, r) <= TOL
+    assert _same_f32(host.gemv(fmt, twq, tws, xq, xd, n, k, mode=0)[0].cpu().numpy(), y)
+    before = _lib.launch_count()
+    yf = host.quant_gemv(fmt, twq, tws, tx, n, k)
+    assert _lib.launch_count() - before == 2
+    assert _same_f32(yf.cpu().numpy(), y)
+    assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, split=False).cpu().numpy(), y)
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 300, 4096, 1), ("tq2_0", 130, 8192, 3), ("q4_0", 64, 4096, 5)])
+def test_tensor_core_gemm_forced_on_few_columns(cuda, fmt, n, k, m):
+    wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 82, cuda)
+    xq, xd = host.quantize(fmt, tx)
+    r, os_ = native.gemv(fmt, wq, ws, xq.cpu().numpy(), xd.cpu().numpy(), k, want_s=True)
+    _lib.call("b2q_set_gemm_min_columns", 1)
+    try:
+        y, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+    finally:
+        _lib.call("b2q_set_gemm_min_columns", 8)
+    assert np.array_equal(s.cpu().numpy(), os_)
+    assert ref.relerr(y.cpu().numpy(), r) <= TOL
