@@ -83,19 +83,39 @@ __device__ __forceinline__ void gemm_tc_finish(const GemvParams& p, uint32_t tme
   tc::fence_before();
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Blocks fetched ahead (raw weights and activation tiles) per format and column tile, within shared memory.
+template <int FMT, int NT>
+struct TcCfg {
+  static constexpr int KS = FMT == 0 ? 1 : 8;        // MMAs (32-value k-steps) per weight block
+  static constexpr int QU = FMT == 0 ? 1 : 4;        // 16-byte units of a row's packed block
+  static constexpr int P = FMT == 0 ? 8 : (NT <= 64 ? 4 : 2);
+  static constexpr int ATILE = 128 * 32, BTILE = NT * 32;
+  static constexpr size_t RAW = (size_t)P * QU * 128 * 16;   // [P][QU][128 threads] 16-byte units
+  static constexpr size_t ATILES = (size_t)2 * KS * ATILE;   // [2][KS] unpacked weight tiles
+  static constexpr size_t BRING = (size_t)P * KS * BTILE;    // [P][KS] activation tiles
+  static constexpr size_t SMEM = RAW + ATILES + BRING;
+};
+
 // FMT 0: Q4_0 (1 MMA per block), FMT 1: TQ2_0 (8 MMAs per block). NT activation columns per CTA.
 template <int FMT, int NT, bool STORE>
 __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
-  constexpr int KS = FMT == 0 ? 1 : 8;      // MMAs (32-value k-steps) per weight block
-  constexpr int ATILE = 128 * 32;           // A bytes per k-step
-  constexpr int BTILE = NT * 32;            // B bytes per k-step
+  using Cfg = TcCfg<FMT, NT>;
+  constexpr int KS = Cfg::KS, QU = Cfg::QU, P = Cfg::P, ATILE = Cfg::ATILE, BTILE = Cfg::BTILE;
   constexpr int NCOLS = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
   extern __shared__ __align__(128) uint8_t tc_smem[];
-  uint8_t* sA = tc_smem;                                             // [2][KS][ATILE]
-  int8_t* sB = reinterpret_cast<int8_t*>(tc_smem + 2 * KS * ATILE);  // [2][KS][BTILE]
+  uint8_t* raw = tc_smem;                                    // own-row packed blocks, fetched P - 1 blocks ahead
+  uint8_t* sA = tc_smem + Cfg::RAW;                          // [2][KS][ATILE]
+  int8_t* sB = reinterpret_cast<int8_t*>(sA + Cfg::ATILES);  // [P][KS][BTILE]
   __shared__ __align__(8) uint64_t full[2];
   // block sums and scales of the columns: three slots (block b in slot b % 3), because a thread may still read block
-  // b - 1's while another already stages block b + 1's (operands and accumulators are only reused after waits)
+  // b - 1's while another already stages block b + 1's (tiles and accumulators are only reused after waits)
   __shared__ int s_xsum[3][NT];
   __shared__ float s_dx[3][NT];
   __shared__ uint32_t s_tmem;
@@ -109,6 +129,26 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   const uint8_t* wrow = p.wq + (row_ok ? row : 0) * p.ldwq;
   const int16_t* srow = p.ws + (row_ok ? row : 0) * p.ldws;
   const uint32_t idesc = tc::instr_desc(NT);
+  const uint32_t raw_base = smem_addr(raw), b_base = smem_addr(sB);
+
+  // issue the copies of block b (weights of this thread's row; its share of the activation tile); one group
+  auto fetch = [&](int b) {
+    if (b < nblk) {
+      const int rs = b % P;
+#pragma unroll
+      for (int u = 0; u < QU; ++u)
+        cp_async16(raw_base + (uint32_t)(((rs * QU + u) * 128 + t) * 16),
+                   wrow + (int64_t)b * (QU * 16) + u * 16, row_ok);
+      constexpr int PIECES = KS * NT * 2;  // (k-step, column, half) 16-byte pieces
+      for (int i = t; i < PIECES; i += 128) {
+        const int s = i / (NT * 2), rem = i - s * NT * 2, c = rem >> 1, half = rem & 1;
+        const bool ok = c < ncols;
+        const int8_t* src = p.xq + (ok ? (col0 + c) * p.ldxq + (int64_t)b * Fmt<FMT>::kBlock + s * 32 + half * 16 : 0);
+        cp_async16(b_base + (uint32_t)((rs * KS + s) * BTILE + tc::core_off(c, 16 * half)), src, ok);
+      }
+    }
+    cp_async_commit();
+  };
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
@@ -121,6 +161,10 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   pdl_wait_then_trigger();
+#pragma unroll
+  for (int b = 0; b < P - 1; ++b) fetch(b);
+  float dx_next = (t < ncols && nblk > 0) ? p.xd[(col0 + t) * p.ldxd] : 0.f;
+  uint16_t sc_pending = (row_ok && nblk > 0) ? (uint16_t)srow[0] : (uint16_t)0, sc_prev = 0;
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -134,13 +178,12 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
 
   int slot = 0, prev_slot = 2;  // b % 3, (b - 1) % 3
   for (int b = 0; b < nblk; ++b) {
-    const int buf = b & 1;
+    const int buf = b & 1, rs = b % P;
     uint8_t* a = sA + buf * KS * ATILE;
-    int8_t* bt = sB + buf * KS * BTILE;
+    cp_async_wait<P - 2>();  // this thread's copies of block b have landed
     // A: this row's block, unpacked to unsigned bytes in natural value order (k-step s = values 32s .. 32s+31)
     if (FMT == 0) {
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (row_ok) w = *reinterpret_cast<const uint4*>(wrow + (int64_t)b * 16);
+      const uint4 w = lds_v4(raw_base + (uint32_t)((rs * 128 + t) * 16));
       const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
       const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
                                   (w.w >> 4) & 0x0F0F0F0Fu);
@@ -151,9 +194,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
       for (int h = 0; h < 2; ++h) {
         uint4 q[2];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-          q[u] = row_ok ? *reinterpret_cast<const uint4*>(wrow + (int64_t)b * 64 + h * 32 + u * 16)
-                        : make_uint4(0u, 0u, 0u, 0u);
+        for (int u = 0; u < 2; ++u) q[u] = lds_v4(raw_base + (uint32_t)(((rs * QU + 2 * h + u) * 128 + t) * 16));
 #pragma unroll
         for (int j = 0; j < 4; ++j) {  // k-step 4h + j: field j of bytes h*32 .. h*32+31 = values h*128 + 32j + t
           const int sh = 2 * j;
@@ -167,37 +208,18 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
         }
       }
     }
-    // B: the block's activations of this CTA's columns (zero for columns past M), the column block sums and scales
-    {
-      constexpr int PIECES = KS * NT * 2;  // 16-byte pieces: (k-step, column, half)
-      for (int i = t; i < PIECES; i += 128) {
-        const int s = i / (NT * 2), rem = i - s * NT * 2, c = rem >> 1, half = rem & 1;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (c < ncols)
-          v = *reinterpret_cast<const uint4*>(p.xq + (col0 + c) * p.ldxq + (int64_t)b * Fmt<FMT>::kBlock + s * 32 +
-                                              half * 16);
-        *reinterpret_cast<uint4*>(bt + s * BTILE + tc::core_off(c, 16 * half)) = v;
-      }
-      if (t < NT) {
-        int sum = 0;
-        float dx = 0.f;
-        if (t < ncols) {
-          const int8_t* xc = p.xq + (col0 + t) * p.ldxq + (int64_t)b * Fmt<FMT>::kBlock;
-#pragma unroll
-          for (int u = 0; u < Fmt<FMT>::kBlock / 16; ++u) {
-            const uint4 v = *reinterpret_cast<const uint4*>(xc + u * 16);
-            sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
-          }
-          dx = p.xd[(col0 + t) * p.ldxd + b];
-        }
-        s_xsum[slot][t] = sum;
-        s_dx[slot][t] = dx;
-      }
+    if (t < NT) {  // this block's column scale (fetched one block ahead) and the next one's fetch
+      s_dx[slot][t] = dx_next;
+      dx_next = (t < ncols && b + 1 < nblk) ? p.xd[(col0 + t) * p.ldxd + b + 1] : 0.f;
     }
+    const uint16_t sc_fin = sc_prev;  // scale of block b - 1 (its epilogue below)
+    sc_prev = sc_pending;             // scale of block b (its epilogue in the next iteration)
+    sc_pending = (row_ok && b + 1 < nblk) ? (uint16_t)srow[b + 1] : (uint16_t)0;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> tensor-core reads
     tc::fence_before();
-    __syncthreads();  // operands of block b complete; every thread finished block b - 2's epilogue
+    __syncthreads();  // block b's operands complete (all threads' copies); block b - 2's epilogue done everywhere
     tc::fence_after();
+    const int8_t* bt = sB + rs * KS * BTILE;
     if (t == 0) {
 #pragma unroll
       for (int s = 0; s < KS; ++s)
@@ -205,17 +227,31 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
                    tc::smem_desc(smem_addr(bt + s * BTILE)), idesc, s > 0 ? 1u : 0u);
       tc::mma_commit(smem_addr(&full[buf]));
     }
+    if (t < NT) {  // column block sums from the staged tile
+      int sum = 0;
+#pragma unroll
+      for (int s = 0; s < KS; ++s)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint4 v = lds_v4(smem_addr(bt + s * BTILE + tc::core_off(t, 16 * half)));
+          sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
+        }
+      s_xsum[slot][t] = sum;
+    }
     if (b > 0)
       gemm_tc_finish<FMT, NT, STORE>(p, tmem + lane_base, full, b - 1, s_xsum, s_dx, prev_slot,
-                                     f16_bits_to_f32((uint16_t)srow[b - 1]), acc, timed_out, row, col0, ncols, nblk,
-                                     row_ok);
+                                     f16_bits_to_f32(sc_fin), acc, timed_out, row, col0,
+                                     ncols, nblk, row_ok);
+    fetch(b + P - 1);  // into the ring slot of block b - 1, whose MMA this thread has seen complete
     prev_slot = slot;
     slot = slot == 2 ? 0 : slot + 1;
   }
+  // the last block's column sums were written after its barrier: one more barrier before every thread reads them
+  __syncthreads();
   if (nblk > 0)
     gemm_tc_finish<FMT, NT, STORE>(p, tmem + lane_base, full, nblk - 1, s_xsum, s_dx, prev_slot,
-                                   f16_bits_to_f32((uint16_t)srow[nblk - 1]), acc, timed_out, row, col0, ncols, nblk,
-                                   row_ok);
+                                   f16_bits_to_f32(sc_prev), acc, timed_out, row, col0, ncols, nblk, row_ok);
+  cp_async_wait<0>();
 
   if (row_ok)
 #pragma unroll
@@ -229,8 +265,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
 
 template <int FMT, int NT>
 static size_t gemm_tc_smem() {
-  constexpr int KS = FMT == 0 ? 1 : 8;
-  return (size_t)2 * KS * (128 * 32 + NT * 32);
+  return TcCfg<FMT, NT>::SMEM;
 }
 
 // Launches the tensor-core GEMM for M >= 8 columns (pre-quantized activations). Returns B2Q_OK, or a negative code.
