@@ -57,27 +57,49 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 }  // namespace tc
 
 // Epilogue of block b (accumulator buf): this row's exact int32 dots -> offset -> scaled f32 sums; S dump if STORE.
-template <int FMT, int NT, bool STORE>
-__device__ __forceinline__ void gemm_tc_finish(const GemvParams& p, uint32_t tmem_row, uint64_t* full, int b,
-                                               const int (&xsum)[3][NT], const float (&xdx)[3][NT], int slot,
-                                               float dw, float (&acc)[NT], bool& timed_out, int64_t row,
-                                               int64_t col0, int ncols, int nblk, bool row_ok) {
-  const int buf = b & 1;
-  if (!mbar_wait(smem_addr(&full[buf]), (uint32_t)((b >> 1) & 1), kWaitLimit)) timed_out = true;
+// Epilogue of block group i (accumulator buf = i & 1, block i*G + j in region buf * G + j): this row's exact int32
+// dots -> offset -> scaled f32 sums; S dump if STORE. Per column, koff = 0x4B400000 - off * sum(x) turns the dot into
+// the f32 bit pattern of 2^23 + 2^22 + s (exact for |s| < 2^22), so f32(s) is one integer add and one exact subtract;
+// the f32 products then run two columns per instruction (packed FP32x2), in the reference's multiply order.
+template <int FMT, int NT, int G, bool STORE>
+__device__ __forceinline__ void gemm_tc_finish(const GemvParams& p, uint32_t tmem_row, uint64_t* full, int i, int nb,
+                                               const int (&koff)[3][G][NT], const float (&xdx)[3][G][NT], int slot,
+                                               const uint16_t (&sc)[G], float (&acc)[NT], bool& timed_out,
+                                               int64_t row, int64_t col0, int ncols, int nblk, bool row_ok) {
+  constexpr float kMagic = 12582912.0f;  // 2^23 + 2^22
+  const int buf = i & 1;
+  if (!mbar_wait(smem_addr(&full[buf]), (uint32_t)((i >> 1) & 1), kWaitLimit)) timed_out = true;
   tc::fence_after();
 #pragma unroll
-  for (int c0 = 0; c0 < NT; c0 += 16) {
-    uint32_t v[16];
-    tc::tmem_ld16(tmem_row + (uint32_t)(buf * NT + c0), v);
+  for (int j = 0; j < G; ++j) {
+    if (j < nb) {
+      const float dw = f16_bits_to_f32(sc[j]);
+      const float2 dw2 = make_float2(dw, dw);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int c = c0 + j;
-      const int s = (int)v[j] - (FMT == 0 ? 8 : 1) * xsum[slot][c];
-      if (FMT == 0)
-        acc[c] = __fmaf_rn(__fmul_rn((float)s, dw), xdx[slot][c], acc[c]);
-      else
-        acc[c] = __fmaf_rn(__fmul_rn(xdx[slot][c], dw), (float)s, acc[c]);
-      if (STORE && row_ok && c < ncols) p.s[((col0 + c) * p.N + row) * nblk + b] = s;
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        uint32_t v[16];
+        tc::tmem_ld16(tmem_row + (uint32_t)((buf * G + j) * NT + c0), v);
+#pragma unroll
+        for (int q = 0; q < 16; q += 2) {
+          const int c = c0 + q;
+          const float2 f = __fadd2_rn(make_float2(__int_as_float((int)v[q] + koff[slot][j][c]),
+                                                  __int_as_float((int)v[q + 1] + koff[slot][j][c + 1])),
+                                      make_float2(-kMagic, -kMagic));  // exact f32(s) of both columns
+          const float2 dx2 = make_float2(xdx[slot][j][c], xdx[slot][j][c + 1]);
+          float2 a2 = make_float2(acc[c], acc[c + 1]);
+          if (FMT == 0)
+            a2 = __ffma2_rn(__fmul2_rn(f, dw2), dx2, a2);  // f32(s) * dw * dx
+          else
+            a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);  // dx * dw * f32(s)
+          acc[c] = a2.x;
+          acc[c + 1] = a2.y;
+          if (STORE && row_ok) {
+            const int64_t base = ((col0 + c) * p.N + row) * nblk + i * G + j;
+            if (c < ncols) p.s[base] = (int)v[q] + koff[slot][j][c] - 0x4B400000;
+            if (c + 1 < ncols) p.s[base + p.N * nblk] = (int)v[q + 1] + koff[slot][j][c + 1] - 0x4B400000;
+          }
+        }
+      }
     }
   }
   tc::fence_before();
@@ -90,34 +112,39 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Blocks fetched ahead (raw weights and activation tiles) per format and column tile, within shared memory.
+// Shape of the pipeline per format and column tile: G weight blocks per iteration (one barrier, one commit and one
+// accumulator wait per group), groups fetched ahead, and the shared-memory layout.
 template <int FMT, int NT>
 struct TcCfg {
-  static constexpr int KS = FMT == 0 ? 1 : 8;        // MMAs (32-value k-steps) per weight block
-  static constexpr int QU = FMT == 0 ? 1 : 4;        // 16-byte units of a row's packed block
+  static constexpr int KS = FMT == 0 ? 1 : 8;  // MMAs (32-value k-steps) per weight block
+  static constexpr int QU = FMT == 0 ? 1 : 4;  // 16-byte units of a row's packed block
+  // G = 1: measured on B200, larger groups (more shared memory, fewer resident CTAs) were slower for Q4_0
+  static constexpr int G = 1;
   static constexpr int P = FMT == 0 ? 8 : (NT <= 64 ? 4 : 2);
   static constexpr int ATILE = 128 * 32, BTILE = NT * 32;
-  static constexpr size_t RAW = (size_t)P * QU * 128 * 16;   // [P][QU][128 threads] 16-byte units
-  static constexpr size_t ATILES = (size_t)2 * KS * ATILE;   // [2][KS] unpacked weight tiles
-  static constexpr size_t BRING = (size_t)P * KS * BTILE;    // [P][KS] activation tiles
+  static constexpr size_t RAW = (size_t)P * G * QU * 128 * 16;    // [P][G][QU][128 threads] 16-byte units
+  static constexpr size_t ATILES = (size_t)2 * G * KS * ATILE;     // [2][G][KS] unpacked weight tiles
+  static constexpr size_t BRING = (size_t)P * G * KS * BTILE;      // [P][G][KS] activation tiles
   static constexpr size_t SMEM = RAW + ATILES + BRING;
+  static constexpr int NCOLS = 2 * G * NT < 32 ? 32 : 2 * G * NT;  // two accumulator sets of G x NT columns
 };
 
 // FMT 0: Q4_0 (1 MMA per block), FMT 1: TQ2_0 (8 MMAs per block). NT activation columns per CTA.
 template <int FMT, int NT, bool STORE>
 __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   using Cfg = TcCfg<FMT, NT>;
-  constexpr int KS = Cfg::KS, QU = Cfg::QU, P = Cfg::P, ATILE = Cfg::ATILE, BTILE = Cfg::BTILE;
-  constexpr int NCOLS = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
+  constexpr int KS = Cfg::KS, QU = Cfg::QU, G = Cfg::G, P = Cfg::P, ATILE = Cfg::ATILE, BTILE = Cfg::BTILE;
+  constexpr int NCOLS = Cfg::NCOLS;
   extern __shared__ __align__(128) uint8_t tc_smem[];
-  uint8_t* raw = tc_smem;                                    // own-row packed blocks, fetched P - 1 blocks ahead
-  uint8_t* sA = tc_smem + Cfg::RAW;                          // [2][KS][ATILE]
-  int8_t* sB = reinterpret_cast<int8_t*>(sA + Cfg::ATILES);  // [P][KS][BTILE]
+  uint8_t* raw = tc_smem;                                    // own-row packed blocks, fetched P - 1 groups ahead
+  uint8_t* sA = tc_smem + Cfg::RAW;                          // [2][G][KS][ATILE]
+  int8_t* sB = reinterpret_cast<int8_t*>(sA + Cfg::ATILES);  // [P][G][KS][BTILE]
   __shared__ __align__(8) uint64_t full[2];
-  // block sums and scales of the columns: three slots (block b in slot b % 3), because a thread may still read block
-  // b - 1's while another already stages block b + 1's (tiles and accumulators are only reused after waits)
-  __shared__ int s_xsum[3][NT];
-  __shared__ float s_dx[3][NT];
+  // per column and block: 0x4B400000 - offset * sum(x) and the scale, in three slots (group i in slot i % 3), because
+  // a thread may still read group i - 1's while another already stages group i + 1's (tiles and accumulators are only
+  // reused after waits)
+  __shared__ int s_koff[3][G][NT];
+  __shared__ float s_dx[3][G][NT];
   __shared__ uint32_t s_tmem;
 
   const int t = threadIdx.x, warp = t >> 5;
@@ -126,25 +153,32 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   const bool row_ok = row < p.N;
   const int ncols = (int)min((int64_t)NT, (int64_t)p.M - col0);
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const int ngrp = (nblk + G - 1) / G;
   const uint8_t* wrow = p.wq + (row_ok ? row : 0) * p.ldwq;
   const int16_t* srow = p.ws + (row_ok ? row : 0) * p.ldws;
   const uint32_t idesc = tc::instr_desc(NT);
   const uint32_t raw_base = smem_addr(raw), b_base = smem_addr(sB);
 
-  // issue the copies of block b (weights of this thread's row; its share of the activation tile); one group
-  auto fetch = [&](int b) {
-    if (b < nblk) {
-      const int rs = b % P;
+  // issue the copies of group i (this thread's row's packed blocks; its share of the activation tiles); one group
+  auto fetch = [&](int i) {
+    if (i < ngrp) {
+      const int rs = i % P;
 #pragma unroll
-      for (int u = 0; u < QU; ++u)
-        cp_async16(raw_base + (uint32_t)(((rs * QU + u) * 128 + t) * 16),
-                   wrow + (int64_t)b * (QU * 16) + u * 16, row_ok);
-      constexpr int PIECES = KS * NT * 2;  // (k-step, column, half) 16-byte pieces
-      for (int i = t; i < PIECES; i += 128) {
-        const int s = i / (NT * 2), rem = i - s * NT * 2, c = rem >> 1, half = rem & 1;
-        const bool ok = c < ncols;
-        const int8_t* src = p.xq + (ok ? (col0 + c) * p.ldxq + (int64_t)b * Fmt<FMT>::kBlock + s * 32 + half * 16 : 0);
-        cp_async16(b_base + (uint32_t)((rs * KS + s) * BTILE + tc::core_off(c, 16 * half)), src, ok);
+      for (int j = 0; j < G; ++j) {
+        const int b = i * G + j;
+#pragma unroll
+        for (int u = 0; u < QU; ++u)
+          cp_async16(raw_base + (uint32_t)((((rs * G + j) * QU + u) * 128 + t) * 16),
+                     wrow + (int64_t)min(b, nblk - 1) * (QU * 16) + u * 16, row_ok && b < nblk);
+      }
+      constexpr int PIECES = G * KS * NT * 2;  // (block, k-step, column, half) 16-byte pieces
+      for (int q = t; q < PIECES; q += 128) {
+        const int js = q / (NT * 2), rem = q - js * NT * 2, c = rem >> 1, half = rem & 1;
+        const int j = js / KS, s = js - j * KS, b = i * G + j;
+        const bool ok = c < ncols && b < nblk;
+        const int8_t* src =
+            p.xq + (ok ? (col0 + c) * p.ldxq + (int64_t)b * Fmt<FMT>::kBlock + s * 32 + half * 16 : 0);
+        cp_async16(b_base + (uint32_t)(((rs * G + j) * KS + s) * BTILE + tc::core_off(c, 16 * half)), src, ok);
       }
     }
     cp_async_commit();
@@ -162,9 +196,16 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   }
   pdl_wait_then_trigger();
 #pragma unroll
-  for (int b = 0; b < P - 1; ++b) fetch(b);
-  float dx_next = (t < ncols && nblk > 0) ? p.xd[(col0 + t) * p.ldxd] : 0.f;
-  uint16_t sc_pending = (row_ok && nblk > 0) ? (uint16_t)srow[0] : (uint16_t)0, sc_prev = 0;
+  for (int i = 0; i < P - 1; ++i) fetch(i);
+  // per-block scales of this row and column scales, one group ahead in registers
+  uint16_t sc_pending[G], sc_prev[G], sc_fin[G];
+  float dx_next[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    sc_pending[j] = (row_ok && j < nblk) ? (uint16_t)srow[j] : (uint16_t)0;
+    sc_prev[j] = 0;
+    dx_next[j] = (t < ncols && j < nblk) ? p.xd[(col0 + t) * p.ldxd + j] : 0.f;
+  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -176,81 +217,97 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   for (int c = 0; c < NT; ++c) acc[c] = 0.f;
   bool timed_out = false;
 
-  int slot = 0, prev_slot = 2;  // b % 3, (b - 1) % 3
-  for (int b = 0; b < nblk; ++b) {
-    const int buf = b & 1, rs = b % P;
-    uint8_t* a = sA + buf * KS * ATILE;
-    cp_async_wait<P - 2>();  // this thread's copies of block b have landed
-    // A: this row's block, unpacked to unsigned bytes in natural value order (k-step s = values 32s .. 32s+31)
-    if (FMT == 0) {
-      const uint4 w = lds_v4(raw_base + (uint32_t)((rs * 128 + t) * 16));
-      const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-      const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                  (w.w >> 4) & 0x0F0F0F0Fu);
-      *reinterpret_cast<uint4*>(a + tc::core_off(t, 0)) = lo;   // values 0..15: low nibbles of bytes 0..15
-      *reinterpret_cast<uint4*>(a + tc::core_off(t, 16)) = hi;  // values 16..31: high nibbles
-    } else {
+  int slot = 0, prev_slot = 2;  // i % 3, (i - 1) % 3
+  for (int i = 0; i < ngrp; ++i) {
+    const int buf = i & 1, rs = i % P;
+    const int nb = min(G, nblk - i * G);
+    uint8_t* a = sA + buf * G * KS * ATILE;
+    cp_async_wait<P - 2>();  // this thread's copies of group i have landed
+    // A: this row's blocks, unpacked to unsigned bytes in natural value order (k-step s = values 32s .. 32s+31)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint4 q[2];
+    for (int j = 0; j < G; ++j) {
+      uint8_t* aj = a + j * KS * ATILE;
+      const uint32_t rj = raw_base + (uint32_t)((rs * G + j) * QU * 128 * 16);
+      if (FMT == 0) {
+        const uint4 w = lds_v4(rj + (uint32_t)(t * 16));
+        const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+        const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                    (w.w >> 4) & 0x0F0F0F0Fu);
+        *reinterpret_cast<uint4*>(aj + tc::core_off(t, 0)) = lo;   // values 0..15: low nibbles of bytes 0..15
+        *reinterpret_cast<uint4*>(aj + tc::core_off(t, 16)) = hi;  // values 16..31: high nibbles
+      } else {
 #pragma unroll
-        for (int u = 0; u < 2; ++u) q[u] = lds_v4(raw_base + (uint32_t)(((rs * QU + 2 * h + u) * 128 + t) * 16));
+        for (int h = 0; h < 2; ++h) {
+          uint4 q[2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {  // k-step 4h + j: field j of bytes h*32 .. h*32+31 = values h*128 + 32j + t
-          const int sh = 2 * j;
-          uint8_t* as = a + (4 * h + j) * ATILE;
+          for (int u = 0; u < 2; ++u) q[u] = lds_v4(rj + (uint32_t)(((2 * h + u) * 128 + t) * 16));
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const uint4 f = make_uint4((q[u].x >> sh) & 0x03030303u, (q[u].y >> sh) & 0x03030303u,
-                                       (q[u].z >> sh) & 0x03030303u, (q[u].w >> sh) & 0x03030303u);
-            *reinterpret_cast<uint4*>(as + tc::core_off(t, 16 * u)) = f;
+          for (int f = 0; f < 4; ++f) {  // k-step 4h + f: field f of bytes h*32 .. h*32+31 = values h*128 + 32f + t
+            const int sh = 2 * f;
+            uint8_t* as = aj + (4 * h + f) * ATILE;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const uint4 v = make_uint4((q[u].x >> sh) & 0x03030303u, (q[u].y >> sh) & 0x03030303u,
+                                         (q[u].z >> sh) & 0x03030303u, (q[u].w >> sh) & 0x03030303u);
+              *reinterpret_cast<uint4*>(as + tc::core_off(t, 16 * u)) = v;
+            }
           }
         }
       }
     }
-    if (t < NT) {  // this block's column scale (fetched one block ahead) and the next one's fetch
-      s_dx[slot][t] = dx_next;
-      dx_next = (t < ncols && b + 1 < nblk) ? p.xd[(col0 + t) * p.ldxd + b + 1] : 0.f;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      if (t < NT) {  // this group's column scales (fetched one group ahead) and the next group's fetch
+        s_dx[slot][j][t] = dx_next[j];
+        const int bn = (i + 1) * G + j;
+        dx_next[j] = (t < ncols && bn < nblk) ? p.xd[(col0 + t) * p.ldxd + bn] : 0.f;
+      }
+      sc_fin[j] = sc_prev[j];      // scales of group i - 1 (its epilogue below)
+      sc_prev[j] = sc_pending[j];  // scales of group i (its epilogue in the next iteration)
+      const int bn = (i + 1) * G + j;
+      sc_pending[j] = (row_ok && bn < nblk) ? (uint16_t)srow[bn] : (uint16_t)0;
     }
-    const uint16_t sc_fin = sc_prev;  // scale of block b - 1 (its epilogue below)
-    sc_prev = sc_pending;             // scale of block b (its epilogue in the next iteration)
-    sc_pending = (row_ok && b + 1 < nblk) ? (uint16_t)srow[b + 1] : (uint16_t)0;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> tensor-core reads
     tc::fence_before();
-    __syncthreads();  // block b's operands complete (all threads' copies); block b - 2's epilogue done everywhere
+    __syncthreads();  // group i's operands complete (all threads' copies); group i - 2's epilogue done everywhere
     tc::fence_after();
-    const int8_t* bt = sB + rs * KS * BTILE;
+    const int8_t* bt = sB + rs * G * KS * BTILE;
     if (t == 0) {
 #pragma unroll
-      for (int s = 0; s < KS; ++s)
-        tc::mma_i8(tmem + (uint32_t)(buf * NT), tc::smem_desc(smem_addr(a + s * ATILE)),
-                   tc::smem_desc(smem_addr(bt + s * BTILE)), idesc, s > 0 ? 1u : 0u);
+      for (int j = 0; j < G; ++j)
+        if (j < nb)
+#pragma unroll
+          for (int s = 0; s < KS; ++s)
+            tc::mma_i8(tmem + (uint32_t)((buf * G + j) * NT), tc::smem_desc(smem_addr(a + (j * KS + s) * ATILE)),
+                       tc::smem_desc(smem_addr(bt + (j * KS + s) * BTILE)), idesc, s > 0 ? 1u : 0u);
       tc::mma_commit(smem_addr(&full[buf]));
     }
-    if (t < NT) {  // column block sums from the staged tile
-      int sum = 0;
+    if (t < NT) {  // column block sums from the staged tiles
 #pragma unroll
-      for (int s = 0; s < KS; ++s)
+      for (int j = 0; j < G; ++j) {
+        int sum = 0;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint4 v = lds_v4(smem_addr(bt + s * BTILE + tc::core_off(t, 16 * half)));
-          sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
-        }
-      s_xsum[slot][t] = sum;
+        for (int s = 0; s < KS; ++s)
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint4 v = lds_v4(smem_addr(bt + (j * KS + s) * BTILE + tc::core_off(t, 16 * half)));
+            sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
+          }
+        s_koff[slot][j][t] = 0x4B400000 - (FMT == 0 ? 8 : 1) * sum;
+      }
     }
-    if (b > 0)
-      gemm_tc_finish<FMT, NT, STORE>(p, tmem + lane_base, full, b - 1, s_xsum, s_dx, prev_slot,
-                                     f16_bits_to_f32(sc_fin), acc, timed_out, row, col0,
-                                     ncols, nblk, row_ok);
-    fetch(b + P - 1);  // into the ring slot of block b - 1, whose MMA this thread has seen complete
+    if (i > 0)
+      gemm_tc_finish<FMT, NT, G, STORE>(p, tmem + lane_base, full, i - 1, G, s_koff, s_dx, prev_slot, sc_fin, acc,
+                                        timed_out, row, col0, ncols, nblk, row_ok);
+    fetch(i + P - 1);  // into the ring slot of group i - 1, whose MMAs this thread has seen complete
     prev_slot = slot;
     slot = slot == 2 ? 0 : slot + 1;
   }
-  // the last block's column sums were written after its barrier: one more barrier before every thread reads them
+  // the last group's column offsets were written after its barrier: one more barrier before every thread reads them
   __syncthreads();
-  if (nblk > 0)
-    gemm_tc_finish<FMT, NT, STORE>(p, tmem + lane_base, full, nblk - 1, s_xsum, s_dx, prev_slot,
-                                   f16_bits_to_f32(sc_prev), acc, timed_out, row, col0, ncols, nblk, row_ok);
+  if (ngrp > 0)
+    gemm_tc_finish<FMT, NT, G, STORE>(p, tmem + lane_base, full, ngrp - 1, nblk - (ngrp - 1) * G, s_koff, s_dx,
+                                      prev_slot, sc_prev, acc, timed_out, row, col0, ncols, nblk, row_ok);
   cp_async_wait<0>();
 
   if (row_ok)
