@@ -904,7 +904,8 @@ __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint
 #ifdef B2Q_RING_MAXNREG
 #define B2Q_RING_BOUNDS __maxnreg__(B2Q_RING_MAXNREG)
 #else
-#define B2Q_RING_BOUNDS __launch_bounds__(kMaxThreads, 1)
+// 16-row groups (one column, one chunk per thread) need more than 128 registers: CTAs of at most 256 threads
+#define B2Q_RING_BOUNDS __launch_bounds__(R >= 16 ? 256 : kMaxThreads, 1)
 #endif
 template <int FMT, int R, int MC, bool XREG>
 __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {

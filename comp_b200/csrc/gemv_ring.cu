@@ -6,6 +6,7 @@ namespace b2q {
 template <int FMT, bool XREG>
 static KernelFn pick(int R, int MC) {
   if (MC == 1) {
+    if (R == 16) return XREG ? gemv_ring_kernel<FMT, 16, 1, true> : nullptr;
     switch (R) {
       case 1: return gemv_ring_kernel<FMT, 1, 1, XREG>;
       case 2: return gemv_ring_kernel<FMT, 2, 1, XREG>;
