@@ -37,14 +37,19 @@ WORKLOADS = {
                 ("q4_0", 4096, 14336, "down")],
     "config0": [("q4_0", 4096, 4096, "config0")],
     "config1": [("tq2_0", 4096, 4096, "config1")],
+    # Q8_0 weights (an extension beyond the reference): the config-3 decoder shapes plus the lm_head, all Q8_0
+    "q8_0": [("q8_0", 6144, 4096, "qkv"), ("q8_0", 4096, 4096, "o_proj"), ("q8_0", 28672, 4096, "gate_up"),
+             ("q8_0", 4096, 14336, "down"), ("q8_0", 128256, 4096, "lm_head")],
 }
-BLOCK = {"q4_0": 32, "tq2_0": 256}
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32}
+BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34}  # ggml block bytes (quant bytes + f16 scale)
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2}
 METRIC = "weight-stream GB/s and us/GEMV (% of HBM peak) at 1/2/4/8 B200 vs host CPU ref"
 L2_BYTES = 126 * 2**20
 
 
 def weight_bytes(fmt, n, k):
-    return n * k * 18 // 32 if fmt == "q4_0" else n * k * 66 // 256
+    return n * k * BLOCK_BYTES[fmt] // BLOCK[fmt]
 
 
 def algo_bytes(fmt, n, k, m):
@@ -159,6 +164,9 @@ def make_layer_gpu(fmt, n, k, seed, dev, rows=None):
     if fmt == "q4_0":
         wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
         ws = (torch.randn((n, nb), device=dev, generator=g) * 0.02).abs().half().view(torch.int16)
+    elif fmt == "q8_0":
+        wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g).view(torch.uint8)
+        ws = (torch.randn((n, nb), device=dev, generator=g) * 0.002).abs().half().view(torch.int16)
     else:
         t = torch.randint(0, 81, (n, k // 4), dtype=torch.uint8, device=dev, generator=g)
         wq = (t % 3) | (((t // 3) % 3) << 2) | (((t // 9) % 3) << 4) | (((t // 27) % 3) << 6)
@@ -188,7 +196,7 @@ def cpu_reference_run(layers_np, steps, warmup):
 
     def one():
         for fmt, wq, ws, x, k in layers_np:
-            if fmt == "q4_0":
+            if fmt in ("q4_0", "q8_0"):
                 xq, xd = native.quant_q8_0(x)
             else:
                 xq, xd, _ = native.quant_q8_K(x)
@@ -324,7 +332,7 @@ def main():
         L.x_host = torch.from_numpy(make_x(k, m, 200 + i)).pin_memory()
         L.x = L.x_host.to(dev)
         L.y = torch.empty((m, n), dtype=torch.float32, device=dev)
-        L.fid = 0 if fmt == "q4_0" else 1
+        L.fid = FMT_ID[fmt]
         L.wsb = host.workspace_size(fmt, n, k, m) if world == 1 else 0
         L.work = torch.empty(max(16, L.wsb), dtype=torch.uint8, device=dev)
         if world > 1:

@@ -5,6 +5,8 @@
 // the GEMVs: every block dot is the exact int32 sum (read from tensor memory per block), Y adds the per-block f32
 // products in the reference's multiply order (Q4_0: f32(s) * dw * dx, TQ2_0: dx * dw * f32(s); kernels.py:93, 141).
 //
+// Q8_0 weights (format 2, an extension beyond the reference) take the same path with signed A and no offset.
+//
 // One CTA of 128 threads computes 128 weight rows x NT activation columns (NT = 16 .. 128, grid.y covers more).
 // Thread t owns weight row t = tensor-memory lane t. Per weight block (Q4_0: 32 values, one MMA with K = 32; TQ2_0:
 // 256 values, eight MMAs accumulated):
@@ -31,9 +33,10 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {  // no swizzle; L
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
          ((uint64_t)1 << 46);
 }
-// kind::i8 instruction descriptor: s32 accumulator, A unsigned 8-bit, B signed 8-bit, both K-major, M = 128, N = nt
-__device__ __forceinline__ uint32_t instr_desc(int nt) {
-  return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | (8u << 24);
+// kind::i8 instruction descriptor: s32 accumulator, A unsigned (or signed) 8-bit, B signed 8-bit, both K-major,
+// M = 128, N = nt
+__device__ __forceinline__ uint32_t instr_desc(int nt, bool a_signed) {
+  return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | (8u << 24);
 }
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -87,7 +90,7 @@ __device__ __forceinline__ void gemm_tc_finish(const GemvParams& p, uint32_t tme
                                       make_float2(-kMagic, -kMagic));  // exact f32(s) of both columns
           const float2 dx2 = make_float2(xdx[slot][j][c], xdx[slot][j][c + 1]);
           float2 a2 = make_float2(acc[c], acc[c + 1]);
-          if (FMT == 0)
+          if (FMT != 1)
             a2 = __ffma2_rn(__fmul2_rn(f, dw2), dx2, a2);  // f32(s) * dw * dx
           else
             a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);  // dx * dw * f32(s)
@@ -116,11 +119,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // accumulator wait per group), groups fetched ahead, and the shared-memory layout.
 template <int FMT, int NT>
 struct TcCfg {
-  static constexpr int KS = FMT == 0 ? 1 : 8;  // MMAs (32-value k-steps) per weight block
-  static constexpr int QU = FMT == 0 ? 1 : 4;  // 16-byte units of a row's packed block
+  static constexpr int KS = FMT == 1 ? 8 : 1;                  // MMAs (32-value k-steps) per weight block
+  static constexpr int QU = FMT == 0 ? 1 : FMT == 1 ? 4 : 2;  // 16-byte units of a row's packed block
   // G = 1: measured on B200, larger groups (more shared memory, fewer resident CTAs) were slower for Q4_0
   static constexpr int G = 1;
-  static constexpr int P = FMT == 0 ? 8 : (NT <= 64 ? 4 : 2);
+  static constexpr int P = FMT == 0 ? 8 : FMT == 2 ? 6 : (NT <= 64 ? 4 : 2);
   static constexpr int ATILE = 128 * 32, BTILE = NT * 32;
   static constexpr size_t RAW = (size_t)P * G * QU * 128 * 16;    // [P][G][QU][128 threads] 16-byte units
   static constexpr size_t ATILES = (size_t)2 * G * KS * ATILE;     // [2][G][KS] unpacked weight tiles
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
   const int ngrp = (nblk + G - 1) / G;
   const uint8_t* wrow = p.wq + (row_ok ? row : 0) * p.ldwq;
   const int16_t* srow = p.ws + (row_ok ? row : 0) * p.ldws;
-  const uint32_t idesc = tc::instr_desc(NT);
+  const uint32_t idesc = tc::instr_desc(NT, FMT == 2);  // Q8_0 weights are signed
   const uint32_t raw_base = smem_addr(raw), b_base = smem_addr(sB);
 
   // issue the copies of group i (this thread's row's packed blocks; its share of the activation tiles); one group
@@ -228,7 +231,10 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
     for (int j = 0; j < G; ++j) {
       uint8_t* aj = a + j * KS * ATILE;
       const uint32_t rj = raw_base + (uint32_t)((rs * G + j) * QU * 128 * 16);
-      if (FMT == 0) {
+      if (FMT == 2) {  // Q8_0: the 32 int8 values as they are
+        *reinterpret_cast<uint4*>(aj + tc::core_off(t, 0)) = lds_v4(rj + (uint32_t)(t * 16));
+        *reinterpret_cast<uint4*>(aj + tc::core_off(t, 16)) = lds_v4(rj + (uint32_t)((128 + t) * 16));
+      } else if (FMT == 0) {
         const uint4 w = lds_v4(rj + (uint32_t)(t * 16));
         const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
         const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
@@ -282,7 +288,10 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
                        tc::smem_desc(smem_addr(bt + (j * KS + s) * BTILE)), idesc, s > 0 ? 1u : 0u);
       tc::mma_commit(smem_addr(&full[buf]));
     }
-    if (t < NT) {  // column block sums from the staged tiles
+    if (t < NT && Fmt<FMT>::kOffset == 0) {
+#pragma unroll
+      for (int j = 0; j < G; ++j) s_koff[slot][j][t] = 0x4B400000;  // no offset to fold in
+    } else if (t < NT) {  // column block sums from the staged tiles
 #pragma unroll
       for (int j = 0; j < G; ++j) {
         int sum = 0;
@@ -293,7 +302,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const GemvParams p) {
             const uint4 v = lds_v4(smem_addr(bt + (j * KS + s) * BTILE + tc::core_off(t, 16 * half)));
             sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
           }
-        s_koff[slot][j][t] = 0x4B400000 - (FMT == 0 ? 8 : 1) * sum;
+        s_koff[slot][j][t] = 0x4B400000 - Fmt<FMT>::kOffset * sum;
       }
     }
     if (i > 0)
@@ -339,6 +348,7 @@ int launch_gemm_tc(const GemvParams& base, int fmt, cudaStream_t stream, bool pd
   }
   B2Q_TC_CASE(0, 16) B2Q_TC_CASE(0, 32) B2Q_TC_CASE(0, 64) B2Q_TC_CASE(0, 128)
   B2Q_TC_CASE(1, 16) B2Q_TC_CASE(1, 32) B2Q_TC_CASE(1, 64) B2Q_TC_CASE(1, 128)
+  B2Q_TC_CASE(2, 16) B2Q_TC_CASE(2, 32) B2Q_TC_CASE(2, 64) B2Q_TC_CASE(2, 128)
 #undef B2Q_TC_CASE
   if (!fn) return fail(B2Q_EINVAL, "gemm_tc: no kernel for fmt %d", fmt);
   cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -358,7 +368,7 @@ int launch_gemm_tc(const GemvParams& base, int fmt, cudaStream_t stream, bool pd
     cudaGetLastError();
     return fail(B2Q_ECUDA, "gemm_tc: launch failed: %s", cudaGetErrorString(e));
   }
-  return after_launch(fmt == 0 ? "gemm_tc_q4_0" : "gemm_tc_tq2_0");
+  return after_launch(fmt == 0 ? "gemm_tc_q4_0" : fmt == 1 ? "gemm_tc_tq2_0" : "gemm_tc_q8_0");
 }
 
 }  // namespace b2q

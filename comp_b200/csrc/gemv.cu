@@ -40,6 +40,14 @@
 
 namespace b2q {
 
+// Weight formats: 0 Q4_0, 1 TQ2_0, 2 Q8_0 (an extension beyond the reference).
+static inline int fmt_block(int fmt) { return fmt == 1 ? 256 : 32; }            // values per block
+static inline int fmt_chunk_values(int fmt) { return fmt == 0 ? 32 : fmt == 1 ? 64 : 16; }  // per 16-byte chunk
+static inline bool fmt_ok(int fmt) { return fmt >= 0 && fmt <= 2; }
+static inline size_t fmt_slot_bytes(int fmt, int C) {
+  return fmt == 0 ? cluster_slot_bytes<0>(C) : fmt == 1 ? cluster_slot_bytes<1>(C) : cluster_slot_bytes<2>(C);
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // ------------------------------------------------------------------------------------------------------------------
 // Host side: planning and launch
@@ -150,13 +158,13 @@ static int max_active_clusters(KernelFn fn, int threads, size_t smem, int cs) {
 
 // Shared memory besides the ring: staged activations (none when they live in registers) and the reduction partials.
 static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, int T, bool xreg) {
-  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  const int nblk = (int)(K / fmt_block(fmt));
   const int Mx = xreg ? 0 : M;
   return (size_t)Mx * K + (size_t)Mx * C * 4 + (size_t)Mx * nblk * 4 + (size_t)2 * (T / 32) * R * MC * 4;
 }
 
 static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
-  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  const int nblk = (int)(K / fmt_block(fmt));
   const uint32_t s = (uint32_t)R * (uint32_t)nblk * 2u;
   return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
 }
@@ -166,7 +174,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  const int C = (int)(K / (fmt == 0 ? 32 : 64));
+  const int C = (int)(K / fmt_chunk_values(fmt));
   const int MC = M == 1 ? 1 : kMaxColumns;
   int CPT = (C + kMaxThreads - 1) / kMaxThreads;
   if (g_tune_cpt > 0) CPT = g_tune_cpt;
@@ -187,7 +195,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
       // 16-row groups: ring path, one column, one chunk per thread, CTAs of at most 256 threads. Measured on B200:
       // TQ2_0 gate_up 2% faster than 8 rows, Q4_0 lm_head unchanged -- so TQ2_0 by default, Q4_0 on request.
-      if (R == 16 && (!ring || !xreg || T > 256 || (fmt == 0 && g_tune_rows != 16))) continue;
+      if (R == 16 && (!ring || !xreg || T > 256 || (fmt != 1 && g_tune_rows != 16))) continue;
       const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T, xreg);
       const int64_t groups = (N + R - 1) / R;
       int stages = 0;
@@ -202,7 +210,7 @@ static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, in
       }
       int cs = 1;
       if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster : (g_tune_cluster == 0 ? 2 : 1);
-      const size_t slot = fmt == 0 ? cluster_slot_bytes<0>(C) : cluster_slot_bytes<1>(C);
+      const size_t slot = fmt_slot_bytes(fmt, C);
       if (cs > 1 && smem + slot > (size_t)di.max_smem_optin && g_tune_cluster == 0) cs = 1;
       if (cs > 1) smem += slot;
       if (smem > (size_t)di.max_smem_optin) continue;
@@ -255,8 +263,8 @@ static int make_warp_plan(int fmt, int64_t N, int64_t K, Plan* out) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  const int C = (int)(K / (fmt == 0 ? 32 : 64));
-  const int nblk = (int)(K / (fmt == 0 ? 32 : 256));
+  const int C = (int)(K / fmt_chunk_values(fmt));
+  const int nblk = (int)(K / fmt_block(fmt));
   const size_t xbytes = (size_t)K + 4 * (size_t)C + 4 * (size_t)nblk;
   const int rows[3] = {4, 2, 1}, stages[3] = {3, 2, 4};
   double best_score = -1.0;
@@ -301,8 +309,8 @@ static int g_splitk_mode = 0;  // 0: never split (default; measured slower on B2
 
 static int choose_splits(int fmt, int64_t K, int64_t M) {
   if (g_splitk_mode == 0 || M < 1 || M > kMaxColumns || K == 0) return 1;
-  const int blk = fmt == 0 ? 32 : 256;
-  const int64_t nblk = K / blk, C = K / (fmt == 0 ? 32 : 64);
+  const int blk = fmt_block(fmt);
+  const int64_t nblk = K / blk, C = K / fmt_chunk_values(fmt);
   if (C <= 256) return 1;
   for (int s = 2; s <= 16; s *= 2) {
     if (nblk % s) continue;
@@ -316,7 +324,7 @@ static int choose_splits(int fmt, int64_t K, int64_t M) {
 static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws,
                            const void* x, const float* xd, const float* y, int64_t N, int64_t K, int64_t M,
                            bool f32_input) {
-  const int blk = fmt == 0 ? 32 : 256;
+  const int blk = fmt_block(fmt);
   if (N < 0 || K < 0 || M < 0) return fail(B2Q_EINVAL, "%s: negative size", who);
   if (K % blk) return fail(B2Q_EINVAL, "%s: K=%lld is not a multiple of the %d-value block", who, (long long)K, blk);
   if (N == 0 || M == 0) return B2Q_OK;  // empty output: no pointer is touched
@@ -324,7 +332,7 @@ static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t 
   if (!aligned(y, 4)) return fail(B2Q_EALIGN, "%s: y must be 4-byte aligned", who);
   if (K == 0) return B2Q_OK;  // empty sums: only Y (= 0) is written
   if (!wq || !ws || !x || (!f32_input && !xd)) return fail(B2Q_EINVAL, "%s: null pointer", who);
-  const int64_t qbytes = K / (fmt == 0 ? 2 : 4);
+  const int64_t qbytes = fmt == 0 ? K / 2 : fmt == 1 ? K / 4 : K;
   if (ldwq < qbytes) return fail(B2Q_EINVAL, "%s: ldwq=%lld < %lld quant bytes per row", who, (long long)ldwq,
                                  (long long)qbytes);
   if (!aligned(wq, 16) || (ldwq % 16)) return fail(B2Q_EALIGN, "%s: wq must be 16-byte aligned, ldwq %% 16 == 0", who);
@@ -373,7 +381,7 @@ static int g_tc_min_m = 8;
 
 // Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD.
 static size_t tc_act_bytes(int fmt, int64_t K, int64_t M) {
-  const int64_t nblk = K / (fmt == 0 ? 32 : 256);
+  const int64_t nblk = K / fmt_block(fmt);
   return ((size_t)M * (size_t)K + 15) / 16 * 16 + (size_t)M * (size_t)nblk * sizeof(float);
 }
 
@@ -386,7 +394,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     }
     return B2Q_OK;
   }
-  const int blk = a.fmt == 0 ? 32 : 256;
+  const int blk = fmt_block(a.fmt);
   const int64_t nblk = a.K / blk;
   // many columns: the tensor-core GEMM, on pre-quantized activations (a fused call quantizes first into the caller's
   // XQ / XD outputs or the workspace; without either it stays on the GEMV path)
@@ -407,7 +415,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
         dq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + ((size_t)a.M * a.K + 15) / 16 * 16);
       }
       if (qo) {
-        const int rc = a.fmt == 0 ? b2q_quant_q8_0(a.x_f32, a.ldx, qo, dq, a.M, a.K, stream)
+        const int rc = a.fmt != 1 ? b2q_quant_q8_0(a.x_f32, a.ldx, qo, dq, a.M, a.K, stream)
                                   : b2q_quant_q8_K(a.x_f32, a.ldx, qo, dq, nullptr, a.M, a.K, stream);
         if (rc) return rc;
         xq = qo;
@@ -441,7 +449,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     if (sp > 1 && (size_t)sp * a.M * a.N * sizeof(float) <= a.workspace_bytes) splits = sp;
   }
   const int64_t Ks = a.K / splits, nblk_s = nblk / splits;
-  const int C = (int)(Ks / (a.fmt == 0 ? 32 : 64));
+  const int C = (int)(Ks / fmt_chunk_values(a.fmt));
   // ring path: every row's scale bytes (and so every group's) must be a whole number of 16-byte units, 16-aligned
   const bool ring_ok = ((nblk * 2) % 16 == 0) && ((nblk_s * 2) % 16 == 0) && aligned(a.ws, 16);
   for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
@@ -516,7 +524,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       cudaGetLastError();
       return fail(B2Q_ECUDA, "gemv: launch failed: %s", cudaGetErrorString(le));
     }
-    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : "gemv_tq2_0");
+    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : a.fmt == 1 ? "gemv_tq2_0" : "gemv_q8_0");
     if (rc) return rc;
     if (splits > 1) {
       DeviceInfo di;
@@ -549,7 +557,7 @@ int quant_gemv_forced_split(int fmt, const uint8_t* wq, int64_t ldwq, const int1
   int rc = check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
   if (M > kMaxColumns) return fail(B2Q_ERANGE, "%s: M=%lld, at most %d columns", who, (long long)M, kMaxColumns);
-  const int blk = fmt == 0 ? 32 : 256;
+  const int blk = fmt_block(fmt);
   const int64_t nblk = K / blk;
   if (splits < 2 || splits > 16 || nblk % splits)
     return fail(B2Q_EINVAL, "%s: splits=%d must be 2..16 and divide the %lld blocks of a row", who, splits,
@@ -602,9 +610,23 @@ int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int
   return launch_gemv(a, (cudaStream_t)stream);
 }
 
+int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
+  int rc = check_gemv_args("b2q_gemv_q8_0", 2, wq, ldwq, ws, xq, xd, y, N, K, M, false);
+  if (rc) return rc;
+  if (variant < 0 || variant > 2) return fail(B2Q_EINVAL, "b2q_gemv_q8_0: variant %d not in 0..2", variant);
+  if (s && !aligned(s, 4)) return fail(B2Q_EALIGN, "b2q_gemv_q8_0: s must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = 2;
+  a.bytes = variant == B2Q_VARIANT_BYTES;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.xq = xq, a.xd = xd, a.y = y, a.ldy = N, a.s = s;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
 int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream) {
-  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not Q4_0 (0) or TQ2_0 (1)", fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", fmt);
   int rc = check_gemv_args("b2q_quant_gemv", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
   if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
@@ -620,7 +642,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 }
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
-  if ((fmt != 0 && fmt != 1) || N <= 0 || K <= 0 || M <= 0 || (K % (fmt == 0 ? 32 : 256))) return 0;
+  if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
   if (g_tc_min_m > 0 && M >= g_tc_min_m) return tc_act_bytes(fmt, K, M);  // the GEMV path ignores it
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
@@ -629,7 +651,7 @@ size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
 int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                       int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, void* workspace,
                       size_t workspace_bytes, b2q_stream_t stream) {
-  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: fmt %d is not Q4_0 (0) or TQ2_0 (1)", fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", fmt);
   int rc = check_gemv_args("b2q_quant_gemv_ws", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
   if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
@@ -650,7 +672,7 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
                        int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
                        int rank, int nranks, long long spin_limit, b2q_stream_t stream) {
   const char* who = "b2q_gemv_allgather";
-  if (fmt != 0 && fmt != 1) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0) or TQ2_0 (1)", who, fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", who, fmt);
   if (nranks < 1 || rank < 0 || rank >= nranks) return fail(B2Q_EINVAL, "%s: rank %d of %d", who, rank, nranks);
   if (M < 1 || M > kMaxColumns) return fail(B2Q_ERANGE, "%s: M=%lld, 1..%d supported", who, (long long)M, kMaxColumns);
   if (K < 1 || n_local < 1 || row0 < 0 || row0 + n_local > N_total)

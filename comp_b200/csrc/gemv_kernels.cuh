@@ -88,13 +88,22 @@ struct GemvParams {
 
 template <int FMT>
 struct Fmt;
+// kQBytes: quant bytes per block; kOffset: the weights' stored offset (value = field - kOffset), folded in as
+// -kOffset * sum(x); kActQ80: the activations are q8_0 (32-value blocks, f16-exact scales), else q8_K.
 template <>
 struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibbles)
-  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2;
+  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 8;
+  static constexpr bool kActQ80 = true;
 };
 template <>
 struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
-  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4;
+  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4, kQBytes = 64, kOffset = 1;
+  static constexpr bool kActQ80 = false;
+};
+template <>
+struct Fmt<2> {  // Q8_0 (an extension beyond the reference: ggml block_q8_0): 32 int8 values, 2 chunks per block
+  static constexpr int kBlock = 32, kChunkShift = 1, kFields = 1, kQBytes = 32, kOffset = 0;
+  static constexpr bool kActQ80 = true;
 };
 
 // Base pointers of this CTA's K split (blockIdx.y); with one split every offset is zero.
@@ -102,7 +111,7 @@ template <int FMT>
 struct Split {
   static __device__ __forceinline__ int64_t nblk(const GemvParams& p) { return p.K / Fmt<FMT>::kBlock; }
   static __device__ __forceinline__ const uint8_t* wq(const GemvParams& p) {
-    return p.wq + (int64_t)blockIdx.y * (p.K / (FMT == 0 ? 2 : 4));
+    return p.wq + (int64_t)blockIdx.y * (p.K / Fmt<FMT>::kBlock * Fmt<FMT>::kQBytes);
   }
   static __device__ __forceinline__ const int16_t* ws(const GemvParams& p) {
     return p.ws + (int64_t)blockIdx.y * nblk(p);
@@ -125,6 +134,7 @@ struct Split {
 template <int FMT>
 __device__ __forceinline__ int perm_unit(int q, int C) {
   if (FMT == 0) return (q & 1) * C + (q >> 1);  // block b = q/2, nibble field h = q%2
+  if (FMT == 2) return q;                        // Q8_0: chunk c holds values 16c .. 16c+15
   const int b = q >> 4, o = q & 15;              // 16 pieces per 256-value block
   const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
   return j * C + 4 * b + c;
@@ -227,7 +237,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
       const int m = idx / nblk, b = idx - m * nblk;
       xscale[idx] = Split<FMT>::xd(p)[(int64_t)m * p.ldxd + b];
     }
-  } else if (FMT == 0) {
+  } else if (Fmt<FMT>::kActQ80) {
     // q8_0: 8 lanes per 32-value block (4 blocks per warp per slot); kUnroll slots of loads in flight per lane
     const int lane = tt & 31, sub = lane & 7, nw = T / 32;
     const bool writer = (blockIdx.x == 0) && (p.xq_out != nullptr);
@@ -250,7 +260,9 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         const uint32_t q = q8_0_quant4(v[u], &d);  // whole warp: shuffles inside
         if (g < total) {
           const int m = g / nblk, b = g - m * nblk;
-          *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + ((sub >> 2) * C + b) * 16 + (sub & 3) * 4) = q;
+          // Q4_0: low / high nibble fields of block b at xs[field][b]; Q8_0: natural order
+          const int pos = FMT == 0 ? ((sub >> 2) * C + b) * 16 + (sub & 3) * 4 : b * 32 + sub * 4;
+          *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + pos) = q;
           const float ds = q8_0_stored_scale(d);
           if (sub == 0) xscale[m * nblk + b] = ds;
           if (writer) {
@@ -311,7 +323,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
       const uint4 v = col[j * C + c];
       sum += bytesum(v.x) + bytesum(v.y) + bytesum(v.z) + bytesum(v.w);
     }
-    xsum[idx] = (FMT == 0) ? 8 * sum : sum;
+    xsum[idx] = Fmt<FMT>::kOffset * sum;
   }
   __syncthreads();
 }
@@ -325,6 +337,12 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
+  if (FMT == 2 && !BYTES) {  // Q8_0: signed weights, no field extraction and no offset
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s = dp4a_ss((int)word_of(w, k), (int)word_of(x[0], k), s);
+    return s;
+  }
   if (!BYTES) {
 #ifndef B2Q_DP4A_SIGNED_ONLY
     if (FMT == 0) {
@@ -387,7 +405,9 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
 #pragma unroll
         for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
           const int xb = (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
-          const int val = (FMT == 0) ? ((wb >> (4 * j)) & 15) - 8 : ((wb >> (2 * j)) & 3) - 1;
+          const int val = (FMT == 0)   ? ((wb >> (4 * j)) & 15) - 8
+                          : (FMT == 1) ? ((wb >> (2 * j)) & 3) - 1
+                                       : (int)(int8_t)wb;
           s += val * xb;
         }
       }
@@ -442,18 +462,17 @@ __device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, in
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int s = chunk_dot<FMT, BYTES>(w[r], xc[m].x, xc[m].sum);
-        if (FMT == 0)
+        if (FMT != 1)  // Q4_0, Q8_0: f32(s) * dw * dx
           acc[r * MC + m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), xc[m].dx, acc[r * MC + m]);
-        else
+        else  // TQ2_0: dx * dw * f32(s)
           acc[r * MC + m] = __fmaf_rn(__fmul_rn(xc[m].dx, dw[r]), (float)s, acc[r * MC + m]);
-        if (STORE) {
+        if (STORE) {  // the block dot: the partial dots of the block's chunks (adjacent lanes) added up
           int sb = s;
-          if (FMT == 1) {
-            sb += __shfl_xor_sync(0xffffffffu, sb, 1);
-            sb += __shfl_xor_sync(0xffffffffu, sb, 2);
-          }
+#pragma unroll
+          for (int sh = 0; sh < Fmt<FMT>::kChunkShift; ++sh) sb += __shfl_xor_sync(0xffffffffu, sb, 1 << sh);
           const int64_t row = g * R + r;
-          if (valid && (FMT == 0 || (c & 3) == 0) && row < p.N) p.s[((int64_t)m * p.N + row) * nblk + blk] = sb;
+          const bool first = (c & ((1 << Fmt<FMT>::kChunkShift) - 1)) == 0;
+          if (valid && first && row < p.N) p.s[((int64_t)m * p.N + row) * nblk + blk] = sb;
         }
       }
     }
@@ -609,6 +628,9 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
       o.x[0] = src[0];
       o.x[1] = src[1];
       o.dx = Split<FMT>::xd(p)[c];
+    } else if (FMT == 2) {
+      o.x[0] = *reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 16);
+      o.dx = Split<FMT>::xd(p)[c >> 1];
     } else {
       const int b = c >> 2, cc = c & 3;
       const int8_t* base = Split<FMT>::xq(p) + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
@@ -620,7 +642,39 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
 #pragma unroll
     for (int j = 0; j < Fmt<FMT>::kFields; ++j)
       sum += bytesum(o.x[j].x) + bytesum(o.x[j].y) + bytesum(o.x[j].z) + bytesum(o.x[j].w);
-    o.sum = (FMT == 0) ? 8 * sum : sum;
+    o.sum = Fmt<FMT>::kOffset * sum;
+    return;
+  }
+  if (FMT == 2) {
+    // q8_0 for Q8_0 weights: chunk c holds values 16c .. 16c+15, the block's other half is on lane c ^ 1. Same
+    // arithmetic as the q8_0 quantizer (amax / 127, roundf(x * id) from the unrounded d, f16-exact stored scale).
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      v[i] = valid ? reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 16)[i]
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q0 = (int)roundf(__fmul_rn(v[i].x, id)), q1 = (int)roundf(__fmul_rn(v[i].y, id));
+      const int q2 = (int)roundf(__fmul_rn(v[i].z, id)), q3 = (int)roundf(__fmul_rn(v[i].w, id));
+      w[i] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+             ((uint32_t)(q3 & 0xff) << 24);
+    }
+    if (!valid) return;
+    o.x[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    o.dx = q8_0_stored_scale(d);
+    if (writer) {
+      *reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 16) = o.x[0];
+      if ((c & 1) == 0 && p.xd_out) Split<FMT>::xd_out(p)[c >> 1] = o.dx;
+    }
     return;
   }
   if (FMT == 0) {

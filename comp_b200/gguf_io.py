@@ -1,4 +1,4 @@
-"""GGUF weight ingest: a Q4_0 / TQ2_0 tensor of a GGUF file -> the GEMV's split planes in GPU memory.
+"""GGUF weight ingest: a Q4_0 / TQ2_0 / Q8_0 tensor of a GGUF file -> the GEMV's split planes in GPU memory.
 
 The tensor's bytes are copied to the GPU as stored (ggml blocks, row after row) and cut into WQ / WS there
 (`host.split_device`, the on-device form of `host.split`, src/komp/host.py:16-22). GGUF lists a 2-D weight's shape as
@@ -10,7 +10,7 @@ import torch
 
 from . import host
 
-GGUF_TYPES = {"Q4_0": "q4_0", "TQ2_0": "tq2_0"}
+GGUF_TYPES = {"Q4_0": "q4_0", "TQ2_0": "tq2_0", "Q8_0": "q8_0"}
 
 
 def tensor_info(reader, name):
@@ -34,6 +34,9 @@ def load_split(path, name, device="cuda", ldwq=None):
 
     reader = gguf.GGUFReader(path)
     fmt, n, k, raw = tensor_info(reader, name)
-    blocks = torch.from_numpy(np.ascontiguousarray(raw).reshape(-1)).to(device)
+    # staged through pinned host memory: the memory-mapped tensor is read once, and the upload is one DMA copy
+    staging = torch.empty(raw.nbytes, dtype=torch.uint8, pin_memory=True)
+    staging.numpy()[:] = np.ascontiguousarray(raw).reshape(-1)
+    blocks = staging.to(device)
     wq, ws = host.split_device(fmt, blocks, n, k, ldwq=ldwq)
     return fmt, wq, ws, n, k

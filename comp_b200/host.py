@@ -17,14 +17,17 @@ import torch
 from . import _lib
 
 # weights: block values, block bytes, quant offset/bytes in the ggml block, scale offset, activation format
-# (the same table as src/komp/host.py:9-12)
+# (q4_0 and tq2_0: the same table as src/komp/host.py:9-12; q8_0 is an extension beyond the reference, ggml
+# block_q8_0 weights multiplied against q8_0 activations)
 FORMATS = {
     "q4_0": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
     "tq2_0": dict(block=256, nbytes=66, qoff=0, qbytes=64, soff=64, act="q8_K"),
+    "q8_0": dict(block=32, nbytes=34, qoff=2, qbytes=32, soff=0, act="q8_0"),
 }
 MODES = {"bytes": 0, "dp4a": 2}  # src/komp/host.py:13
 ACT_BLOCK = {"q8_0": 32, "q8_K": 256}
-FMT_ID = {"q4_0": 0, "tq2_0": 1}
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2}
+GEMV_ENTRY = {"q4_0": "b2q_gemv_q4_0", "tq2_0": "b2q_gemv_tq2_0", "q8_0": "b2q_gemv_q8_0"}
 
 
 def _fmt(fmt):
@@ -236,7 +239,7 @@ def gemv(fmt, wq, ws, xq, xd, n, k, block_n=32, nb=4, mode=0, num_warps=4, store
     xd = xd.contiguous()
     y = torch.empty((m, n), dtype=torch.float32, device=dev)
     s = torch.empty((m, n, k // f["block"]), dtype=torch.int32, device=dev) if store_s else None
-    name = "b2q_gemv_q4_0" if fmt == "q4_0" else "b2q_gemv_tq2_0"
+    name = GEMV_ENTRY[fmt]
     with _on(dev):
         _lib.call(name, wq.data_ptr(), wq.stride(0), ws.data_ptr(), xq.data_ptr(), xd.data_ptr(), y.data_ptr(),
                   s.data_ptr() if store_s else None, n, k, m, mode, _stream(dev))

@@ -44,6 +44,7 @@ typedef struct CUstream_st* b2q_stream_t;
  * All variants return identical int32 block dots and identical Y. Mirrors host.MODES (src/komp/host.py:13). */
 #define B2Q_FMT_Q4_0 0
 #define B2Q_FMT_TQ2_0 1
+#define B2Q_FMT_Q8_0 2 /* extension: ggml block_q8_0 weights (no counterpart in the reference) */
 #define B2Q_VARIANT_BYTES 0
 #define B2Q_VARIANT_DP4A 2
 
@@ -100,9 +101,19 @@ int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int
                    int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
 
 /*
+ * Q8_0 x q8_0 decode GEMV: Y[m][n] = sum_b f32(s[m][n][b]) * dw[n][b] * dx[m][b], s = sum_i wq_i * xq_i (int8 x int8).
+ * An extension beyond the reference (COMP has Q4_0 and TQ2_0 only): the weights are ggml block_q8_0 (f16 d, 32
+ * int8), split like Q4_0 into a quant plane and a scale plane; the activations are the same q8_0 planes as Q4_0's.
+ *   wq: u8 [N][ldwq] (the int8 values, 32 bytes per 32-value block), ws: int16 [N][K/32] (f16 bits),
+ *   xq: int8 [M][K], xd: f32 [M][K/32], y: f32 [M][N], s: int32 [M][N][K/32] or NULL.
+ */
+int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
+
+/*
  * Fused quantizer prologue + GEMV (one launch): every CTA quantizes f32 x into shared memory with exactly the math of
  * b2q_quant_q8_0 / b2q_quant_q8_K, then runs the GEMV. xq/xd (nullable) also receive the quantized activations
- * (written by CTA 0 only), byte-identical to the standalone quantizer. fmt = B2Q_FMT_Q4_0 or B2Q_FMT_TQ2_0.
+ * (written by CTA 0 only), byte-identical to the standalone quantizer. fmt = B2Q_FMT_Q4_0, B2Q_FMT_TQ2_0 or B2Q_FMT_Q8_0.
  * Fuses host.quantize + host.gemv (src/komp/host.py:63-85) into one kernel; no reference counterpart as one call.
  */
 int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
@@ -134,7 +145,8 @@ int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
 
 /*
  * ggml blocks -> split planes on the device (model load path). blocks: n rows of k values as ggml Q4_0 (fmt 0,
- * 18-byte blocks: f16 d, 16 quant bytes) or TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d), row-major,
+ * 18-byte blocks: f16 d, 16 quant bytes), TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d) or Q8_0 (fmt 2,
+ * 34-byte blocks: f16 d, 32 int8), row-major,
  * 16-byte aligned device memory (a GGUF tensor's bytes as stored). Writes WQ [n][ldwq] (ldwq >= quant bytes per row,
  * multiple of 16) and WS [n][k/blk] int16 (f16 bits), exactly host.split's planes. Replaces the host-side numpy cut
  * of src/komp/host.py:16-22 for weights already on the GPU.

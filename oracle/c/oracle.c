@@ -131,14 +131,22 @@ static int32_t dot_tq2_0(const uint8_t* q, const int8_t* x) {
   return s;
 }
 
+/* Exact int32 dot of one Q8_0 block (32 int8 weights) with 32 int8 activations (an extension: ggml block_q8_0). */
+static int32_t dot_q8_0(const uint8_t* q, const int8_t* x) {
+  int32_t s = 0;
+  for (int i = 0; i < 32; ++i) s += (int32_t)(int8_t)q[i] * x[i];
+  return s;
+}
+
 /*
- * y[m][n] = KURN reference dot (f64, sequential over blocks; q4_0: (dw*dx)*s, tq2_0: (dx*dw)*s, dx of q8_0 read back
- * as its f16), s (nullable) = int32 block dots [M][N][nb]. nthreads <= 0 uses the OpenMP default.
+ * y[m][n] = KURN reference dot (f64, sequential over blocks; q4_0 / q8_0: (dw*dx)*s, tq2_0: (dx*dw)*s, dx of q8_0
+ * activations read back as its f16), s (nullable) = int32 block dots [M][N][nb]. fmt: 0 Q4_0, 1 TQ2_0, 2 Q8_0.
+ * nthreads <= 0 uses the OpenMP default.
  */
 void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd,
               int64_t N, int64_t K, int64_t M, double* y, int32_t* s, int nthreads) {
-  const int blk = fmt == 0 ? 32 : 256;
-  const int qb = fmt == 0 ? 16 : 64;
+  const int blk = fmt == 1 ? 256 : 32;
+  const int qb = fmt == 0 ? 16 : fmt == 1 ? 64 : 32;
   const int64_t nb = K / blk;
 #ifdef _OPENMP
   if (nthreads > 0) omp_set_num_threads(nthreads);
@@ -152,12 +160,14 @@ void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const
       const int8_t* xr = xq + m * K;
       double total = 0.0;
       for (int64_t b = 0; b < nb; ++b) {
-        const int32_t d = fmt == 0 ? dot_q4_0(row + b * qb, xr + b * blk) : dot_tq2_0(row + b * qb, xr + b * blk);
+        const int32_t d = fmt == 0   ? dot_q4_0(row + b * qb, xr + b * blk)
+                          : fmt == 1 ? dot_tq2_0(row + b * qb, xr + b * blk)
+                                     : dot_q8_0(row + b * qb, xr + b * blk);
         if (s) s[(m * N + n) * nb + b] = d;
         const double dw = (double)orc_half_to_float((uint16_t)ws[n * nb + b]);
         double dx = (double)xd[m * nb + b];
-        if (fmt == 0) dx = (double)orc_half_to_float(orc_float_to_half(xd[m * nb + b]));
-        const double scale = fmt == 0 ? dw * dx : dx * dw;
+        if (fmt != 1) dx = (double)orc_half_to_float(orc_float_to_half(xd[m * nb + b]));
+        const double scale = fmt != 1 ? dw * dx : dx * dw;
         total += scale * (double)d;
       }
       y[m * N + n] = total;

@@ -7,10 +7,14 @@ results are bit-identical, not approximate.
 
 import numpy as np
 
-BLOCK = {"q4_0": 32, "tq2_0": 256}
-ACT = {"q4_0": "q8_0", "tq2_0": "q8_K"}
-QBYTES = {"q4_0": 16, "tq2_0": 64}
-NBYTES = {"q4_0": 18, "tq2_0": 66}
+# q8_0 weights are an extension beyond the reference (which has Q4_0 and TQ2_0 only): ggml's Q8_0 block of an f16 scale
+# and 32 int8 values, against q8_0 activations, with Q4_0's multiply order; pinned to gguf-py's Q8_0 codec.
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32}
+ACT = {"q4_0": "q8_0", "tq2_0": "q8_K", "q8_0": "q8_0"}
+QBYTES = {"q4_0": 16, "tq2_0": 64, "q8_0": 32}
+NBYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34}
+QOFF = {"q4_0": 2, "tq2_0": 0, "q8_0": 2}
+SOFF = {"q4_0": 0, "tq2_0": 64, "q8_0": 0}
 TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:113)
 
 F32 = np.float32
@@ -121,8 +125,14 @@ def decode_tq2_0(wq, k):
     return (vals.astype(np.int8) - 1).reshape(n, k)
 
 
+def decode_q8_0(wq, k):
+    """Q8_0 quant plane uint8 [n][k] -> int8 values [n][k] (ggml block_q8_0.qs, natural order)."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    return wq[:, :k].view(np.int8).copy()
+
+
 def decode(fmt, wq, k):
-    return decode_q4_0(wq, k) if fmt == "q4_0" else decode_tq2_0(wq, k)
+    return {"q4_0": decode_q4_0, "tq2_0": decode_tq2_0, "q8_0": decode_q8_0}[fmt](wq, k)
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -154,13 +164,13 @@ def reference_dot(fmt, ws, xd, s):
     dw = np.asarray(ws, dtype=np.int16).view(np.float16).astype(np.float64)  # [n][nb]
     xd = np.asarray(xd, dtype=np.float32)
     # q8_0 blocks carry an f16 scale (the stored xd is already f16-exact); q8_K blocks carry the f32 scale
-    dx = (xd.astype(np.float16) if fmt == "q4_0" else xd).astype(np.float64)  # [m][nb]
+    dx = (xd.astype(np.float16) if ACT[fmt] == "q8_0" else xd).astype(np.float64)  # [m][nb]
     s = np.asarray(s)
     m, n, nb = s.shape
     total = np.zeros((m, n), dtype=np.float64)
     for b in range(nb):
         sb = s[:, :, b].astype(np.float64)
-        if fmt == "q4_0":
+        if fmt in ("q4_0", "q8_0"):
             total += (dw[None, :, b] * dx[:, None, b]) * sb
         else:
             total += (dx[:, None, b] * dw[None, :, b]) * sb
@@ -208,8 +218,9 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
     """ggml weight blocks (bytes) for n rows of k values.
 
     random:  q4_0 quant bytes uniform 0..255, d = f16(|N(0, 0.02)|); tq2_0 crumbs uniform {0,1,2},
-             d = f16(|N(0, 0.05)|).
-    extreme: q4_0 nibbles only 0 or 15; tq2_0 crumbs 0, 2 and 3 (3 decodes to +2); scales include 0, f16 subnormals,
+             d = f16(|N(0, 0.05)|); q8_0 values uniform -127..127, d = f16(|N(0, 0.002)|).
+    extreme: q4_0 nibbles only 0 or 15; tq2_0 crumbs 0, 2 and 3 (3 decodes to +2); q8_0 values -128, -127 and 127;
+             scales include 0, f16 subnormals,
              the largest normal f16 below 2^8 and negative scales."""
     blk = BLOCK[fmt]
     nb = k // blk
@@ -221,6 +232,11 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
             nib = rng.integers(0, 16, size=(n, nb, 32), dtype=np.uint8)
         q = (nib[:, :, :16] | (nib[:, :, 16:] << 4)).astype(np.uint8)
         sd = 0.02
+    elif fmt == "q8_0":
+        vals = rng.choice(np.array([-128, -127, 127], dtype=np.int8), size=(n, nb, 32)) if extreme else \
+            rng.integers(-127, 128, size=(n, nb, 32)).astype(np.int8)
+        q = vals.view(np.uint8)
+        sd = 0.002
     else:
         crumbs = rng.choice(np.array([0, 2, 3], dtype=np.uint8), size=(n, nb, 256)) if extreme else \
             rng.integers(0, 3, size=(n, nb, 256), dtype=np.uint8)
@@ -234,8 +250,7 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
         pick = rng.choice(flat.size, size=min(flat.size, 8), replace=False)
         specials = np.array([0.0, 6e-8, 3e-5, 255.9, -0.75, -1e-3, 1.0, 2.0 ** -14], dtype=np.float16)
         flat[pick] = specials[: pick.size]
-    qoff = 2 if fmt == "q4_0" else 0
-    soff = 0 if fmt == "q4_0" else 64
+    qoff, soff = QOFF[fmt], SOFF[fmt]
     out[:, :, qoff : qoff + QBYTES[fmt]] = q
     out[:, :, soff : soff + 2] = d.view(np.uint8).reshape(n, nb, 2)
     return out.tobytes()
@@ -302,8 +317,7 @@ def split(fmt, W, n, k):
     """ggml blocks -> (WQ uint8 [n][qbytes*k/blk], WS int16 [n][k/blk]) (src/komp/host.py:16-22)."""
     blk = BLOCK[fmt]
     b = np.frombuffer(W, dtype=np.uint8).reshape(n, k // blk, NBYTES[fmt])
-    qoff = 2 if fmt == "q4_0" else 0
-    soff = 0 if fmt == "q4_0" else 64
+    qoff, soff = QOFF[fmt], SOFF[fmt]
     wq = np.ascontiguousarray(b[:, :, qoff : qoff + QBYTES[fmt]]).reshape(n, -1)
     ws = np.ascontiguousarray(b[:, :, soff : soff + 2]).view(np.int16).reshape(n, k // blk)
     return wq, ws
@@ -316,6 +330,9 @@ def random_split(fmt, rng, n, k):
     if fmt == "q4_0":
         wq = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
         d = np.abs(rng.normal(0.0, 0.02, size=(n, nb))).astype(np.float16)
+    elif fmt == "q8_0":
+        wq = rng.integers(-127, 128, size=(n, k), dtype=np.int8).view(np.uint8)
+        d = np.abs(rng.normal(0.0, 0.002, size=(n, nb))).astype(np.float16)
     else:
         # crumbs uniform in {0,1,2}: draw each byte's 4 crumbs from base-3 digits of a uniform 0..80
         t = rng.integers(0, 81, size=(n, k // 4), dtype=np.uint8)

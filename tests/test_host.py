@@ -87,7 +87,7 @@ def test_compute_calls_refuse_cpu_tensors():
         host.gemv("q4_0", torch.zeros((2, 32), dtype=torch.uint8), torch.zeros((2, 2), dtype=torch.int16),
                   torch.zeros((1, 64), dtype=torch.int8), torch.zeros((1, 2)), 2, 64)
     with pytest.raises(ValueError, match="unknown weight format"):
-        host.quantize("q8_0", x)
+        host.quantize("q5_K", x)
 
 
 def test_partition_covers_rows_once():

@@ -1,4 +1,4 @@
-"""GGUF ingest (comp_b200.gguf_io): a Q4_0 / TQ2_0 tensor written with gguf-py is read back as the same ggml block
+"""GGUF ingest (comp_b200.gguf_io): a Q4_0 / TQ2_0 / Q8_0 tensor written with gguf-py is read back as the same ggml block
 bytes with KURN's (n, k); host.split of those bytes is the reference's plane cut (src/komp/host.py:16-22). The
 on-device cut (host.split_device, b2q_split_blocks) is checked against host.split in tests/test_gpu_parity.py."""
 
@@ -26,7 +26,7 @@ def _write(path, tensors):
 def test_gguf_tensor_round_trip_and_split(tmp_path):
     rng = np.random.default_rng(61)
     specs = [("blk.0.ffn_down.weight", "q4_0", 37, 416), ("blk.0.ffn_gate.weight", "tq2_0", 5, 768),
-             ("output.weight", "q4_0", 64, 4096)]
+             ("output.weight", "q4_0", 64, 4096), ("blk.0.ffn_up.weight", "q8_0", 11, 1024)]
     tensors = [(name, fmt, ref.weight_blocks(fmt, rng, n, k), n, k) for name, fmt, n, k in specs]
     path = tmp_path / "t.gguf"
     _write(path, tensors)

@@ -63,20 +63,46 @@ def test_gemv_oracle_matches_reference(golden, cid):
     assert np.array_equal(rc.view(np.uint64), r.view(np.uint64))  # C and numpy reference dots: bit-identical
 
 
-@pytest.mark.parametrize("fmt", ["q4_0", "tq2_0"])
+@pytest.mark.parametrize("fmt", ["q4_0", "tq2_0", "q8_0"])
 def test_decode_matches_gguf_dequantize(fmt):
     gq = pytest.importorskip("gguf.quants")
     gguf = pytest.importorskip("gguf")
     n, k = 7, 1024
-    W, _ = ref.problem(fmt, n, k, 1, seed=4, extreme=(fmt == "q4_0"))
+    W, _ = ref.problem(fmt, n, k, 1, seed=4, extreme=(fmt != "tq2_0"))
     wq, ws = ref.split(fmt, W, n, k)
-    t = gguf.GGMLQuantizationType.Q4_0 if fmt == "q4_0" else gguf.GGMLQuantizationType.TQ2_0
+    t = getattr(gguf.GGMLQuantizationType, fmt.upper())
     deq = gq.dequantize(np.frombuffer(W, dtype=np.uint8).reshape(n, -1), t).astype(np.float64)
     vals = ref.decode(fmt, wq, k).astype(np.float64)
     blk = ref.BLOCK[fmt]
     d = ws.view(np.float16).astype(np.float64).repeat(blk, axis=1)
     assert np.allclose(deq, vals * d, rtol=0, atol=1e-3 * np.abs(d).max())
     assert np.array_equal(np.sign(deq), np.sign(vals * d))
+
+
+@pytest.mark.parametrize("extreme", [False, True])
+def test_q8_0_gemv_oracle_pinned_to_gguf(extreme):
+    """Q8_0 weights (an extension beyond the reference) against q8_0 activations: the oracle's int32 block dots and
+    f64 reference dot equal the float64 product of gguf-py's own dequantization of both operands (weights read as
+    ggml Q8_0 blocks, activations as the q8_0 blocks the quantizer stores), and the C oracle agrees bit for bit."""
+    gq = pytest.importorskip("gguf.quants")
+    gguf = pytest.importorskip("gguf")
+    n, k, m = 9, 2048, 3
+    W, x = ref.problem("q8_0", n, k, m, seed=12, extreme=extreme)
+    wq, ws = ref.split("q8_0", W, n, k)
+    xq, xd = ref.quantize("q8_0", x)
+    r, s = ref.gemv("q8_0", wq, ws, xq, xd, k)
+    # block dots: int8 x int8 of the stored values
+    vals = ref.decode("q8_0", wq, k).astype(np.int64).reshape(n, k // 32, 32)
+    want_s = np.einsum("nbv,mbv->mnb", vals, xq.astype(np.int64).reshape(m, k // 32, 32))
+    assert np.array_equal(s, want_s)
+    T = gguf.GGMLQuantizationType.Q8_0
+    wdq = gq.dequantize(np.frombuffer(W, dtype=np.uint8).reshape(n, -1), T).astype(np.float64)
+    from comp_b200 import host
+
+    xdq = gq.dequantize(np.frombuffer(host.q8_0_blocks(xq, xd), dtype=np.uint8).reshape(m, -1), T).astype(np.float64)
+    assert ref.relerr(xdq @ wdq.T, r) <= 1e-9
+    rc, sc = native.gemv("q8_0", wq, ws, xq, xd, k, want_s=True)
+    assert np.array_equal(sc, s) and np.array_equal(rc.view(np.uint64), r.view(np.uint64))
 
 
 def test_dp4a_and_decode_probes_match_reference(golden):
