@@ -40,6 +40,7 @@ SIGNATURES = {
     "b2q_set_warps": (INT, [INT]),
     "b2q_set_cluster": (INT, [INT]),
     "b2q_set_gemm_min_columns": (INT, [INT]),
+    "b2q_set_gemm_schedule": (INT, [INT]),
     "b2q_set_splitk": (INT, [INT]),
     "b2q_device_error": (INT, [ctypes.POINTER(ctypes.c_int), INT]),
     "b2q_ipc_get_handle": (INT, [P, P, ctypes.POINTER(ctypes.c_uint64)]),

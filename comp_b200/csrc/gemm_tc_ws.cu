@@ -1,0 +1,701 @@
+// Warp-specialized, persistent tensor-core GEMM (tcgen05 kind::i8) for the fused quantize + GEMM path with many
+// activation columns (M >= 8: prefill, batched or speculative decode).
+//
+// Same results as gemm_tc.cu and the GEMVs: every int32 block dot is exact, and Y adds the per-block f32 products in
+// the reference's multiply order (Q4_0 / Q8_0: f32(s) * dw * dx; TQ2_0: dx * dw * f32(s); kernels.py:93, 141), blocks
+// in ascending order -- so Y is bit-identical to the other schedules. What changes is who does what:
+//   * a prep kernel quantizes the f32 activations with the math of b2q_quant_q8_0 / b2q_quant_q8_K straight into the
+//     MMA operand layout (per column tile of NT columns and 32-value unit: one NT x 32-byte K-major tile of 8 x 16-byte
+//     core matrices), and writes per column and weight block the scale dx and koff = 0x4B400000 - offset * sum(x)
+//     (the weights' offset and the exact int-to-float conversion of gemm_tc.cu folded into one integer add);
+//   * warp 8 (producer) streams per stage -- 128 packed weight bytes of each of the tile's 128 rows -- the rows'
+//     weights (one 2-D TMA tensor copy of a 128-row x 128-byte box, 128-byte swizzled so that the unpacking reads are
+//     free of bank conflicts; rows past N read as zeros), the stage's activation tiles and its (dx, koff) pairs (one
+//     bulk copy each) into a ring of P stages;
+//   * warps 4-7 (thread r = tile row r) unpack each 32-value unit of their row into the MMA's A tile (a ring of RA
+//     tiles);
+//   * one thread of warp 9 issues each unit's MMA (M = 128, N = NT, K = 32) into its block's accumulator (a ring of
+//     RT accumulators in tensor memory) and commits completions to the mbarriers the other roles wait on;
+//   * warps 0-3 (thread t = tile row t = tensor-memory lane t) run each weight block's epilogue: its NT exact int32
+//     dots from tensor memory, scaled and summed into NT f32 registers in block order; each row's block scales come
+//     through a per-thread cp.async ring.
+// Unpacking and epilogue run in separate warps so that their latency chains overlap (measured: with one set of warps
+// doing both, each 32-value unit cost the sum of both chains and the MMA warp sat idle most of the time).
+// The CTAs are persistent: CTA i takes the (row tile, column tile) pairs i, i + gridDim.x, ...; the stage ring and
+// the unit / block counters run on across tile boundaries. Roles synchronize only through mbarriers (no CTA barrier in
+// the loop). Every wait is bounded: a timeout sets the device error word and ends all roles, which then wait (bounded)
+// for their copies and MMAs in flight, and the tensor memory is freed.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "tc_device.cuh"
+
+namespace b2q {
+
+struct WsParams {
+  CUtensorMap wmap;   // the weights' quant plane as a 2-D byte tensor [N][row bytes], 128 x 128-byte boxes, 128B swizzle
+  const uint8_t* wq;
+  int64_t ldwq;
+  const int16_t* ws;
+  int64_t ldws;
+  const int8_t* xt;   // activation tiles [nct][K/32][NT*32]
+  const int32_t* dk;  // [nct][nblk][2][NT]: dx (f32 bits), koff
+  float* y;
+  int64_t ldy;
+  int64_t row0;
+  int64_t N;
+  int64_t K;
+  int M;
+  int nct;     // column tiles
+  int ntiles;  // row tiles x column tiles
+};
+
+// Pipeline shape per weight format and column tile. A stage is 128 packed weight bytes of each row: 8 Q4_0 blocks,
+// 2 TQ2_0 blocks or 4 Q8_0 blocks (SU 32-value units). Roles hand work over in groups of GU units (one barrier phase,
+// one fence and one commit per group, not per unit). P is chosen so that two CTAs fit on an SM where the registers
+// allow it (NT <= 32).
+template <int FMT, int NT>
+struct WsCfg {
+  static constexpr int UPB = FMT == 1 ? 8 : 1;                    // units per weight block
+  static constexpr int WU = FMT == 0 ? 16 : FMT == 1 ? 8 : 32;   // packed weight bytes per unit and row
+  static constexpr int RB = 128;                                  // packed weight bytes per row and stage
+  static constexpr int SU = RB / WU;                              // units per stage
+  static constexpr int SB = SU / UPB;                             // weight blocks per stage
+  static constexpr int RAW = 128 * RB;                            // the weight box (128B-swizzled rows)
+  static constexpr int BT = NT * 32;                              // one unit's activation tile
+  static constexpr int BST = SU * BT;
+  static constexpr int DKB = 2 * NT * 4;                          // (dx, koff) of one block
+  static constexpr int DKS = SB * DKB;
+  static constexpr int STAGE = (RAW + BST + DKS + 1023) / 1024 * 1024;  // swizzled boxes start on 1024 bytes
+  static constexpr int P = FMT == 0 ? (NT == 16 ? 3 : NT == 32 ? 2 : NT == 64 ? 4 : 3)
+                                    : FMT == 1 ? (NT == 16 || NT == 64 ? 3 : 2) : (NT <= 32 ? 3 : 4);
+  static constexpr int GU = NT == 128 && UPB == 1 ? 2 : 4;         // units per hand-over group
+  static constexpr int RAG = 2;                                   // A-tile groups in flight
+  static constexpr int RA = RAG * GU;                             // A tiles
+  static constexpr int ATILE = 128 * 32;
+  static constexpr int AG = UPB == 1 ? GU : 1;                    // blocks per accumulator group
+  static constexpr int RTG = 2;                                   // accumulator groups in flight
+  static constexpr int RT = RTG * AG;                             // accumulators (blocks) in tensor memory
+  static constexpr int BB = NT == 16 && AG % 2 == 0 ? 2 : 1;      // blocks per tensor-memory round trip
+  static constexpr int CW = NT <= 32 ? NT : 32;                   // columns per round trip
+  static constexpr int SBB = SB * 2;                              // scale bytes per row and stage (16, 4 or 8)
+  static constexpr int PS = 3, LA = 2;                            // scale ring depth, prefetch distance (stages)
+  static constexpr int TCOLS = RT * NT <= 32 ? 32 : RT * NT <= 64 ? 64 : RT * NT <= 128 ? 128 : RT * NT <= 256 ? 256
+                                                                                                           : 512;
+  // + 1024: the kernel aligns its base to 1024 bytes (the swizzle pattern follows the shared-memory address bits)
+  static constexpr size_t SMEM = (size_t)P * STAGE + (size_t)RA * ATILE + (size_t)PS * 128 * SBB + 1024;
+  // registers are allocated per SM sub-partition (16K each) and a CTA's 10 warps land on them 3, 3, 2, 2: two CTAs
+  // put 6 warps on one sub-partition, so two CTAs per SM need at most 85 registers a thread; one CTA at most 170
+  static constexpr int MAXREG = NT <= 32 ? 80 : 168;
+  static_assert(PS >= LA + 1, "scale ring: the slot refilled at a stage's start is no longer read");
+  static_assert(SU % GU == 0 && SB % AG == 0 && (UPB == 1 || UPB % GU == 0), "groups never straddle stages");
+  static_assert(RT * NT <= 512 && NT % 16 == 0 && CW % 16 == 0, "tensor memory");
+};
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// 2-D TMA tensor copy of the box at (x bytes, y rows) into this CTA's shared memory (the weights: this GPU's own
+// memory), completion counted in bytes on `bar`
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                            uint64_t pol, bool hint) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  if (hint)
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar), "l"(pol)
+        : "memory");
+  else
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_plain(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// One 32-value unit of row r -> its row of an A tile, as unsigned (Q4_0, TQ2_0) or signed (Q8_0) bytes in value order.
+// raw: the row's 128 bytes of the stage, whose 16-byte chunk c sits at chunk c ^ (r % 8) (TMA 128B swizzle).
+template <int FMT>
+__device__ __forceinline__ void unpack_unit(uint32_t raw, int sw, int u, uint8_t* at, int r, const uint4 (&tq)[2]) {
+  uint4 lo, hi;
+  if (FMT == 0) {
+    const uint4 w = lds_v4(raw + (uint32_t)((u ^ sw) << 4));
+    lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+    hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                    (w.w >> 4) & 0x0F0F0F0Fu);
+  } else if (FMT == 2) {
+    lo = lds_v4(raw + (uint32_t)(((2 * u) ^ sw) << 4));
+    hi = lds_v4(raw + (uint32_t)(((2 * u + 1) ^ sw) << 4));
+  } else {  // TQ2_0 k-step s = u % 8 of a block: values 32s..32s+31 = field s % 4 of the (preloaded) 32 bytes tq
+    const int sh = 2 * (u & 3);
+    lo = make_uint4((tq[0].x >> sh) & 0x03030303u, (tq[0].y >> sh) & 0x03030303u, (tq[0].z >> sh) & 0x03030303u,
+                    (tq[0].w >> sh) & 0x03030303u);
+    hi = make_uint4((tq[1].x >> sh) & 0x03030303u, (tq[1].y >> sh) & 0x03030303u, (tq[1].z >> sh) & 0x03030303u,
+                    (tq[1].w >> sh) & 0x03030303u);
+  }
+  *reinterpret_cast<uint4*>(at + tc::core_off(r, 0)) = lo;
+  *reinterpret_cast<uint4*>(at + tc::core_off(r, 16)) = hi;
+}
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
+    gemm_tc_ws_kernel(const __grid_constant__ WsParams p) {
+  using C = WsCfg<FMT, NT>;
+  constexpr int P = C::P, SU = C::SU, SB = C::SB, RA = C::RA, RT = C::RT, UPB = C::UPB, PS = C::PS, LA = C::LA;
+  constexpr int GU = C::GU, RAG = C::RAG, AG = C::AG, RTG = C::RTG;
+  extern __shared__ __align__(1024) uint8_t ws_smem[];
+  __shared__ __align__(8) uint64_t bar_full[P], bar_empty[P], bar_afull[RAG], bar_aempty[RAG], bar_accf[RTG],
+      bar_acce[RTG];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const uint32_t sbase = (smem_addr(ws_smem) + 1023u) & ~1023u;
+  const uint32_t a_base = sbase + P * C::STAGE;
+  const uint32_t sc_base = a_base + RA * C::ATILE;
+  const int nunits = (int)(p.K / 32);
+  const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
+  const int S = nunits / SU;  // stages per tile
+  const int my_tiles = (int)blockIdx.x < p.ntiles ? (p.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total_stages = my_tiles * S;
+  volatile int* abort_flag = &s_abort;
+  // the abort flag as lane 0 of the warp sees it, so that every lane takes the same branch (full-warp syncs follow)
+  auto aborted = [&]() { return __shfl_sync(0xffffffffu, *abort_flag, 0) != 0; };
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
+                 "n"(C::TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (t == 0) {
+    for (int i = 0; i < P; ++i) {
+      mbar_init(smem_addr(&bar_full[i]), 1);
+      mbar_init(smem_addr(&bar_empty[i]), 4 + 4 + 1);  // unpack warps, epilogue warps, the MMA commit
+    }
+    for (int i = 0; i < RAG; ++i) {
+      mbar_init(smem_addr(&bar_afull[i]), 4);
+      mbar_init(smem_addr(&bar_aempty[i]), 1);
+    }
+    for (int i = 0; i < RTG; ++i) {
+      mbar_init(smem_addr(&bar_accf[i]), 1);
+      mbar_init(smem_addr(&bar_acce[i]), 4);
+    }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = s_tmem;
+
+  // (row tile, column tile, stage within the tile) of this CTA's global stage G
+  auto stage_tile = [&](int G, int& rt, int& ct, int& s) {
+    const int k = G / S;
+    s = G - k * S;
+    const int tile = (int)blockIdx.x + k * (int)gridDim.x;
+    rt = tile / p.nct;
+    ct = tile - rt * p.nct;
+  };
+
+  int issued = 0;    // producer: stages whose copies were issued
+  int g_issued = 0;  // MMA thread: unit groups issued
+  if (warp == 8) {
+    // ---------------- producer ----------------
+    const bool stream_once = p.nct == 1;  // several column tiles re-read the weights from L2: no evict-first hint
+    const uint64_t pol = evict_first_policy();
+    auto issue_weights = [&](int G) {
+      if (lane == 0) {
+        int rt, ct, s;
+        stage_tile(G, rt, ct, s);
+        const uint32_t bar = smem_addr(&bar_full[G % P]);
+        // the whole box counts, rows past N included (filled with zeros)
+        mbar_expect_tx(bar, (uint32_t)(C::RAW + C::BST + C::DKS));
+        tma_load_2d(sbase + (uint32_t)((G % P) * C::STAGE), &p.wmap, s * C::RB, rt * 128, bar, pol, stream_once);
+      }
+    };
+    auto issue_acts = [&](int G) {
+      if (lane == 0) {
+        int rt, ct, s;
+        stage_tile(G, rt, ct, s);
+        const uint32_t bar = smem_addr(&bar_full[G % P]);
+        const uint32_t st = sbase + (uint32_t)((G % P) * C::STAGE);
+        bulk_g2s_plain(st + C::RAW, p.xt + ((int64_t)ct * nunits + (int64_t)s * SU) * C::BT, C::BST, bar);
+        bulk_g2s_plain(st + C::RAW + C::BST,
+                       reinterpret_cast<const uint8_t*>(p.dk) + ((int64_t)ct * nblk + (int64_t)s * SB) * C::DKB,
+                       C::DKS, bar);
+      }
+    };
+    // the first stages' weights before waiting for the prep kernel (weights do not depend on it)
+    const int pre = min(P, total_stages);
+    for (int G = 0; G < pre; ++G) issue_weights(G);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int G = 0; G < pre; ++G) issue_acts(G);
+    issued = pre;
+    for (int G = pre; G < total_stages; ++G) {
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(smem_addr(&bar_empty[G % P]), (uint32_t)(((G / P) & 1) ^ 1), kWaitLimit);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      if (aborted()) break;
+      issue_weights(G);
+      issue_acts(G);
+      issued = G + 1;
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::instr_desc(NT, FMT == 2);  // Q8_0 weights are signed
+      const int total_groups = total_stages * (SU / GU);
+      bool ok = true;
+      for (int g = 0; g < total_groups && ok && !*abort_flag; ++g) {
+        const int U0 = g * GU, G = U0 / SU, u0 = U0 - G * SU;
+        if (u0 == 0) ok = mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1), kWaitLimit);
+        if (ok) ok = mbar_wait(smem_addr(&bar_afull[g % RAG]), (uint32_t)((g / RAG) & 1), kWaitLimit);
+        if (!ok) break;
+        const uint32_t bst = sbase + (uint32_t)((G % P) * C::STAGE + C::RAW);
+        const uint32_t at = a_base + (uint32_t)((g % RAG) * GU * C::ATILE);
+#pragma unroll
+        for (int i = 0; i < GU; ++i) {
+          const int U = U0 + i, B = U / UPB, ub = U - B * UPB;
+          if (ub == 0 && B % AG == 0) {  // the first block of an accumulator group: its accumulators are free
+            const int a = B / AG;
+            ok = mbar_wait(smem_addr(&bar_acce[a % RTG]), (uint32_t)(((a / RTG) & 1) ^ 1), kWaitLimit);
+            if (!ok) break;
+          }
+          tc::fence_after();
+          tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)),
+                     tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT)), idesc, ub > 0 ? 1u : 0u);
+          if (ub == UPB - 1 && B % AG == AG - 1) tc::mma_commit(smem_addr(&bar_accf[(B / AG) % RTG]));
+        }
+        if (!ok) break;
+        tc::mma_commit(smem_addr(&bar_aempty[g % RAG]));
+        if (u0 + GU == SU) tc::mma_commit(smem_addr(&bar_empty[G % P]));  // the stage's activation tiles are read
+        g_issued = g + 1;
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp >= 4) {
+    // ---------------- unpack (warps 4-7): thread r = tile row r ----------------
+    const int r = t - 128;
+    const int sw = r & 7;
+    uint8_t* const a_ptr = ws_smem + (a_base - smem_addr(ws_smem));
+    const int total_groups = total_stages * (SU / GU);
+    uint32_t raw = 0;
+    bool ok = true;
+    for (int g = 0; g < total_groups; ++g) {
+      const int U0 = g * GU, G = U0 / SU, u0 = U0 - G * SU;
+      if (u0 == 0) {
+        const bool got = __all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1),
+                                                            kWaitLimit));
+        if (!got) ok = false;
+        if (!got || aborted()) break;
+        raw = sbase + (uint32_t)((G % P) * C::STAGE + r * C::RB);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_aempty[g % RAG]), (uint32_t)(((g / RAG) & 1) ^ 1),
+                                              kWaitLimit))) {
+        ok = false;
+        break;
+      }
+      uint8_t* at = a_ptr + (g % RAG) * GU * C::ATILE;
+      uint4 tq[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+      if (FMT == 1) {  // the group's 4 k-steps are the 4 fields of the same 32 bytes: (block, half) = (u0 / 8, u0 % 8 / 4)
+        const int c0 = (u0 >> 3) * 4 + ((u0 & 7) >> 2) * 2;
+        tq[0] = lds_v4(raw + (uint32_t)((c0 ^ sw) << 4));
+        tq[1] = lds_v4(raw + (uint32_t)(((c0 + 1) ^ sw) << 4));
+      }
+#pragma unroll
+      for (int i = 0; i < GU; ++i) unpack_unit<FMT>(raw, sw, u0 + i, at + i * C::ATILE, r, tq);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_addr(&bar_afull[g % RAG]));
+        if (u0 + GU == SU) mbar_arrive(smem_addr(&bar_empty[G % P]));  // this warp is done with the stage's weights
+      }
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+  } else {
+    // ---------------- epilogue (warps 0-3): thread t = tile row t = tensor-memory lane t ----------------
+    constexpr float kMagic = 12582912.0f;  // 2^23 + 2^22
+    constexpr int BB = C::BB, CW = C::CW;
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    float acc[NT];
+#pragma unroll
+    for (int c = 0; c < NT; ++c) acc[c] = 0.f;
+    // this row's block scales of stage G, LA stages ahead, into its own slot of the scale ring
+    auto prefetch_scales = [&](int G) {
+      if (G < total_stages) {
+        int rt, ct, s;
+        stage_tile(G, rt, ct, s);
+        const int64_t row = (int64_t)rt * 128 + t;
+        const bool ok = row < p.N;
+        cp_async_ca<C::SBB>(sc_base + (uint32_t)(((G % PS) * 128 + t) * C::SBB),
+                            p.ws + (ok ? row : 0) * p.ldws + (int64_t)s * SB, ok);
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int G = 0; G < LA; ++G) prefetch_scales(G);
+    const int total_agroups = my_tiles * nblk / AG;
+    int ep_k = 0, ep_b = 0;  // tile of this CTA's list and block in the tile
+    bool ok = true;
+    for (int a = 0; a < total_agroups; ++a) {
+      const int B0 = a * AG, GB = B0 / SB, j0 = B0 - GB * SB;
+      if (j0 == 0) {  // a new stage: scales LA stages ahead; this stage's (dx, koff) have landed
+        prefetch_scales(GB + LA);
+        cp_async_wait<LA>();
+        const bool got = __all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_full[GB % P]), (uint32_t)((GB / P) & 1),
+                                                            kWaitLimit));
+        if (!got) ok = false;
+        if (!got || aborted()) break;
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_accf[a % RTG]), (uint32_t)((a / RTG) & 1), kWaitLimit))) {
+        ok = false;
+        break;
+      }
+      tc::fence_after();
+      const uint32_t dk0 = sbase + (uint32_t)((GB % P) * C::STAGE + C::RAW + C::BST);
+      const uint32_t sc0 = sc_base + (uint32_t)(((GB % PS) * 128 + t) * C::SBB);
+#pragma unroll
+      for (int jb = 0; jb < AG; jb += BB) {
+#pragma unroll
+        for (int c0 = 0; c0 < NT; c0 += CW) {
+          uint32_t v[BB][CW];
+#pragma unroll
+          for (int bb = 0; bb < BB; ++bb)
+#pragma unroll
+            for (int h = 0; h < CW; h += 16)
+              tc::tmem_ld16_nowait(tmem + lane_base + (uint32_t)(((B0 + jb + bb) % RT) * NT + c0 + h),
+                                   *reinterpret_cast<uint32_t(*)[16]>(&v[bb][h]));
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int bb = 0; bb < BB; ++bb) {  // blocks in ascending order: the sum order of the reference
+            const int j = j0 + jb + bb;
+            const uint32_t dkp = dk0 + (uint32_t)(j * C::DKB);
+            const float dw = f16_bits_to_f32(lds_u16(sc0 + (uint32_t)(j * 2)));
+            const float2 dw2 = make_float2(dw, dw);
+#pragma unroll
+            for (int q = 0; q < CW; q += 4) {
+              const uint4 dx4 = lds_v4(dkp + (uint32_t)((c0 + q) * 4));
+              const uint4 ko4 = lds_v4(dkp + (uint32_t)((NT + c0 + q) * 4));
+              const float dxs[4] = {__uint_as_float(dx4.x), __uint_as_float(dx4.y), __uint_as_float(dx4.z),
+                                    __uint_as_float(dx4.w)};
+              const int kos[4] = {(int)ko4.x, (int)ko4.y, (int)ko4.z, (int)ko4.w};
+#pragma unroll
+              for (int e = 0; e < 4; e += 2) {
+                const int c = c0 + q + e;
+                const float2 f = __fadd2_rn(make_float2(__int_as_float((int)v[bb][q + e] + kos[e]),
+                                                        __int_as_float((int)v[bb][q + e + 1] + kos[e + 1])),
+                                            make_float2(-kMagic, -kMagic));  // exact f32(s) of both columns
+                const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
+                float2 a2 = make_float2(acc[c], acc[c + 1]);
+                if (FMT != 1)
+                  a2 = __ffma2_rn(__fmul2_rn(f, dw2), dx2, a2);  // f32(s) * dw * dx
+                else
+                  a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);  // dx * dw * f32(s)
+                acc[c] = a2.x;
+                acc[c + 1] = a2.y;
+              }
+            }
+          }
+        }
+      }
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_addr(&bar_acce[a % RTG]));
+        if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_empty[GB % P]));  // this warp is done with the stage's (dx, koff)
+      }
+      ep_b += AG;
+      if (ep_b == nblk) {  // the tile's last block: store its rows of Y
+        const int tile = (int)blockIdx.x + ep_k * (int)gridDim.x;
+        const int rt = tile / p.nct, ct = tile - rt * p.nct;
+        const int64_t row = (int64_t)rt * 128 + t;
+        const int col0 = ct * NT, ncols = min(NT, p.M - col0);
+        if (row < p.N) {
+#pragma unroll
+          for (int c = 0; c < NT; ++c)
+            if (c < ncols) p.y[(int64_t)(col0 + c) * p.ldy + p.row0 + row] = acc[c];
+        }
+#pragma unroll
+        for (int c = 0; c < NT; ++c) acc[c] = 0.f;
+        ep_b = 0;
+        ++ep_k;
+      }
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+    cp_async_wait<0>();
+  }
+
+  // ---------------- teardown: nothing in flight when the CTA leaves ----------------
+  if (warp == 8 && lane == 0)
+    for (int G = max(0, issued - P); G < issued; ++G)
+      mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1), kWaitLimit);
+  if (warp == 9 && lane == 0 && g_issued > 0)
+    mbar_wait(smem_addr(&bar_aempty[(g_issued - 1) % RAG]), (uint32_t)(((g_issued - 1) / RAG) & 1), kWaitLimit);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (t == 0 && *abort_flag) atomicCAS(&g_device_error, 0, kErrTimeout);
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(C::TCOLS));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Prep: f32 activations -> MMA activation tiles + (dx, koff), quantized with the standalone quantizers' device math
+// (identical bytes and scales); optionally also the standard XQ / XD planes (xq_out, xd_out). Columns M .. nct*NT-1
+// are padding: zero tiles, dx = 0, koff = 0x4B400000 (their accumulators are never stored).
+// ---------------------------------------------------------------------------------------------------------------
+
+// q8_0 (Q4_0 and Q8_0 weights): 8 lanes per 32-value block, as b2q_quant_q8_0; a unit is one block.
+template <int FMT, int NT>
+__global__ void __launch_bounds__(256) tc_prep_q8_0_kernel(const float* __restrict__ x, int64_t ldx, int M, int64_t K,
+                                                           int nct, int8_t* __restrict__ xt, int32_t* __restrict__ dk,
+                                                           int8_t* __restrict__ xq_out, float* __restrict__ xd_out) {
+  pdl_wait_then_trigger();
+  const int64_t nblk = K / 32;
+  const int64_t total = (int64_t)nct * NT * nblk;
+  const int sub = threadIdx.x & 7;
+  const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int64_t nwarp = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t base = gwarp * 4; base < total; base += nwarp * 4) {  // warp-uniform bound (shuffles)
+    const int64_t g = base + ((threadIdx.x & 31) >> 3);
+    const bool ok = g < total;
+    const int64_t c = ok ? g / nblk : 0, b = ok ? g % nblk : 0;
+    const bool valid = ok && c < M;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) v = *reinterpret_cast<const float4*>(x + c * ldx + b * 32 + sub * 4);
+    float d;
+    const uint32_t q = q8_0_quant4(v, &d);
+    int sum = bytesum(q);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (ok) {
+      const int ct = (int)(c / NT), cl = (int)(c % NT);
+      *reinterpret_cast<uint32_t*>(xt + ((int64_t)ct * nblk + b) * (NT * 32) + tc::core_off(cl, sub * 4)) = q;
+      const float dx = valid ? q8_0_stored_scale(d) : 0.f;
+      if (sub == 0) {
+        int32_t* d2 = dk + ((int64_t)ct * nblk + b) * 2 * NT;
+        d2[cl] = __float_as_int(dx);
+        d2[NT + cl] = 0x4B400000 - Fmt<FMT>::kOffset * sum;
+      }
+      if (valid && xq_out) {
+        *reinterpret_cast<uint32_t*>(xq_out + c * K + b * 32 + sub * 4) = q;
+        if (sub == 0) xd_out[c * nblk + b] = dx;
+      }
+    }
+  }
+}
+
+// q8_K (TQ2_0 weights): one warp per 256-value block, as b2q_quant_q8_K; the block is 8 units.
+template <int NT>
+__global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restrict__ x, int64_t ldx, int M, int64_t K,
+                                                           int nct, int8_t* __restrict__ xt, int32_t* __restrict__ dk,
+                                                           int8_t* __restrict__ xq_out, float* __restrict__ xd_out) {
+  pdl_wait_then_trigger();
+  const int64_t nblk = K / 256, nunits = K / 32;
+  const int64_t total = (int64_t)nct * NT * nblk;
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t g = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); g < total; g += stride) {
+    const int64_t c = g / nblk, b = g % nblk;
+    const bool valid = c < M;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+      const float* src = x + c * ldx + b * 256 + lane * 8;
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 e = *reinterpret_cast<const float4*>(src + 4);
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = e.x, v[5] = e.y, v[6] = e.z, v[7] = e.w;
+    }
+    uint32_t qlo, qhi;
+    const float d = q8_K_quant8(v, lane, &qlo, &qhi);
+    int sum = bytesum(qlo) + bytesum(qhi);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int ct = (int)(c / NT), cl = (int)(c % NT);
+    const int64_t unit = b * 8 + (lane >> 2);
+    *reinterpret_cast<uint2*>(xt + ((int64_t)ct * nunits + unit) * (NT * 32) + tc::core_off(cl, (lane & 3) * 8)) =
+        make_uint2(qlo, qhi);
+    if (lane == 0) {
+      int32_t* d2 = dk + ((int64_t)ct * nblk + b) * 2 * NT;
+      d2[cl] = __float_as_int(valid ? d : 0.f);
+      d2[NT + cl] = 0x4B400000 - sum;
+    }
+    if (valid && xq_out) {
+      *reinterpret_cast<uint2*>(xq_out + c * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
+      if (lane == 0) xd_out[c * nblk + b] = d;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------------------------
+
+static int ws_nt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+static int ws_stage_values(int fmt) { return fmt == 0 ? 256 : fmt == 1 ? 512 : 128; }
+
+// Workspace bytes of the warp-specialized path (activation tiles, then the (dx, koff) pairs), or 0 if the shape does
+// not fit its stages (K a whole number of stages: Q4_0 256, TQ2_0 512, Q8_0 128 values).
+size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M) {
+  if (K <= 0 || M <= 0 || K % ws_stage_values(fmt)) return 0;
+  const int NT = ws_nt(M);
+  const int64_t cols = (M + NT - 1) / NT * NT;
+  const int64_t nblk = K / (fmt == 1 ? 256 : 32);
+  return ((size_t)cols * (size_t)K + 15) / 16 * 16 + (size_t)cols * (size_t)nblk * 8;
+}
+
+template <int FMT, int NT>
+static int launch_ws(const WsParams& wp, const float* x, int64_t ldx, int8_t* xq_out, float* xd_out,
+                     cudaStream_t stream, bool pdl) {
+  using C = WsCfg<FMT, NT>;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  // prep
+  {
+    const int64_t nblk = wp.K / Fmt<FMT>::kBlock;
+    const int64_t items = (int64_t)wp.nct * NT * nblk;
+    const int64_t per_cta = FMT == 1 ? 8 : 32;  // 256-thread CTAs: 8 warps x (1 q8_K block | 4 q8_0 blocks)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((items + per_cta - 1) / per_cta,
+                                                                        (int64_t)di.sms * 8)));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    int8_t* xt = const_cast<int8_t*>(wp.xt);
+    int32_t* dk = const_cast<int32_t*>(wp.dk);
+    if constexpr (FMT == 1)
+      e = cudaLaunchKernelEx(&cfg, tc_prep_q8_K_kernel<NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk, xq_out, xd_out);
+    else
+      e = cudaLaunchKernelEx(&cfg, tc_prep_q8_0_kernel<FMT, NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk, xq_out, xd_out);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(B2Q_ECUDA, "gemm_tc_ws: prep launch failed: %s", cudaGetErrorString(e));
+    }
+    rc = after_launch("tc_prep");
+    if (rc) return rc;
+  }
+  // GEMM
+  auto fn = gemm_tc_ws_kernel<FMT, NT>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemm_tc_ws: %s", cudaGetErrorString(e));
+  // all of the unified L1 / shared storage as shared memory: otherwise the driver may pick a split that holds one CTA
+  // per SM where the occupancy query (and the persistent grid sized from it) counts two
+  e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemm_tc_ws: %s", cudaGetErrorString(e));
+  // CTAs per SM, computed here: the runtime's occupancy query answers 1 for every kernel that allocates tensor memory
+  // (it cannot know how many columns), which would halve this persistent grid. Limits: shared memory (dynamic +
+  // static + the per-CTA reservation), registers per SM sub-partition (16K each; a CTA's 10 warps take at most 3 on
+  // one), threads, and tensor-memory columns. Too high a count would only queue CTAs, not deadlock them: they do not
+  // wait on one another, and an allocation that finds no free columns waits for a finishing CTA.
+  int occ = 0;
+  {
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, (const void*)fn);
+    if (e != cudaSuccess) return fail(B2Q_ECUDA, "gemm_tc_ws: %s", cudaGetErrorString(e));
+    int dev = 0, smem_sm = 0, resv = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    const int by_smem = smem_sm / (int)(C::SMEM + fa.sharedSizeBytes + (size_t)resv);
+    const int warp_regs = (fa.numRegs + 7) / 8 * 8 * 32;
+    const int by_regs = 16384 / (3 * warp_regs);
+    occ = std::min(std::min(by_smem, by_regs), std::min(2048 / 320, 512 / C::TCOLS));
+  }
+  if (occ < 1) return fail(B2Q_ECUDA, "gemm_tc_ws: the kernel does not fit an SM");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min<int64_t>(wp.ntiles, (int64_t)di.sms * occ));
+  cfg.blockDim = dim3(320);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, fn, wp);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(B2Q_ECUDA, "gemm_tc_ws: launch failed: %s", cudaGetErrorString(e));
+  }
+  return after_launch(FMT == 0 ? "gemm_tc_ws_q4_0" : FMT == 1 ? "gemm_tc_ws_tq2_0" : "gemm_tc_ws_q8_0");
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver library)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static int encode_weight_map(CUtensorMap* map, const uint8_t* wq, int64_t row_bytes, int64_t N, int64_t ldwq) {
+  static std::once_flag once;
+  static EncodeTiledFn encode = nullptr;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<EncodeTiledFn>(fn);
+    else
+      cudaGetLastError();
+  });
+  if (!encode) return fail(B2Q_ECUDA, "gemm_tc_ws: cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)N};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldwq};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(wq), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B2Q_ECUDA, "gemm_tc_ws: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B2Q_OK;
+}
+
+// Fused quantize + tensor-core GEMM, warp-specialized (two launches). The caller checked gemm_tc_ws_bytes(...) > 0
+// and workspace_bytes >= it, a 16-byte aligned workspace, weights and x; ws rows contiguous (ldws = K / block).
+int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                      int8_t* xq_out, float* xd_out, float* y, int64_t ldy, int64_t row0, int64_t N, int64_t K,
+                      int64_t M, void* workspace, cudaStream_t stream, bool pdl) {
+  const int NT = ws_nt(M);
+  WsParams wp{};
+  const int64_t row_bytes = K / (fmt == 1 ? 256 : 32) * (fmt == 0 ? 16 : fmt == 1 ? 64 : 32);
+  const int rc = encode_weight_map(&wp.wmap, wq, row_bytes, N, ldwq);
+  if (rc) return rc;
+  wp.wq = wq;
+  wp.ldwq = ldwq;
+  wp.ws = ws;
+  wp.ldws = K / (fmt == 1 ? 256 : 32);
+  wp.nct = (int)((M + NT - 1) / NT);
+  wp.xt = reinterpret_cast<const int8_t*>(workspace);
+  wp.dk = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(workspace) +
+                                           ((size_t)wp.nct * NT * (size_t)K + 15) / 16 * 16);
+  wp.y = y;
+  wp.ldy = ldy;
+  wp.row0 = row0;
+  wp.N = N;
+  wp.K = K;
+  wp.M = (int)M;
+  wp.ntiles = (int)((N + 127) / 128) * wp.nct;
+#define B2Q_WS_CASE(F, T) \
+  if (fmt == F && NT == T) return launch_ws<F, T>(wp, x, ldx, xq_out, xd_out, stream, pdl);
+  B2Q_WS_CASE(0, 16) B2Q_WS_CASE(0, 32) B2Q_WS_CASE(0, 64) B2Q_WS_CASE(0, 128)
+  B2Q_WS_CASE(1, 16) B2Q_WS_CASE(1, 32) B2Q_WS_CASE(1, 64) B2Q_WS_CASE(1, 128)
+  B2Q_WS_CASE(2, 16) B2Q_WS_CASE(2, 32) B2Q_WS_CASE(2, 64) B2Q_WS_CASE(2, 128)
+#undef B2Q_WS_CASE
+  return fail(B2Q_EINVAL, "gemm_tc_ws: no kernel for fmt %d", fmt);
+}
+
+}  // namespace b2q

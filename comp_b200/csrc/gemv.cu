@@ -375,14 +375,25 @@ struct LaunchArgs {
 // Tensor-core GEMM for many columns (gemm_tc.cu): pre-quantized activations, M >= the threshold below.
 int launch_gemm_tc(const GemvParams& base, int fmt, cudaStream_t stream, bool pdl);
 
+// Warp-specialized persistent tensor-core GEMM with its quantizing prep kernel (gemm_tc_ws.cu): the fused path's
+// schedule when the workspace holds its activation tiles (gemm_tc_ws_bytes > 0: K a whole number of stages).
+size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M);
+int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
+                      int8_t* xq_out, float* xd_out, float* y, int64_t ldy, int64_t row0, int64_t N, int64_t K,
+                      int64_t M, void* workspace, cudaStream_t stream, bool pdl);
+
 // Columns from which a layer runs on the tensor-core GEMM (0 = never). Below it the GEMV kernels, which re-read the
 // weights per group of 4 columns, are the better fit.
 static int g_tc_min_m = 8;
+// Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
+static int g_tc_schedule = 0;
 
-// Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD.
+// Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD (per-block
+// schedule), or the warp-specialized schedule's activation tiles -- whichever is larger.
 static size_t tc_act_bytes(int fmt, int64_t K, int64_t M) {
   const int64_t nblk = K / fmt_block(fmt);
-  return ((size_t)M * (size_t)K + 15) / 16 * 16 + (size_t)M * (size_t)nblk * sizeof(float);
+  const size_t v1 = ((size_t)M * (size_t)K + 15) / 16 * 16 + (size_t)M * (size_t)nblk * sizeof(float);
+  return std::max(v1, gemm_tc_ws_bytes(fmt, K, M));
 }
 
 static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
@@ -407,6 +418,13 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       a.ldwq % 16 == 0) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
+    if (a.x_f32 && !a.s && g_tc_schedule == 0 && a.workspace && aligned(a.workspace, 16) && aligned(a.ws, 16) &&
+        aligned(a.x_f32, 16) && a.ldx % 4 == 0) {
+      const size_t wsb = gemm_tc_ws_bytes(a.fmt, a.K, a.M);
+      if (wsb && a.workspace_bytes >= wsb)
+        return launch_gemm_tc_ws(a.fmt, a.wq, a.ldwq, a.ws, a.x_f32, a.ldx, a.xq_out, a.xd_out, a.y, a.ldy, a.row0,
+                                 a.N, a.K, a.M, a.workspace, stream, g_pdl != 0);
+    }
     if (a.x_f32) {
       int8_t* qo = a.xq_out;
       float* dq = a.xd_out;
@@ -717,6 +735,13 @@ int b2q_set_splitk(int mode) {
 int b2q_set_gemm_min_columns(int m) {
   if (m < 0) return fail(B2Q_EINVAL, "b2q_set_gemm_min_columns: m must be >= 0 (0 = never)");
   g_tc_min_m = m;
+  return B2Q_OK;
+}
+
+int b2q_set_gemm_schedule(int schedule) {
+  if (schedule != 0 && schedule != 1)
+    return fail(B2Q_EINVAL, "b2q_set_gemm_schedule: 0 (warp-specialized where it applies) or 1 (per-block)");
+  g_tc_schedule = schedule;
   return B2Q_OK;
 }
 

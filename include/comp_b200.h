@@ -212,6 +212,12 @@ int b2q_set_warps(int warps);
  * from the GEMV path only by the f32 summation order. */
 int b2q_set_gemm_min_columns(int m);
 
+/* Tuning hook (process-wide): the fused tensor-core schedule. 0 (default) = warp-specialized where it applies (a
+ * workspace of b2q_workspace_size bytes, K a whole number of 128-byte weight stages): a quantizing prep kernel writes
+ * the activations in the MMA tile layout, then a persistent GEMM with producer, MMA and unpack/epilogue warps; 1 = the
+ * per-block schedule. Identical results (same int32 dots, same f32 order). */
+int b2q_set_gemm_schedule(int schedule);
+
 /* Benchmark/tuning hook (process-wide): ring path with one column -- the CTAs of a thread-block cluster of this size
  * (2, 4 or 8) split the activation prologue, each quantizing its share once and storing it into every member's shared
  * memory; 1 = off, 0 = planner's choice. Results do not change (identical bytes, identical summation order). */

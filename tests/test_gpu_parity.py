@@ -508,6 +508,16 @@ def _tensor_core_checks(cuda, fmt, n, k, m):
     assert _lib.launch_count() - before == 2
     assert _same_f32(yf.cpu().numpy(), y)
     assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, split=False).cpu().numpy(), y)
+    # the quantized activations the fused call returns are the standalone quantizer's bytes
+    ya, fq, fd = host.quant_gemv(fmt, twq, tws, tx, n, k, return_act=True)
+    assert np.array_equal(fq.cpu().numpy(), oq) and _same_f32(fd.cpu().numpy(), od)
+    assert _same_f32(ya.cpu().numpy(), y)
+    # both fused schedules (warp-specialized where the shape allows it, per-block) give the same Y
+    _lib.call("b2q_set_gemm_schedule", 1)
+    try:
+        assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy(), y)
+    finally:
+        _lib.call("b2q_set_gemm_schedule", 0)
 
 
 @pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 300, 4096, 1), ("tq2_0", 130, 8192, 3), ("q4_0", 64, 4096, 5),
@@ -523,3 +533,37 @@ def test_tensor_core_gemm_forced_on_few_columns(cuda, fmt, n, k, m):
         _lib.call("b2q_set_gemm_min_columns", 8)
     assert np.array_equal(s.cpu().numpy(), os_)
     assert ref.relerr(y.cpu().numpy(), r) <= TOL
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 40000, 4096, 16), ("tq2_0", 40000, 4096, 12), ("q8_0", 40000, 2048, 16),
+                                       ("q4_0", 20000, 2048, 40), ("tq2_0", 9000, 8192, 130),
+                                       ("q8_0", 12000, 4096, 100)])
+def test_tensor_core_persistent_tiles(cuda, fmt, n, k, m):
+    """More (row tile, column tile) pairs than resident CTAs, so each persistent CTA of the warp-specialized GEMM walks
+    several tiles with its stage ring running on across them: sampled rows against the C oracle, and every row
+    bit-identical to the per-block schedule; the bounded waits never fire."""
+    import ctypes
+
+    rng = np.random.default_rng(91)
+    wq, ws = ref.random_split(fmt, rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    twq, tws, tx = _t(wq, cuda), _t(ws, cuda), _t(x, cuda)
+    _lib.call("b2q_set_gemm_min_columns", 1)  # also where the planner would keep a narrow layer on the GEMV path
+    try:
+        before = _lib.launch_count()
+        y = host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy()
+        assert _lib.launch_count() - before == 2  # prep (quantizer) + GEMM
+        _lib.call("b2q_set_gemm_schedule", 1)
+        y1 = host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy()
+    finally:
+        _lib.call("b2q_set_gemm_schedule", 0)
+        _lib.call("b2q_set_gemm_min_columns", 8)
+    assert _same_f32(y, y1)
+    rows = np.unique(np.concatenate([rng.choice(n, 256, replace=False), [0, 127, 128, n - 1]]))
+    oq, od = ref.quantize(fmt, x)
+    r, _ = native.gemv(fmt, wq[rows], ws[rows], oq, od, k)
+    assert ref.relerr(y[:, rows], r) <= TOL
+    code = ctypes.c_int(-1)
+    _lib.call("b2q_device_error", ctypes.byref(code), 1)
+    assert code.value == 0
+
