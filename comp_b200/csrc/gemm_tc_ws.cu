@@ -6,19 +6,20 @@
 // in ascending order -- so Y is bit-identical to the other schedules. What changes is who does what:
 //   * a prep kernel quantizes the f32 activations with the math of b2q_quant_q8_0 / b2q_quant_q8_K straight into the
 //     MMA operand layout (per column tile of NT columns and 32-value unit: one NT x 32-byte K-major tile of 8 x 16-byte
-//     core matrices), and writes per column and weight block the scale dx and koff = 0x4B400000 - offset * sum(x)
-//     (the weights' offset and the exact int-to-float conversion of gemm_tc.cu folded into one integer add);
+//     core matrices), and writes per column and weight block the scale dx;
 //   * warp 8 (producer) streams per stage -- 128 packed weight bytes of each of the tile's 128 rows -- the rows'
 //     weights (one 2-D TMA tensor copy of a 128-row x 128-byte box, 128-byte swizzled so that the unpacking reads are
-//     free of bank conflicts; rows past N read as zeros), the stage's activation tiles and its (dx, koff) pairs (one
+//     free of bank conflicts; rows past N read as zeros), the stage's activation tiles and its column scales (one
 //     bulk copy each) into a ring of P stages;
 //   * warps 4-7 (thread r = tile row r) unpack each 32-value unit of their row into the MMA's A tile (a ring of RA
-//     tiles);
+//     tiles) as the signed weight values (Q4_0 nibble - 8, TQ2_0 crumb - 1), so the tensor cores' int32 dots are the
+//     exact block dots with no offset term;
 //   * one thread of warp 9 issues each unit's MMA (M = 128, N = NT, K = 32) into its block's accumulator (a ring of
 //     RT accumulators in tensor memory) and commits completions to the mbarriers the other roles wait on;
 //   * warps 0-3 (thread t = tile row t = tensor-memory lane t) run each weight block's epilogue: its NT exact int32
-//     dots from tensor memory, scaled and summed into NT f32 registers in block order; each row's block scales come
-//     through a per-thread cp.async ring.
+//     dots from tensor memory, converted exactly (2^23 + 2^22 + s as f32 bits by one integer add, valid for
+//     |s| < 2^22), scaled and summed into NT f32 registers in block order; each row's block scales come through a
+//     per-thread cp.async ring.
 // Unpacking and epilogue run in separate warps so that their latency chains overlap (measured: with one set of warps
 // doing both, each 32-value unit cost the sum of both chains and the MMA warp sat idle most of the time).
 // The CTAs are persistent: CTA i takes the (row tile, column tile) pairs i, i + gridDim.x, ...; the stage ring and
@@ -40,7 +41,7 @@ struct WsParams {
   const int16_t* ws;
   int64_t ldws;
   const int8_t* xt;   // activation tiles [nct][K/32][NT*32]
-  const int32_t* dk;  // [nct][nblk][2][NT]: dx (f32 bits), koff
+  const float* dk;    // [nct][nblk][NT]: the column scales dx
   float* y;
   int64_t ldy;
   int64_t row0;
@@ -65,7 +66,7 @@ struct WsCfg {
   static constexpr int RAW = 128 * RB;                            // the weight box (128B-swizzled rows)
   static constexpr int BT = NT * 32;                              // one unit's activation tile
   static constexpr int BST = SU * BT;
-  static constexpr int DKB = 2 * NT * 4;                          // (dx, koff) of one block
+  static constexpr int DKB = NT * 4;                              // column scales of one block
   static constexpr int DKS = SB * DKB;
   static constexpr int STAGE = (RAW + BST + DKS + 1023) / 1024 * 1024;  // swizzled boxes start on 1024 bytes
   static constexpr int P = FMT == 0 ? (NT == 16 ? 3 : NT == 32 ? 2 : NT == 64 ? 4 : 3)
@@ -75,10 +76,10 @@ struct WsCfg {
   static constexpr int RA = RAG * GU;                             // A tiles
   static constexpr int ATILE = 128 * 32;
   static constexpr int AG = UPB == 1 ? GU : 1;                    // blocks per accumulator group
-  static constexpr int RTG = 2;                                   // accumulator groups in flight
+  static constexpr int RTG = NT == 16 && UPB == 1 ? 4 : 2;          // accumulator groups in flight
   static constexpr int RT = RTG * AG;                             // accumulators (blocks) in tensor memory
   static constexpr int BB = NT == 16 && AG % 2 == 0 ? 2 : 1;      // blocks per tensor-memory round trip
-  static constexpr int CW = NT <= 32 ? NT : 32;                   // columns per round trip
+  static constexpr int CW = NT == 64 ? 32 : 16;                   // columns per round trip (register budget)
   static constexpr int SBB = SB * 2;                              // scale bytes per row and stage (16, 4 or 8)
   static constexpr int PS = 3, LA = 2;                            // scale ring depth, prefetch distance (stages)
   static constexpr int TCOLS = RT * NT <= 32 ? 32 : RT * NT <= 64 ? 64 : RT * NT <= 128 ? 128 : RT * NT <= 256 ? 256
@@ -120,25 +121,25 @@ __device__ __forceinline__ void bulk_g2s_plain(uint32_t dst, const void* src, ui
                : "memory");
 }
 
-// One 32-value unit of row r -> its row of an A tile, as unsigned (Q4_0, TQ2_0) or signed (Q8_0) bytes in value order.
+// One 32-value unit of row r -> its row of an A tile: the signed weight values (int8) in value order. Per byte,
+// (f + 0x78) ^ 0x80 = f - 8 for a nibble f and (f + 0x7F) ^ 0x80 = f - 1 for a crumb f (no carry leaves a byte).
 // raw: the row's 128 bytes of the stage, whose 16-byte chunk c sits at chunk c ^ (r % 8) (TMA 128B swizzle).
 template <int FMT>
 __device__ __forceinline__ void unpack_unit(uint32_t raw, int sw, int u, uint8_t* at, int r, const uint4 (&tq)[2]) {
   uint4 lo, hi;
   if (FMT == 0) {
     const uint4 w = lds_v4(raw + (uint32_t)((u ^ sw) << 4));
-    lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-    hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                    (w.w >> 4) & 0x0F0F0F0Fu);
+    auto nib = [](uint32_t x) { return ((x & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u; };
+    lo = make_uint4(nib(w.x), nib(w.y), nib(w.z), nib(w.w));
+    hi = make_uint4(nib(w.x >> 4), nib(w.y >> 4), nib(w.z >> 4), nib(w.w >> 4));
   } else if (FMT == 2) {
     lo = lds_v4(raw + (uint32_t)(((2 * u) ^ sw) << 4));
     hi = lds_v4(raw + (uint32_t)(((2 * u + 1) ^ sw) << 4));
   } else {  // TQ2_0 k-step s = u % 8 of a block: values 32s..32s+31 = field s % 4 of the (preloaded) 32 bytes tq
     const int sh = 2 * (u & 3);
-    lo = make_uint4((tq[0].x >> sh) & 0x03030303u, (tq[0].y >> sh) & 0x03030303u, (tq[0].z >> sh) & 0x03030303u,
-                    (tq[0].w >> sh) & 0x03030303u);
-    hi = make_uint4((tq[1].x >> sh) & 0x03030303u, (tq[1].y >> sh) & 0x03030303u, (tq[1].z >> sh) & 0x03030303u,
-                    (tq[1].w >> sh) & 0x03030303u);
+    auto crumb = [sh](uint32_t x) { return (((x >> sh) & 0x03030303u) + 0x7F7F7F7Fu) ^ 0x80808080u; };
+    lo = make_uint4(crumb(tq[0].x), crumb(tq[0].y), crumb(tq[0].z), crumb(tq[0].w));
+    hi = make_uint4(crumb(tq[1].x), crumb(tq[1].y), crumb(tq[1].z), crumb(tq[1].w));
   }
   *reinterpret_cast<uint4*>(at + tc::core_off(r, 0)) = lo;
   *reinterpret_cast<uint4*>(at + tc::core_off(r, 16)) = hi;
@@ -255,7 +256,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = tc::instr_desc(NT, FMT == 2);  // Q8_0 weights are signed
+      const uint32_t idesc = tc::instr_desc(NT, true);  // signed weight values (unpacked with their offset applied)
       const int total_groups = total_stages * (SU / GU);
       bool ok = true;
       for (int g = 0; g < total_groups && ok && !*abort_flag; ++g) {
@@ -263,6 +264,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         if (u0 == 0) ok = mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1), kWaitLimit);
         if (ok) ok = mbar_wait(smem_addr(&bar_afull[g % RAG]), (uint32_t)((g / RAG) & 1), kWaitLimit);
         if (!ok) break;
+        tc::fence_after();
         const uint32_t bst = sbase + (uint32_t)((G % P) * C::STAGE + C::RAW);
         const uint32_t at = a_base + (uint32_t)((g % RAG) * GU * C::ATILE);
 #pragma unroll
@@ -272,8 +274,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
             const int a = B / AG;
             ok = mbar_wait(smem_addr(&bar_acce[a % RTG]), (uint32_t)(((a / RTG) & 1) ^ 1), kWaitLimit);
             if (!ok) break;
+            tc::fence_after();
           }
-          tc::fence_after();
           tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)),
                      tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT)), idesc, ub > 0 ? 1u : 0u);
           if (ub == UPB - 1 && B % AG == AG - 1) tc::mma_commit(smem_addr(&bar_accf[(B / AG) % RTG]));
@@ -351,7 +353,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     bool ok = true;
     for (int a = 0; a < total_agroups; ++a) {
       const int B0 = a * AG, GB = B0 / SB, j0 = B0 - GB * SB;
-      if (j0 == 0) {  // a new stage: scales LA stages ahead; this stage's (dx, koff) have landed
+      if (j0 == 0) {  // a new stage: row scales LA stages ahead; this stage's column scales have landed
         prefetch_scales(GB + LA);
         cp_async_wait<LA>();
         const bool got = __all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_full[GB % P]), (uint32_t)((GB / P) & 1),
@@ -364,8 +366,10 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         break;
       }
       tc::fence_after();
-      const uint32_t dk0 = sbase + (uint32_t)((GB % P) * C::STAGE + C::RAW + C::BST);
-      const uint32_t sc0 = sc_base + (uint32_t)(((GB % PS) * 128 + t) * C::SBB);
+      // column and row scales by plain loads: the compiler may issue them ahead of the tensor-memory wait
+      const uint8_t* dk0 = ws_smem + (sbase - smem_addr(ws_smem)) + (GB % P) * C::STAGE + C::RAW + C::BST;
+      const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(ws_smem + (sc_base - smem_addr(ws_smem)) +
+                                                              ((GB % PS) * 128 + t) * C::SBB);
 #pragma unroll
       for (int jb = 0; jb < AG; jb += BB) {
 #pragma unroll
@@ -381,21 +385,18 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
 #pragma unroll
           for (int bb = 0; bb < BB; ++bb) {  // blocks in ascending order: the sum order of the reference
             const int j = j0 + jb + bb;
-            const uint32_t dkp = dk0 + (uint32_t)(j * C::DKB);
-            const float dw = f16_bits_to_f32(lds_u16(sc0 + (uint32_t)(j * 2)));
+            const float4* dxp = reinterpret_cast<const float4*>(dk0 + j * C::DKB);
+            const float dw = f16_bits_to_f32(sc0[j]);
             const float2 dw2 = make_float2(dw, dw);
 #pragma unroll
             for (int q = 0; q < CW; q += 4) {
-              const uint4 dx4 = lds_v4(dkp + (uint32_t)((c0 + q) * 4));
-              const uint4 ko4 = lds_v4(dkp + (uint32_t)((NT + c0 + q) * 4));
-              const float dxs[4] = {__uint_as_float(dx4.x), __uint_as_float(dx4.y), __uint_as_float(dx4.z),
-                                    __uint_as_float(dx4.w)};
-              const int kos[4] = {(int)ko4.x, (int)ko4.y, (int)ko4.z, (int)ko4.w};
+              const float4 dx4 = dxp[(c0 + q) / 4];
+              const float dxs[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
 #pragma unroll
               for (int e = 0; e < 4; e += 2) {
                 const int c = c0 + q + e;
-                const float2 f = __fadd2_rn(make_float2(__int_as_float((int)v[bb][q + e] + kos[e]),
-                                                        __int_as_float((int)v[bb][q + e + 1] + kos[e + 1])),
+                const float2 f = __fadd2_rn(make_float2(__int_as_float((int)v[bb][q + e] + 0x4B400000),
+                                                        __int_as_float((int)v[bb][q + e + 1] + 0x4B400000)),
                                             make_float2(-kMagic, -kMagic));  // exact f32(s) of both columns
                 const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
                 float2 a2 = make_float2(acc[c], acc[c + 1]);
@@ -414,7 +415,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(smem_addr(&bar_acce[a % RTG]));
-        if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_empty[GB % P]));  // this warp is done with the stage's (dx, koff)
+        if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_empty[GB % P]));  // this warp is done with the stage's scales
       }
       ep_b += AG;
       if (ep_b == nblk) {  // the tile's last block: store its rows of Y
@@ -451,15 +452,15 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Prep: f32 activations -> MMA activation tiles + (dx, koff), quantized with the standalone quantizers' device math
-// (identical bytes and scales); optionally also the standard XQ / XD planes (xq_out, xd_out). Columns M .. nct*NT-1
-// are padding: zero tiles, dx = 0, koff = 0x4B400000 (their accumulators are never stored).
+// Prep: f32 activations -> MMA activation tiles + column scales dx, quantized with the standalone quantizers' device
+// math (identical bytes and scales); optionally also the standard XQ / XD planes (xq_out, xd_out). Columns M ..
+// nct*NT-1 are padding: zero tiles, dx = 0 (their accumulators are never stored).
 // ---------------------------------------------------------------------------------------------------------------
 
 // q8_0 (Q4_0 and Q8_0 weights): 8 lanes per 32-value block, as b2q_quant_q8_0; a unit is one block.
 template <int FMT, int NT>
 __global__ void __launch_bounds__(256) tc_prep_q8_0_kernel(const float* __restrict__ x, int64_t ldx, int M, int64_t K,
-                                                           int nct, int8_t* __restrict__ xt, int32_t* __restrict__ dk,
+                                                           int nct, int8_t* __restrict__ xt, float* __restrict__ dk,
                                                            int8_t* __restrict__ xq_out, float* __restrict__ xd_out) {
   pdl_wait_then_trigger();
   const int64_t nblk = K / 32;
@@ -476,19 +477,11 @@ __global__ void __launch_bounds__(256) tc_prep_q8_0_kernel(const float* __restri
     if (valid) v = *reinterpret_cast<const float4*>(x + c * ldx + b * 32 + sub * 4);
     float d;
     const uint32_t q = q8_0_quant4(v, &d);
-    int sum = bytesum(q);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
     if (ok) {
       const int ct = (int)(c / NT), cl = (int)(c % NT);
       *reinterpret_cast<uint32_t*>(xt + ((int64_t)ct * nblk + b) * (NT * 32) + tc::core_off(cl, sub * 4)) = q;
       const float dx = valid ? q8_0_stored_scale(d) : 0.f;
-      if (sub == 0) {
-        int32_t* d2 = dk + ((int64_t)ct * nblk + b) * 2 * NT;
-        d2[cl] = __float_as_int(dx);
-        d2[NT + cl] = 0x4B400000 - Fmt<FMT>::kOffset * sum;
-      }
+      if (sub == 0) dk[((int64_t)ct * nblk + b) * NT + cl] = dx;
       if (valid && xq_out) {
         *reinterpret_cast<uint32_t*>(xq_out + c * K + b * 32 + sub * 4) = q;
         if (sub == 0) xd_out[c * nblk + b] = dx;
@@ -500,7 +493,7 @@ __global__ void __launch_bounds__(256) tc_prep_q8_0_kernel(const float* __restri
 // q8_K (TQ2_0 weights): one warp per 256-value block, as b2q_quant_q8_K; the block is 8 units.
 template <int NT>
 __global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restrict__ x, int64_t ldx, int M, int64_t K,
-                                                           int nct, int8_t* __restrict__ xt, int32_t* __restrict__ dk,
+                                                           int nct, int8_t* __restrict__ xt, float* __restrict__ dk,
                                                            int8_t* __restrict__ xq_out, float* __restrict__ xd_out) {
   pdl_wait_then_trigger();
   const int64_t nblk = K / 256, nunits = K / 32;
@@ -519,18 +512,11 @@ __global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restri
     }
     uint32_t qlo, qhi;
     const float d = q8_K_quant8(v, lane, &qlo, &qhi);
-    int sum = bytesum(qlo) + bytesum(qhi);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const int ct = (int)(c / NT), cl = (int)(c % NT);
     const int64_t unit = b * 8 + (lane >> 2);
     *reinterpret_cast<uint2*>(xt + ((int64_t)ct * nunits + unit) * (NT * 32) + tc::core_off(cl, (lane & 3) * 8)) =
         make_uint2(qlo, qhi);
-    if (lane == 0) {
-      int32_t* d2 = dk + ((int64_t)ct * nblk + b) * 2 * NT;
-      d2[cl] = __float_as_int(valid ? d : 0.f);
-      d2[NT + cl] = 0x4B400000 - sum;
-    }
+    if (lane == 0) dk[((int64_t)ct * nblk + b) * NT + cl] = valid ? d : 0.f;
     if (valid && xq_out) {
       *reinterpret_cast<uint2*>(xq_out + c * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
       if (lane == 0) xd_out[c * nblk + b] = d;
@@ -546,14 +532,14 @@ static int ws_nt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 
 
 static int ws_stage_values(int fmt) { return fmt == 0 ? 256 : fmt == 1 ? 512 : 128; }
 
-// Workspace bytes of the warp-specialized path (activation tiles, then the (dx, koff) pairs), or 0 if the shape does
+// Workspace bytes of the warp-specialized path (activation tiles, then the column scales), or 0 if the shape does
 // not fit its stages (K a whole number of stages: Q4_0 256, TQ2_0 512, Q8_0 128 values).
 size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M) {
   if (K <= 0 || M <= 0 || K % ws_stage_values(fmt)) return 0;
   const int NT = ws_nt(M);
   const int64_t cols = (M + NT - 1) / NT * NT;
   const int64_t nblk = K / (fmt == 1 ? 256 : 32);
-  return ((size_t)cols * (size_t)K + 15) / 16 * 16 + (size_t)cols * (size_t)nblk * 8;
+  return ((size_t)cols * (size_t)K + 15) / 16 * 16 + (size_t)cols * (size_t)nblk * 4;
 }
 
 template <int FMT, int NT>
@@ -580,7 +566,7 @@ static int launch_ws(const WsParams& wp, const float* x, int64_t ldx, int8_t* xq
     cfg.numAttrs = 1;
     cudaError_t e;
     int8_t* xt = const_cast<int8_t*>(wp.xt);
-    int32_t* dk = const_cast<int32_t*>(wp.dk);
+    float* dk = const_cast<float*>(wp.dk);
     if constexpr (FMT == 1)
       e = cudaLaunchKernelEx(&cfg, tc_prep_q8_K_kernel<NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk, xq_out, xd_out);
     else
@@ -680,7 +666,7 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
   wp.ldws = K / (fmt == 1 ? 256 : 32);
   wp.nct = (int)((M + NT - 1) / NT);
   wp.xt = reinterpret_cast<const int8_t*>(workspace);
-  wp.dk = reinterpret_cast<const int32_t*>(reinterpret_cast<const uint8_t*>(workspace) +
+  wp.dk = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(workspace) +
                                            ((size_t)wp.nct * NT * (size_t)K + 15) / 16 * 16);
   wp.y = y;
   wp.ldy = ldy;
