@@ -280,6 +280,9 @@ def main():
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
     ap.add_argument("--pdl", default="on", choices=["on", "off"], help="programmatic dependent launch of the GEMVs")
+    ap.add_argument("--e2e-api", default="pinned", choices=["pinned", "device"],
+                    help="N = 1 end-to-end leg: b2q_quant_gemv_pinned (pinned host x in, Y stored into pinned host "
+                         "memory by the kernel) or host.quant_gemv on device buffers with torch memcpys around it")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -460,8 +463,26 @@ def main():
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
 
     y_dev = [torch.empty((m, L.n), dtype=torch.float32, device=dev) for L in layers] if world == 1 else None
+    pinned = world == 1 and args.e2e_api == "pinned"
+    if pinned:
+        pin_ws = [torch.empty(max(256, host.pinned_workspace_size(L.fmt, L.n, L.k, m)), dtype=torch.uint8,
+                              device=dev) for L in layers]
+
+    def e2e_step_pinned():
+        # every step, one C-ABI call per layer with host buffers: a copy kernel pulls the layer's x from pinned host
+        # memory, the fused GEMV stores Y into pinned host memory; the host then waits and reads the results
+        for i, L in enumerate(layers):
+            wq, ws = L.w[0]
+            rc = lib.b2q_quant_gemv_pinned(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x_host.data_ptr(),
+                                           L.x_host.stride(0), y_host[i].data_ptr(), L.n, L.k, m,
+                                           pin_ws[i].data_ptr(), pin_ws[i].numel(), sptr)
+            if rc != 0:
+                raise RuntimeError(_lib.last_error())
+        stream.synchronize()  # the step's results are read on the host
 
     def e2e_step():
+        if pinned:
+            return e2e_step_pinned()
         # every step: the layers' inputs from pinned host memory, the GEMVs back to back through the public API (so
         # each one's weight stream can start while the previous one finishes), every layer's output back to pinned
         # host memory, then the host waits for all of it
@@ -543,8 +564,11 @@ def main():
                          "us_per_launch": round(dom_ms * 1e3, 3), "algorithmic_bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "api": "comp_b200.host.quant_gemv (fused quantize + GEMV per layer)" if world == 1 else
-                    f"comp_b200.dist.RowShardedGemv ({exchange_name})"},
+                    "steps": e2e_steps,
+                    "api": ("C-ABI b2q_quant_gemv_pinned per layer (pinned host x in, the kernels copy x in and store "
+                            "Y into pinned host memory; host sync every step)" if pinned else
+                            "comp_b200.host.quant_gemv (fused quantize + GEMV per layer; torch memcpy of x in, Y out)")
+                    if world == 1 else f"comp_b200.dist.RowShardedGemv ({exchange_name})"},
             "gpu_launches": launches,
             "clocks": cs,
         }

@@ -45,6 +45,11 @@ cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// The argument checks of the fused quantize + GEMV entry points (f32 activations x [M][K], row stride K), without a
+// launch (gemv.cu).
+int check_quant_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x,
+                          const float* y, int64_t N, int64_t K, int64_t M);
+
 // Fused quantize + split-K GEMV with exactly `splits` K splits, partial sums in `workspace` (gemv.cu).
 int quant_gemv_forced_split(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                             float* y, int64_t N, int64_t K, int64_t M, int splits, float* workspace,

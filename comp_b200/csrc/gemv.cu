@@ -343,6 +343,12 @@ static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t 
   return B2Q_OK;
 }
 
+int check_quant_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x,
+                          const float* y, int64_t N, int64_t K, int64_t M) {
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", who, fmt);
+  return check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
+}
+
 struct LaunchArgs {
   int fmt;
   bool bytes;

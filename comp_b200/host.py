@@ -289,3 +289,39 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
                   y.data_ptr(), n, k, m, workspace.data_ptr() if wsb else None,
                   workspace.numel() * workspace.element_size() if wsb else 0, _stream(dev))
     return (y, xq, xd) if return_act else y
+
+
+def pinned_workspace_size(fmt, n, k, m):
+    """Bytes of device workspace quant_gemv_pinned needs for this shape (staged activations + GEMV workspace)."""
+    return int(_lib.load().b2q_pinned_workspace_size(FMT_ID[fmt], n, k, m))
+
+
+def quant_gemv_pinned(fmt, wq, ws, x, n, k, out, workspace=None):
+    """quant_gemv with the activations and the output in page-locked host memory.
+
+    x: f32 [M][K] CPU tensor in pinned memory (x.pin_memory()); out: contiguous f32 [M][N] pinned CPU tensor that
+    receives Y. The copy of x to the GPU and the store of Y to `out` are made by the kernels through the buffers'
+    device mappings (no memcpy), on the current stream of the weights' device, asynchronously: synchronize that
+    stream before reading `out`. Y equals quant_gemv(fmt, wq, ws, x.cuda(), n, k) bit for bit. workspace: optional CUDA
+    byte tensor of at least pinned_workspace_size(fmt, n, k, M) bytes, 256-byte aligned (allocated here when None).
+    Returns `out`."""
+    _fmt(fmt)
+    dev = _need_cuda("quant_gemv_pinned", wq, ws)
+    _check_weights(fmt, wq, ws, n, k)
+    for t, name in ((x, "x"), (out, "out")):
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu" or not t.is_pinned():
+            raise ValueError(f"quant_gemv_pinned: {name} must be a pinned CPU tensor (tensor.pin_memory())")
+    if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != k or x.stride(1) != 1:
+        raise ValueError(f"quant_gemv_pinned: x must be float32 [M][{k}] with unit column stride, got {x.dtype} "
+                         f"{tuple(x.shape)}")
+    m = x.shape[0]
+    if out.dtype != torch.float32 or tuple(out.shape) != (m, n) or not out.is_contiguous():
+        raise ValueError(f"quant_gemv_pinned: out must be a contiguous float32 [{m}][{n}] pinned CPU tensor")
+    need = pinned_workspace_size(fmt, n, k, m)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    with _on(dev):
+        _lib.call("b2q_quant_gemv_pinned", FMT_ID[fmt], wq.data_ptr(), wq.stride(0), ws.data_ptr(), x.data_ptr(),
+                  x.stride(0), out.data_ptr(), n, k, m, workspace.data_ptr(),
+                  workspace.numel() * workspace.element_size(), _stream(dev))
+    return out

@@ -143,6 +143,25 @@ int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
                       int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, void* workspace,
                       size_t workspace_bytes, b2q_stream_t stream);
 
+/* Device workspace bytes b2q_quant_gemv_pinned needs for this layer: the staged activations (M * K f32, rounded up
+ * to 256 bytes) followed by b2q_workspace_size(fmt, N, K, M). 0 for an empty layer. */
+size_t b2q_pinned_workspace_size(int fmt, int64_t N, int64_t K, int64_t M);
+
+/*
+ * b2q_quant_gemv_ws with the activations and the output in page-locked host memory: x_host [M][ldx] f32 (16-byte
+ * aligned, ldx % 4 == 0) and y_host [M][N] f32, both mapped for the current device (cudaHostAlloc, cudaHostRegister
+ * with cudaHostRegisterMapped, torch pin_memory); anything else is refused with B2Q_EINVAL before any launch.
+ * workspace: device memory, 256-byte aligned, >= b2q_pinned_workspace_size bytes. A copy kernel reads x through its
+ * device mapping into the workspace, then the fused GEMV (exactly b2q_quant_gemv_ws: same schedule, bit-identical Y)
+ * stores Y straight into y_host -- no memcpy, so consecutive calls keep the programmatic overlap of their kernels.
+ * Asynchronous on `stream`: read y_host after synchronizing the stream. Two launches (three when the layer takes a
+ * two-kernel schedule). Host-buffer form of host.quantize + host.gemv (src/komp/host.py:63-85), whose callers pass
+ * torch tensors that may live on the host; no single-call counterpart in the reference.
+ */
+int b2q_quant_gemv_pinned(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x_host,
+                          int64_t ldx, float* y_host, int64_t N, int64_t K, int64_t M, void* workspace,
+                          size_t workspace_bytes, b2q_stream_t stream);
+
 /*
  * ggml blocks -> split planes on the device (model load path). blocks: n rows of k values as ggml Q4_0 (fmt 0,
  * 18-byte blocks: f16 d, 16 quant bytes), TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d) or Q8_0 (fmt 2,
