@@ -169,8 +169,56 @@ static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
   return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
 }
 
+// Plans depend only on the device, the layer shape and the tuning hooks, so each is computed once: the occupancy
+// queries behind a plan cost host time that a decode loop, which waits for every step's result, would otherwise pay
+// before every first launch of a step.
+struct PlanKey {
+  int dev, fmt, M, splits;
+  bool bytes, ring_ok;
+  int64_t N, K;
+  int tune[6];
+  bool operator==(const PlanKey& o) const {
+    return dev == o.dev && fmt == o.fmt && M == o.M && splits == o.splits && bytes == o.bytes &&
+           ring_ok == o.ring_ok && N == o.N && K == o.K && std::equal(tune, tune + 6, o.tune);
+  }
+};
+struct PlanHash {
+  size_t operator()(const PlanKey& k) const {
+    size_t h = std::hash<int64_t>()(k.N) * 1000003u ^ std::hash<int64_t>()(k.K);
+    h = h * 31u + (size_t)(k.dev * 7 + k.fmt) * 131u + (size_t)k.M * 17u + (size_t)k.splits;
+    h = h * 31u + (k.bytes ? 1u : 0u) + (k.ring_ok ? 2u : 0u);
+    for (int t : k.tune) h = h * 31u + (size_t)t;
+    return h;
+  }
+};
+static std::mutex g_plan_mu;
+static std::unordered_map<PlanKey, Plan, PlanHash> g_plans;
+
+static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out, int splits);
+
 // K is the per-split K; `splits` CTAs rows share the SMs (the grid is splits x grid_x).
 static int make_plan(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out, int splits = 1) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(B2Q_ECUDA, "gemv: cudaGetDevice failed");
+  const PlanKey key{dev, fmt, M, splits, bytes, ring_ok, N, K,
+                    {g_tune_rows, g_tune_cpt, g_tune_grid, g_tune_stages, g_tune_path, g_tune_cluster}};
+  {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) {
+      *out = it->second;
+      return B2Q_OK;
+    }
+  }
+  const int rc = make_plan_uncached(fmt, bytes, ring_ok, N, K, M, out, splits);
+  if (rc == B2Q_OK) {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    g_plans[key] = *out;
+  }
+  return rc;
+}
+
+static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int64_t K, int M, Plan* out, int splits) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
