@@ -54,7 +54,8 @@ __device__ __forceinline__ float f16_bits_to_f32(uint16_t bits) { return __half2
 
 // ---------------------------------------------------------------------------------------------------------------
 // Activation quantizers. Only correctly rounded float operations: IEEE division, single multiplies (never fused),
-// roundf (half away from zero) / rintf (half to even), f16 conversion with round-to-nearest-even.
+// roundf (half away from zero), round half to even (rintf, or an exact add of 1.5 * 2^23: q8_K_bits), f16
+// conversion with round-to-nearest-even.
 // ---------------------------------------------------------------------------------------------------------------
 
 // q8_0 for one 32-value block held by 8 consecutive lanes (4 values each, lanes aligned to a multiple of 8).
@@ -78,6 +79,19 @@ __device__ __forceinline__ uint32_t q8_0_quant4(float4 v, float* d_out) {
 
 // f32(f16_rne(d)): the scale stored for a q8_0 block (the f16 ggml keeps, widened back to f32).
 __device__ __forceinline__ float q8_0_stored_scale(float d) { return __half2float(__float2half_rn(d)); }
+
+// q = min(127, rint(p)) of a q8_K product p = fl(iscale * x), |p| <= 127 + ulp, without the conversion unit:
+// fl(min(p, 127) + 1.5 * 2^23) is exactly 1.5 * 2^23 + rint(min(p, 127)) (round to nearest even at unit spacing),
+// whose bits are 0x4B400000 + q, so their low byte is q's byte. min before rounding equals min after it because 127
+// is an integer; a NaN product gives 127 either way (fminf).
+__device__ __forceinline__ uint32_t q8_K_bits(float p) {
+  return __float_as_uint(__fadd_rn(fminf(p, 127.0f), 12582912.0f));
+}
+
+// The low bytes of four words, packed little-endian (a -> byte 0).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
 
 // q8_K for one 256-value block held by a full warp (8 consecutive values per lane: lane l holds values 8l..8l+7).
 // Writes the 8 quants packed into q_lo/q_hi (little-endian) and returns d (0 for an all-zero block).
@@ -108,15 +122,11 @@ __device__ __forceinline__ float q8_K_quant8(const float (&v)[8], int lane, uint
   const float mx = __shfl_sync(0xffffffffu, mine, first >> 3);
   const bool nz = amax != 0.0f;
   const float iscale = __fdiv_rn(-127.0f, nz ? mx : 1.0f);
-  uint32_t w[2] = {0u, 0u};
+  uint32_t b8[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    int q = (int)fminf(rintf(__fmul_rn(iscale, v[i])), 127.0f);
-    q = nz ? q : 0;
-    w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
-  }
-  *q_lo = w[0];
-  *q_hi = w[1];
+  for (int i = 0; i < 8; ++i) b8[i] = q8_K_bits(__fmul_rn(iscale, v[i]));
+  *q_lo = nz ? pack_low_bytes(b8[0], b8[1], b8[2], b8[3]) : 0u;
+  *q_hi = nz ? pack_low_bytes(b8[4], b8[5], b8[6], b8[7]) : 0u;
   return nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
 }
 

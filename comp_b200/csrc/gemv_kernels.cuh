@@ -730,20 +730,32 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
 #pragma unroll
       for (int t = 0; t < 16; ++t) v[j][t] = 0.f;
   }
-  // local largest magnitude, its lowest value index, and its signed value (values visited in increasing index)
-  float amax = 0.f, cand = 0.f;
-  int first = 256;
+  // Local largest magnitude (0 when there is none: NaN never wins), by a balanced tree rather than a 64-step chain.
+  float mx16[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int t = 0; t < 16; ++t)
+    mx16[t] = fmaxf(fmaxf(fabsf(v[0][t]), fabsf(v[1][t])), fmaxf(fabsf(v[2][t]), fabsf(v[3][t])));
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const float a = fabsf(v[j][t]);
-      if (a > amax) {
-        amax = a;
-        first = vbase + j * 32 + t;
-        cand = v[j][t];
-      }
-    }
+  for (int n = 8; n >= 1; n >>= 1)
+#pragma unroll
+    for (int t = 0; t < n; ++t) mx16[t] = fmaxf(mx16[t], mx16[t + n]);
+  float amax = fmaxf(mx16[0], 0.0f);
+  // The lowest value index whose magnitude is amax, with that value's sign bit: key = index * 2 + sign, minimum over
+  // the values (a tree again); no match leaves 0x7fffffff (an all-NaN chunk, where amax is 0).
+  int key16[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    key16[t] = 0x7fffffff;
+#pragma unroll
+    for (int j = 3; j >= 0; --j)  // lower field = lower index: it overrides
+      if (fabsf(v[j][t]) == amax) key16[t] = ((vbase + j * 32 + t) << 1) | (int)(__float_as_uint(v[j][t]) >> 31);
+  }
+#pragma unroll
+  for (int n = 8; n >= 1; n >>= 1)
+#pragma unroll
+    for (int t = 0; t < n; ++t) key16[t] = min(key16[t], key16[t + n]);
+  int first = key16[0] == 0x7fffffff ? 256 : key16[0] >> 1;
+  float cand = (key16[0] & 1) ? -amax : amax;  // the signed value at `first`: its magnitude is amax
   // combine over the 4 threads of the block: larger magnitude wins, equal magnitudes keep the lower index
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
@@ -758,21 +770,18 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   }
   const bool nz = amax != 0.0f;
   const float iscale = __fdiv_rn(-127.0f, nz ? cand : 1.0f);
+  // q = min(127, rint(iscale * x)) through q8_K_bits (no conversion unit), bytes packed with prmt, summed with dp4a
   int sum = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      uint32_t word = 0;
+      uint32_t b4[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int q = (int)fminf(rintf(__fmul_rn(iscale, v[j][k * 4 + e])), 127.0f);
-        q = nz ? q : 0;
-        sum += q;
-        word |= (uint32_t)(q & 0xff) << (8 * e);
-      }
-      w[k] = word;
+      for (int e = 0; e < 4; ++e) b4[e] = q8_K_bits(__fmul_rn(iscale, v[j][k * 4 + e]));
+      w[k] = nz ? pack_low_bytes(b4[0], b4[1], b4[2], b4[3]) : 0u;
+      sum = __dp4a((int)w[k], 0x01010101, sum);
     }
     o.x[j] = make_uint4(w[0], w[1], w[2], w[3]);
   }
