@@ -280,9 +280,10 @@ def main():
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
     ap.add_argument("--pdl", default="on", choices=["on", "off"], help="programmatic dependent launch of the GEMVs")
-    ap.add_argument("--e2e-api", default="pinned", choices=["pinned", "device"],
-                    help="N = 1 end-to-end leg: b2q_quant_gemv_pinned (pinned host x in, Y stored into pinned host "
-                         "memory by the kernel) or host.quant_gemv on device buffers with torch memcpys around it")
+    ap.add_argument("--e2e-api", default="auto", choices=["auto", "pinned", "device"],
+                    help="end-to-end leg: pinned host x in and Y stored into pinned host memory by the kernels "
+                         "(N = 1: b2q_quant_gemv_pinned, N > 1: RowShardedGemv(x_host, out=y_host)), or device "
+                         "buffers with torch memcpys around each call; auto = pinned at N = 1, device at N > 1")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -463,15 +464,19 @@ def main():
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
 
     y_dev = [torch.empty((m, L.n), dtype=torch.float32, device=dev) for L in layers] if world == 1 else None
-    pinned = world == 1 and args.e2e_api == "pinned"
-    if pinned:
+    pinned = args.e2e_api == "pinned" or (args.e2e_api == "auto" and world == 1)
+    if pinned and world == 1:
         pin_ws = [torch.empty(max(256, host.pinned_workspace_size(L.fmt, L.n, L.k, m)), dtype=torch.uint8,
                               device=dev) for L in layers]
 
     def e2e_step_pinned():
-        # every step, one C-ABI call per layer with host buffers: a copy kernel pulls the layer's x from pinned host
-        # memory, the fused GEMV stores Y into pinned host memory; the host then waits and reads the results
+        # every step, one call per layer with host buffers: a copy kernel pulls the layer's x from pinned host memory,
+        # the fused GEMV (N > 1: with the all-gather) stores Y into pinned host memory; the host then waits and reads
+        # the results
         for i, L in enumerate(layers):
+            if world > 1:
+                L.objs[0](L.x_host, out=y_host[i])
+                continue
             wq, ws = L.w[0]
             rc = lib.b2q_quant_gemv_pinned(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x_host.data_ptr(),
                                            L.x_host.stride(0), y_host[i].data_ptr(), L.n, L.k, m,
@@ -568,7 +573,9 @@ def main():
                     "api": ("C-ABI b2q_quant_gemv_pinned per layer (pinned host x in, the kernels copy x in and store "
                             "Y into pinned host memory; host sync every step)" if pinned else
                             "comp_b200.host.quant_gemv (fused quantize + GEMV per layer; torch memcpy of x in, Y out)")
-                    if world == 1 else f"comp_b200.dist.RowShardedGemv ({exchange_name})"},
+                    if world == 1 else f"comp_b200.dist.RowShardedGemv ({exchange_name}" +
+                    ("; pinned host x in, Y stored into pinned host memory)" if pinned else
+                     "; torch memcpy of x in, Y out)")},
             "gpu_launches": launches,
             "clocks": cs,
         }

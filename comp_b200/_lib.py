@@ -31,6 +31,8 @@ SIGNATURES = {
     "b2q_workspace_size": (ctypes.c_size_t, [INT, I64, I64, I64]),
     "b2q_pinned_workspace_size": (ctypes.c_size_t, [INT, I64, I64, I64]),
     "b2q_quant_gemv_pinned": (INT, [INT, P, I64, P, P, I64, P, I64, I64, I64, P, ctypes.c_size_t, P]),
+    "b2q_host_device_pointer": (INT, [P, ctypes.POINTER(ctypes.c_void_p)]),
+    "b2q_stage_pinned": (INT, [P, I64, P, I64, I64, P]),
     "b2q_split_blocks": (INT, [INT, P, I64, I64, P, I64, P, P]),
     "b2q_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "b2q_quant_gemv_splitk_noalloc": (INT, [INT, P, I64, P, P, I64, P, I64, I64, I64, INT, P]),

@@ -143,3 +143,43 @@ extern "C" int b2q_quant_gemv_pinned(int fmt, const uint8_t* wq, int64_t ldwq, c
   return b2q_quant_gemv_ws(fmt, wq, ldwq, ws, stage, K, nullptr, nullptr, reinterpret_cast<float*>(y_dev), N, K, M,
                            gws, gemv_ws, stream);
 }
+
+extern "C" int b2q_host_device_pointer(const void* host, void** dev) {
+  using namespace b2q;
+  if (!dev) return fail(B2Q_EINVAL, "b2q_host_device_pointer: null output");
+  *dev = nullptr;
+  return mapped("b2q_host_device_pointer", "the buffer", host, dev);
+}
+
+extern "C" int b2q_stage_pinned(const float* x_host, int64_t ldx, float* stage, int64_t M, int64_t K,
+                                b2q_stream_t stream) {
+  using namespace b2q;
+  static const char* who = "b2q_stage_pinned";
+  if (M < 0 || K < 0) return fail(B2Q_EINVAL, "%s: negative size", who);
+  if (M == 0 || K == 0) return B2Q_OK;
+  void* x_dev = nullptr;
+  int rc = mapped(who, "x", x_host, &x_dev);
+  if (rc) return rc;
+  if (K % 4 || ldx < K || (ldx % 4) || !aligned(x_dev, 16))
+    return fail(B2Q_EALIGN, "%s: x must be 16-byte aligned, K and ldx multiples of 4, ldx >= K", who);
+  if (!stage || !aligned(stage, 16)) return fail(B2Q_EALIGN, "%s: stage must be 16-byte aligned device memory", who);
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, stage) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(B2Q_EINVAL, "%s: stage must be device memory", who);
+  }
+  DeviceInfo di;
+  rc = device_info(&di);
+  if (rc) return rc;
+  const int64_t K4 = K / 4, total4 = M * K4;
+  const int64_t want = (total4 + (int64_t)kCopyThreads * kCopyVec - 1) / ((int64_t)kCopyThreads * kCopyVec);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)di.sms * 8));
+  cudaError_t le = launch_maybe_pdl(pinned_x_copy_kernel, dim3(grid), dim3(kCopyThreads), 0, (cudaStream_t)stream,
+                                    reinterpret_cast<const float4*>(x_dev), ldx / 4, reinterpret_cast<float4*>(stage),
+                                    K4, total4);
+  if (le != cudaSuccess) {
+    cudaGetLastError();
+    return fail(B2Q_ECUDA, "%s: launch failed: %s", who, cudaGetErrorString(le));
+  }
+  return after_launch(who);
+}

@@ -12,7 +12,9 @@ Exchange paths:
           (value, flag) store into its receive buffer (CUDA IPC mappings over NVLink), and each CTA collects its
           slice of the peers' rows with bounded polls -- no fences, no grid-wide barrier. One launch per layer,
           graph-capturable. The returned Y is this layer's output buffer: call t's result stays valid until the
-          layer's next call.
+          layer's next call. Given a pinned host `out`, the kernel stores Y there instead (b2q_host_device_pointer).
+Host buffers: x may be a pinned CPU tensor (copied to the GPU by a kernel, b2q_stage_pinned) and `out` a pinned CPU
+tensor, so a decode loop that keeps its activations on the host needs no memcpy around the layer.
   "nccl"  host.quant_gemv, then torch.distributed.all_gather_into_tensor of equal-size padded slices.
 """
 
@@ -126,18 +128,37 @@ class RowShardedGemv:
             self._rxpeers = torch.tensor(self._rxmap.ptrs, dtype=torch.int64, device=dev)
         dist.barrier(group=self.group)
 
-    def _p2p(self, x):
+    def _p2p(self, x, out=None):
         m = x.shape[0]
         if m > self.max_m:
             raise ValueError(f"p2p exchange: M={m} > max_m={self.max_m}")
         self._calls += 1
         with host._on(self.dev):
+            if out is None:
+                yp = self.y.data_ptr()
+            else:  # the kernel stores the whole Y (its rows and the peers') straight into the pinned buffer
+                dp = ctypes.c_void_p()
+                _lib.call("b2q_host_device_pointer", out.data_ptr(), ctypes.byref(dp))
+                yp = dp.value
             _lib.call("b2q_gemv_allgather", host.FMT_ID[self.fmt], self.wq.data_ptr(), self.wq.stride(0),
-                      self.ws.data_ptr(), x.data_ptr(), x.stride(0), self.y.data_ptr(), self.rx.data_ptr(),
+                      self.ws.data_ptr(), x.data_ptr(), x.stride(0), yp, self.rx.data_ptr(),
                       self._rxpeers.data_ptr(), self.rx_stride, self.done.data_ptr(), self.status.data_ptr(),
                       self.row0, self.rows, self.n, self.k, m, self.rank, self.world, SPIN_LIMIT,
                       torch.cuda.current_stream(self.dev).cuda_stream)
-        return self.y[:m]
+        return self.y[:m] if out is None else out
+
+    def _stage(self, x):
+        """Pinned host x [M][K] -> this layer's device staging buffer, copied by a kernel through x's device mapping
+        (b2q_stage_pinned: the following GEMV starts its weight stream while x arrives)."""
+        if not x.is_pinned() or x.stride(1) != 1:
+            raise ValueError("x on the host must be a pinned CPU tensor (tensor.pin_memory()) with unit column stride")
+        m = x.shape[0]
+        if getattr(self, "_xs", None) is None or self._xs.shape[0] < m:
+            self._xs = torch.empty((max(m, self.max_m), self.k), dtype=torch.float32, device=self.dev)
+        with host._on(self.dev):
+            _lib.call("b2q_stage_pinned", x.data_ptr(), x.stride(0), self._xs.data_ptr(), m, self.k,
+                      torch.cuda.current_stream(self.dev).cuda_stream)
+        return self._xs[:m]
 
     def status_code(self):
         """0, or 1 if a receive poll timed out (synchronizes)."""
@@ -157,11 +178,24 @@ class RowShardedGemv:
         dist.all_gather_into_tensor(gathered, part, group=self.group)
         return assemble(gathered, self.world, m, self.per, self.n)
 
-    def __call__(self, x):
+    def __call__(self, x, out=None):
+        """Y [M][N] on every rank. x: f32 [M][K] on this rank's GPU, or a pinned CPU tensor (then a kernel copies it to
+        the GPU). out: optional pinned CPU f32 [M][N] that receives Y (the fused exchange stores into it directly; the
+        NCCL exchange copies into it); it is complete once the current stream is synchronized. Returns out if given."""
         if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.k:
             raise ValueError(f"x must be float32 [M][{self.k}], got {x.dtype} {tuple(x.shape)}")
-        x = host._rows_aligned(x)
-        return self._p2p(x) if self.exchange == "p2p" else self._nccl(x)
+        m = x.shape[0]
+        if out is not None and (out.device.type != "cpu" or not out.is_pinned() or out.dtype != torch.float32 or
+                                tuple(out.shape) != (m, self.n) or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous pinned CPU float32 [{m}][{self.n}] tensor")
+        x = self._stage(x) if x.device.type == "cpu" else host._rows_aligned(x)
+        if self.exchange == "p2p":
+            return self._p2p(x, out)
+        y = self._nccl(x)
+        if out is None:
+            return y
+        out.copy_(y, non_blocking=True)
+        return out
 
     def close(self):
         """Unmaps the peers' buffers (collective: every rank calls it, after its last use of the layer)."""

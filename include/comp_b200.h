@@ -163,6 +163,23 @@ int b2q_quant_gemv_pinned(int fmt, const uint8_t* wq, int64_t ldwq, const int16_
                           size_t workspace_bytes, b2q_stream_t stream);
 
 /*
+ * The device address of page-locked host memory mapped for the current device (cudaHostAlloc, cudaHostRegister with
+ * cudaHostRegisterMapped, torch pin_memory), so that a kernel of this library may store its Y there (e.g. the output
+ * of b2q_gemv_allgather, which only ever writes Y). Anything else (pageable or device memory) gives B2Q_EINVAL and
+ * *dev = NULL. Helper of the host-buffer paths; no reference counterpart.
+ */
+int b2q_host_device_pointer(const void* host, void** dev);
+
+/*
+ * Copies activations x_host [M][ldx] f32 (page-locked, mapped; 16-byte aligned, K and ldx multiples of 4) into
+ * stage [M][K] (device memory, 16-byte aligned) with a kernel that reads x through its device mapping: it loads
+ * before its programmatic-dependency wait and releases the next kernel at once, so a GEMV launched after it starts
+ * streaming weights while x arrives (and waits for the copy before reading x). Asynchronous on `stream`. The copy
+ * step of b2q_quant_gemv_pinned on its own, for callers that launch the GEMV themselves (row-sharded layers).
+ */
+int b2q_stage_pinned(const float* x_host, int64_t ldx, float* stage, int64_t M, int64_t K, b2q_stream_t stream);
+
+/*
  * ggml blocks -> split planes on the device (model load path). blocks: n rows of k values as ggml Q4_0 (fmt 0,
  * 18-byte blocks: f16 d, 16 quant bytes), TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d) or Q8_0 (fmt 2,
  * 34-byte blocks: f16 d, 32 int8), row-major,

@@ -50,6 +50,16 @@ def main():
                 y = L(x).clone()
                 if not torch.equal(y.view(torch.int32), want.view(torch.int32)):
                     fails.append(f"{fmt} {n}x{k} m={m} {exchange} call {t}: max diff {(y - want).abs().max().item()}")
+            # host buffers: pinned x copied in by a kernel, Y stored into pinned host memory (two calls in a row)
+            xh = x.cpu().pin_memory()
+            outs = [torch.full((m, n), float("nan")).pin_memory() for _ in range(2)]
+            for o in outs:
+                if L(xh, out=o) is not o:
+                    fails.append(f"{fmt} {n}x{k} {exchange} pinned: out not returned")
+            torch.cuda.current_stream(dev).synchronize()
+            for t, o in enumerate(outs):
+                if not torch.equal(o.view(torch.int32), want.cpu().view(torch.int32)):
+                    fails.append(f"{fmt} {n}x{k} m={m} {exchange} pinned call {t}: mismatch")
             if L.exchange == "p2p":
                 # capture two calls (both output buffers) in a graph and replay it
                 s = torch.cuda.Stream(dev)

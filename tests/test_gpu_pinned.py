@@ -130,3 +130,30 @@ def test_pinned_refuses_unreachable_memory(cuda):
     torch.cuda.current_stream().synchronize()
     assert not out.numpy().any()
     assert _no_device_error()
+
+
+def test_stage_pinned_and_host_device_pointer(cuda):
+    """b2q_stage_pinned copies pinned rows (padded row stride) into device memory exactly; b2q_host_device_pointer
+    gives a pinned buffer's device address; both refuse pageable and device memory (and staging into host memory)
+    before any launch."""
+    m, k, ldx = 3, 8192, 8200
+    _, _, x, _, _, xh = _layer("tq2_0", 4, k, m, 11, cuda, ldx)
+    stage = torch.full((m, k), float("nan"), device=cuda)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    before = _lib.launch_count()
+    assert lib.b2q_stage_pinned(xh.data_ptr(), ldx, stage.data_ptr(), m, k, stream) == 0
+    assert _lib.launch_count() - before == 1
+    assert _same_f32(stage.cpu().numpy(), x)
+    pageable = np.ascontiguousarray(x)
+    before = _lib.launch_count()
+    assert lib.b2q_stage_pinned(pageable.ctypes.data, k, stage.data_ptr(), m, k, stream) == -1
+    assert lib.b2q_stage_pinned(stage.data_ptr(), k, stage.data_ptr(), m, k, stream) == -1   # device memory as x
+    assert lib.b2q_stage_pinned(xh.data_ptr(), ldx, xh.data_ptr(), m, k, stream) == -1       # host memory as stage
+    assert lib.b2q_stage_pinned(xh.data_ptr() + 4, ldx, stage.data_ptr(), m, k, stream) == -2
+    assert _lib.launch_count() == before
+    dp = ctypes.c_void_p()
+    assert lib.b2q_host_device_pointer(xh.data_ptr(), ctypes.byref(dp)) == 0 and dp.value
+    assert lib.b2q_host_device_pointer(pageable.ctypes.data, ctypes.byref(dp)) == -1 and not dp.value
+    assert lib.b2q_host_device_pointer(stage.data_ptr(), ctypes.byref(dp)) == -1 and not dp.value
+    assert _no_device_error()
