@@ -472,8 +472,12 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       a.ldwq % 16 == 0) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
-    if (a.x_f32 && !a.s && g_tc_schedule == 0 && a.workspace && aligned(a.workspace, 16) && aligned(a.ws, 16) &&
-        aligned(a.x_f32, 16) && a.ldx % 4 == 0) {
+    // Measured on B200 (same box, lm_head-sized layers, M = 16..128): the warp-specialized schedule is faster everywhere
+    // except 128-column tiles of the 32-value block formats (Q4_0 1683 vs 1493 us, Q8_0 907 vs 772 us at M = 128),
+    // where the per-block kernel stays; TQ2_0 keeps it at every width (198 vs 439 us at M = 128).
+    const bool ws_fits = !(tc_nt == 128 && a.fmt != 1);
+    if (a.x_f32 && !a.s && g_tc_schedule == 0 && ws_fits && a.workspace && aligned(a.workspace, 16) &&
+        aligned(a.ws, 16) && aligned(a.x_f32, 16) && a.ldx % 4 == 0) {
       const size_t wsb = gemm_tc_ws_bytes(a.fmt, a.K, a.M);
       if (wsb && a.workspace_bytes >= wsb)
         return launch_gemm_tc_ws(a.fmt, a.wq, a.ldwq, a.ws, a.x_f32, a.ldx, a.xq_out, a.xd_out, a.y, a.ldy, a.row0,

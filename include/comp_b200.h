@@ -249,7 +249,8 @@ int b2q_set_warps(int warps);
 int b2q_set_gemm_min_columns(int m);
 
 /* Tuning hook (process-wide): the fused tensor-core schedule. 0 (default) = warp-specialized where it applies (a
- * workspace of b2q_workspace_size bytes, K a whole number of 128-byte weight stages): a quantizing prep kernel writes
+ * workspace of b2q_workspace_size bytes, K a whole number of 128-byte weight stages, and not the 128-column tiles
+ * (M > 64) of Q4_0 / Q8_0, where the per-block schedule measured faster): a quantizing prep kernel writes
  * the activations in the MMA tile layout, then a persistent GEMM with producer, MMA and unpack/epilogue warps; 1 = the
  * per-block schedule. Identical results (same int32 dots, same f32 order). */
 int b2q_set_gemm_schedule(int schedule);
