@@ -40,10 +40,13 @@ WORKLOADS = {
     # Q8_0 weights (an extension beyond the reference): the config-3 decoder shapes plus the lm_head, all Q8_0
     "q8_0": [("q8_0", 6144, 4096, "qkv"), ("q8_0", 4096, 4096, "o_proj"), ("q8_0", 28672, 4096, "gate_up"),
              ("q8_0", 4096, 14336, "down"), ("q8_0", 128256, 4096, "lm_head")],
+    # IQ4_NL weights (a second extension): the same shapes, all IQ4_NL
+    "iq4_nl": [("iq4_nl", 6144, 4096, "qkv"), ("iq4_nl", 4096, 4096, "o_proj"), ("iq4_nl", 28672, 4096, "gate_up"),
+               ("iq4_nl", 4096, 14336, "down"), ("iq4_nl", 128256, 4096, "lm_head")],
 }
-BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32}
-BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34}  # ggml block bytes (quant bytes + f16 scale)
-FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2}
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32}
+BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18}  # ggml block bytes (quant bytes + f16 scale)
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}
 METRIC = "weight-stream GB/s and us/GEMV (% of HBM peak) at 1/2/4/8 B200 vs host CPU ref"
 L2_BYTES = 126 * 2**20
 
@@ -161,9 +164,10 @@ def make_layer_gpu(fmt, n, k, seed, dev, rows=None):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     nb = k // BLOCK[fmt]
-    if fmt == "q4_0":
+    if fmt in ("q4_0", "iq4_nl"):
         wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
-        ws = (torch.randn((n, nb), device=dev, generator=g) * 0.02).abs().half().view(torch.int16)
+        sd = 0.02 if fmt == "q4_0" else 0.002
+        ws = (torch.randn((n, nb), device=dev, generator=g) * sd).abs().half().view(torch.int16)
     elif fmt == "q8_0":
         wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g).view(torch.uint8)
         ws = (torch.randn((n, nb), device=dev, generator=g) * 0.002).abs().half().view(torch.int16)

@@ -40,13 +40,17 @@
 
 namespace b2q {
 
-// Weight formats: 0 Q4_0, 1 TQ2_0, 2 Q8_0 (an extension beyond the reference).
-static inline int fmt_block(int fmt) { return fmt == 1 ? 256 : 32; }            // values per block
-static inline int fmt_chunk_values(int fmt) { return fmt == 0 ? 32 : fmt == 1 ? 64 : 16; }  // per 16-byte chunk
-static inline bool fmt_ok(int fmt) { return fmt >= 0 && fmt <= 2; }
-static inline size_t fmt_slot_bytes(int fmt, int C) {
-  return fmt == 0 ? cluster_slot_bytes<0>(C) : fmt == 1 ? cluster_slot_bytes<1>(C) : cluster_slot_bytes<2>(C);
+// Weight formats: 0 Q4_0, 1 TQ2_0, 2 Q8_0, 3 IQ4_NL (2 and 3: extensions beyond the reference).
+static inline int fmt_block(int fmt) { return fmt == 1 ? 256 : 32; }  // values per block
+static inline int fmt_chunk_values(int fmt) {                         // per 16-byte chunk
+  return (fmt == 0 || fmt == 3) ? 32 : fmt == 1 ? 64 : 16;
 }
+static inline bool fmt_ok(int fmt) { return fmt >= 0 && fmt <= 3; }
+static inline size_t fmt_slot_bytes(int fmt, int C) {
+  return fmt == 0 ? cluster_slot_bytes<0>(C) : fmt == 1 ? cluster_slot_bytes<1>(C)
+                  : fmt == 2 ? cluster_slot_bytes<2>(C) : cluster_slot_bytes<3>(C);
+}
+static const char* fmt_list = "Q4_0 (0), TQ2_0 (1), Q8_0 (2) or IQ4_NL (3)";
 
 // ------------------------------------------------------------------------------------------------------------------
 // ------------------------------------------------------------------------------------------------------------------
@@ -380,7 +384,7 @@ static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t 
   if (!aligned(y, 4)) return fail(B2Q_EALIGN, "%s: y must be 4-byte aligned", who);
   if (K == 0) return B2Q_OK;  // empty sums: only Y (= 0) is written
   if (!wq || !ws || !x || (!f32_input && !xd)) return fail(B2Q_EINVAL, "%s: null pointer", who);
-  const int64_t qbytes = fmt == 0 ? K / 2 : fmt == 1 ? K / 4 : K;
+  const int64_t qbytes = (fmt == 0 || fmt == 3) ? K / 2 : fmt == 1 ? K / 4 : K;
   if (ldwq < qbytes) return fail(B2Q_EINVAL, "%s: ldwq=%lld < %lld quant bytes per row", who, (long long)ldwq,
                                  (long long)qbytes);
   if (!aligned(wq, 16) || (ldwq % 16)) return fail(B2Q_EALIGN, "%s: wq must be 16-byte aligned, ldwq %% 16 == 0", who);
@@ -393,7 +397,7 @@ static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t 
 
 int check_quant_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x,
                           const float* y, int64_t N, int64_t K, int64_t M) {
-  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", who, fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not %s", who, fmt, fmt_list);
   return check_gemv_args(who, fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
 }
 
@@ -468,8 +472,9 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   const int tc_nt = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
   const bool tc_wide = device_info(&tc_di) == B2Q_OK &&
                        ((a.N + 127) / 128) * ((a.M + tc_nt - 1) / tc_nt) >= (int64_t)tc_di.sms;
+  // (IQ4_NL has no tensor-core kernel: its many-column layers stay on the GEMV path)
   if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || g_tc_min_m < 8) && !a.rx_peers && aligned(a.wq, 16) &&
-      a.ldwq % 16 == 0) {
+      a.ldwq % 16 == 0 && a.fmt != 3) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
     // Measured on B200 (same box, lm_head-sized layers, M = 16..128): the warp-specialized schedule is faster everywhere
@@ -600,7 +605,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       cudaGetLastError();
       return fail(B2Q_ECUDA, "gemv: launch failed: %s", cudaGetErrorString(le));
     }
-    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : a.fmt == 1 ? "gemv_tq2_0" : "gemv_q8_0");
+    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : a.fmt == 1 ? "gemv_tq2_0" : a.fmt == 2 ? "gemv_q8_0" : "gemv_iq4_nl");
     if (rc) return rc;
     if (splits > 1) {
       DeviceInfo di;
@@ -686,6 +691,20 @@ int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int
   return launch_gemv(a, (cudaStream_t)stream);
 }
 
+int b2q_gemv_iq4_nl(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                    int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
+  int rc = check_gemv_args("b2q_gemv_iq4_nl", 3, wq, ldwq, ws, xq, xd, y, N, K, M, false);
+  if (rc) return rc;
+  if (variant < 0 || variant > 2) return fail(B2Q_EINVAL, "b2q_gemv_iq4_nl: variant %d not in 0..2", variant);
+  if (s && !aligned(s, 4)) return fail(B2Q_EALIGN, "b2q_gemv_iq4_nl: s must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = 3;
+  a.bytes = variant == B2Q_VARIANT_BYTES;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.xq = xq, a.xd = xd, a.y = y, a.ldy = N, a.s = s;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
 int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
                   int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
   int rc = check_gemv_args("b2q_gemv_q8_0", 2, wq, ldwq, ws, xq, xd, y, N, K, M, false);
@@ -702,7 +721,7 @@ int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8
 
 int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream) {
-  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv: fmt %d is not %s", fmt, fmt_list);
   int rc = check_gemv_args("b2q_quant_gemv", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
   if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
@@ -719,7 +738,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
-  if (g_tc_min_m > 0 && M >= g_tc_min_m) return tc_act_bytes(fmt, K, M);  // the GEMV path ignores it
+  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3) return tc_act_bytes(fmt, K, M);  // the GEMV path ignores it
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
 }
@@ -727,7 +746,7 @@ size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
 int b2q_quant_gemv_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                       int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, void* workspace,
                       size_t workspace_bytes, b2q_stream_t stream) {
-  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "b2q_quant_gemv_ws: fmt %d is not %s", fmt, fmt_list);
   int rc = check_gemv_args("b2q_quant_gemv_ws", fmt, wq, ldwq, ws, x, nullptr, y, N, K, M, true);
   if (rc) return rc;
   if (N > 0 && M > 0 && K > 0 && (ldx < K || (ldx % 4)))
@@ -748,7 +767,7 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
                        int32_t* status, int64_t row0, int64_t n_local, int64_t N_total, int64_t K, int64_t M,
                        int rank, int nranks, long long spin_limit, b2q_stream_t stream) {
   const char* who = "b2q_gemv_allgather";
-  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", who, fmt);
+  if (!fmt_ok(fmt)) return fail(B2Q_EINVAL, "%s: fmt %d is not %s", who, fmt, fmt_list);
   if (nranks < 1 || rank < 0 || rank >= nranks) return fail(B2Q_EINVAL, "%s: rank %d of %d", who, rank, nranks);
   if (M < 1 || M > kMaxColumns) return fail(B2Q_ERANGE, "%s: M=%lld, 1..%d supported", who, (long long)M, kMaxColumns);
   if (K < 1 || n_local < 1 || row0 < 0 || row0 + n_local > N_total)

@@ -89,22 +89,40 @@ struct GemvParams {
 template <int FMT>
 struct Fmt;
 // kQBytes: quant bytes per block; kOffset: the weights' stored offset (value = field - kOffset), folded in as
-// -kOffset * sum(x); kActQ80: the activations are q8_0 (32-value blocks, f16-exact scales), else q8_K.
+// -kOffset * sum(x); kActQ80: the activations are q8_0 (32-value blocks, f16-exact scales), else q8_K; kLayout: the
+// format whose quant-plane and activation layout this one shares (IQ4_NL is laid out exactly as Q4_0).
 template <>
 struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibbles)
-  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 8;
+  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 8, kLayout = 0;
   static constexpr bool kActQ80 = true;
 };
 template <>
 struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
-  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4, kQBytes = 64, kOffset = 1;
+  static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4, kQBytes = 64, kOffset = 1, kLayout = 1;
   static constexpr bool kActQ80 = false;
 };
 template <>
 struct Fmt<2> {  // Q8_0 (an extension beyond the reference: ggml block_q8_0): 32 int8 values, 2 chunks per block
-  static constexpr int kBlock = 32, kChunkShift = 1, kFields = 1, kQBytes = 32, kOffset = 0;
+  static constexpr int kBlock = 32, kChunkShift = 1, kFields = 1, kQBytes = 32, kOffset = 0, kLayout = 2;
   static constexpr bool kActQ80 = true;
 };
+template <>
+struct Fmt<3> {  // IQ4_NL (an extension: ggml block_iq4_nl): Q4_0's layout (kLayout 0), nibbles index 16 int8 levels
+  static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 0, kLayout = 0;
+  static constexpr bool kActQ80 = true;
+};
+
+// ggml's IQ4_NL levels (kvalues_iq4nl) as little-endian int8 bytes: levels 0-3, 4-7, 8-11, 12-15.
+constexpr uint32_t kIq4Lv0 = 0xBFAD9881u, kIq4Lv1 = 0xF6EADDCFu, kIq4Lv2 = 0x26190D01u, kIq4Lv3 = 0x71594535u;
+
+// The levels of the four nibbles in bits 0-15 of `nibs`, as four int8 bytes (nibble j -> byte j): two byte-permute
+// lookups, one in each half of the table (index = nibble & 7), and a third that takes each byte from the half its
+// nibble's bit 3 selects.
+__device__ __forceinline__ uint32_t iq4nl_levels4(uint32_t nibs) {
+  const uint32_t lo = __byte_perm(kIq4Lv0, kIq4Lv1, nibs & 0x7777u);
+  const uint32_t hi = __byte_perm(kIq4Lv2, kIq4Lv3, nibs & 0x7777u);
+  return __byte_perm(lo, hi, 0x3210u | ((nibs >> 1) & 0x4444u));
+}
 
 // Base pointers of this CTA's K split (blockIdx.y); with one split every offset is zero.
 template <int FMT>
@@ -133,8 +151,8 @@ struct Split {
 // Position (in 16-byte units, within one activation column) of the q-th 16-byte piece of the natural int8 layout.
 template <int FMT>
 __device__ __forceinline__ int perm_unit(int q, int C) {
-  if (FMT == 0) return (q & 1) * C + (q >> 1);  // block b = q/2, nibble field h = q%2
-  if (FMT == 2) return q;                        // Q8_0: chunk c holds values 16c .. 16c+15
+  if (Fmt<FMT>::kLayout == 0) return (q & 1) * C + (q >> 1);  // block b = q/2, nibble field h = q%2
+  if (FMT == 2) return q;                                       // Q8_0: chunk c holds values 16c .. 16c+15
   const int b = q >> 4, o = q & 15;              // 16 pieces per 256-value block
   const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
   return j * C + 4 * b + c;
@@ -261,7 +279,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
         if (g < total) {
           const int m = g / nblk, b = g - m * nblk;
           // Q4_0: low / high nibble fields of block b at xs[field][b]; Q8_0: natural order
-          const int pos = FMT == 0 ? ((sub >> 2) * C + b) * 16 + (sub & 3) * 4 : b * 32 + sub * 4;
+          const int pos = Fmt<FMT>::kLayout == 0 ? ((sub >> 2) * C + b) * 16 + (sub & 3) * 4 : b * 32 + sub * 4;
           *reinterpret_cast<uint32_t*>(xs + (int64_t)m * K + pos) = q;
           const float ds = q8_0_stored_scale(d);
           if (sub == 0) xscale[m * nblk + b] = ds;
@@ -337,6 +355,18 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
+  if (FMT == 3 && !BYTES) {
+    // IQ4_NL: word k holds the nibbles of values 4k..4k+3 (low) and 16+4k..16+4k+3 (high); the lookups give the levels
+    // in nibble order (value 4k, 16+4k, 4k+1, 16+4k+1 | 4k+2, ...), so the activations are interleaved to match
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t wk = word_of(w, k), xa = word_of(x[0], k), xb = word_of(x[1], k);
+      s = __dp4a((int)iq4nl_levels4(wk), (int)__byte_perm(xa, xb, 0x5140u), s);
+      s = __dp4a((int)iq4nl_levels4(wk >> 16), (int)__byte_perm(xa, xb, 0x7362u), s);
+    }
+    return s;
+  }
   if (FMT == 2 && !BYTES) {  // Q8_0: signed weights, no field extraction and no offset
     int s = 0;
 #pragma unroll
@@ -405,7 +435,8 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
 #pragma unroll
         for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
           const int xb = (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
-          const int val = (FMT == 0)   ? ((wb >> (4 * j)) & 15) - 8
+          const int val = (FMT == 3)   ? (int)(int8_t)(iq4nl_levels4((wb >> (4 * j)) & 15) & 0xffu)
+                          : (FMT == 0) ? ((wb >> (4 * j)) & 15) - 8
                           : (FMT == 1) ? ((wb >> (2 * j)) & 3) - 1
                                        : (int)(int8_t)wb;
           s += val * xb;
@@ -623,7 +654,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   const bool writer = (blockIdx.x < (unsigned)max(1, p.cluster)) && (p.xq_out != nullptr) && valid;
   if (p.x_f32 == nullptr) {
     if (!valid) return;
-    if (FMT == 0) {
+    if (Fmt<FMT>::kLayout == 0) {
       const uint4* src = reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 32);
       o.x[0] = src[0];
       o.x[1] = src[1];
@@ -677,7 +708,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     }
     return;
   }
-  if (FMT == 0) {
+  if (Fmt<FMT>::kLayout == 0) {
     if (!valid) return;
     const float4* src = reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 32);
     float4 v[8];
@@ -701,7 +732,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     }
     o.x[0] = make_uint4(w[0], w[1], w[2], w[3]);  // values 0..15 (low-nibble field)
     o.x[1] = make_uint4(w[4], w[5], w[6], w[7]);  // values 16..31 (high-nibble field)
-    o.sum = 8 * sum;
+    o.sum = Fmt<FMT>::kOffset * sum;
     o.dx = q8_0_stored_scale(d);
     if (writer) {
       uint4* dst = reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 32);

@@ -31,6 +31,10 @@ KernelFn reg_kernel_for(int fmt, bool bytes, int R, int MC, bool xreg) {
     if (bytes) return xreg ? pick<2, true, true>(R, MC) : pick<2, true, false>(R, MC);
     return xreg ? pick<2, false, true>(R, MC) : pick<2, false, false>(R, MC);
   }
+  if (fmt == 3) {
+    if (bytes) return xreg ? pick<3, true, true>(R, MC) : pick<3, true, false>(R, MC);
+    return xreg ? pick<3, false, true>(R, MC) : pick<3, false, false>(R, MC);
+  }
   if (bytes) return xreg ? pick<1, true, true>(R, MC) : pick<1, true, false>(R, MC);
   return xreg ? pick<1, false, true>(R, MC) : pick<1, false, false>(R, MC);
 }

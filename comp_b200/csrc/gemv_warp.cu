@@ -1,4 +1,5 @@
-// Instantiations of the warp-rows GEMV kernel (one activation column): Q4_0, TQ2_0 and Q8_0, R = 1, 2, 4 rows per group.
+// Instantiations of the warp-rows GEMV kernel (one activation column): Q4_0, TQ2_0, Q8_0 and IQ4_NL, R = 1, 2, 4
+// rows per group.
 #include "gemv_kernels.cuh"
 
 namespace b2q {
@@ -15,6 +16,12 @@ KernelFn warp_kernel_for(int fmt, int R) {
       case 1: return gemv_warp_kernel<2, 1>;
       case 2: return gemv_warp_kernel<2, 2>;
       case 4: return gemv_warp_kernel<2, 4>;
+    }
+  } else if (fmt == 3) {
+    switch (R) {
+      case 1: return gemv_warp_kernel<3, 1>;
+      case 2: return gemv_warp_kernel<3, 2>;
+      case 4: return gemv_warp_kernel<3, 4>;
     }
   } else {
     switch (R) {

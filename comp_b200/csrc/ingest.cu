@@ -54,8 +54,9 @@ using namespace b2q;
 extern "C" int b2q_split_blocks(int fmt, const uint8_t* blocks, int64_t n, int64_t k, uint8_t* wq, int64_t ldwq,
                                 int16_t* ws, b2q_stream_t stream) {
   const char* who = "b2q_split_blocks";
-  if (fmt < 0 || fmt > 2) return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1) or Q8_0 (2)", who, fmt);
-  const int blk = fmt == 1 ? 256 : 32, qb = fmt == 0 ? 16 : fmt == 1 ? 64 : 32;
+  if (fmt < 0 || fmt > 3)
+    return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1), Q8_0 (2) or IQ4_NL (3)", who, fmt);
+  const int blk = fmt == 1 ? 256 : 32, qb = (fmt == 0 || fmt == 3) ? 16 : fmt == 1 ? 64 : 32;
   if (n < 0 || k < 0) return fail(B2Q_EINVAL, "%s: negative size", who);
   if (k % blk) return fail(B2Q_EINVAL, "%s: k=%lld is not a multiple of the %d-value block", who, (long long)k, blk);
   const int64_t nb = k / blk, total = n * nb;
@@ -66,7 +67,7 @@ extern "C" int b2q_split_blocks(int fmt, const uint8_t* blocks, int64_t n, int64
   if (!aligned(blocks, 16) || !aligned(wq, 16) || (ldwq % 16) || !aligned(ws, 2))
     return fail(B2Q_EALIGN, "%s: blocks and wq must be 16-byte aligned, ldwq %% 16 == 0, ws 2-byte aligned", who);
   const unsigned grid = (unsigned)((total + 255) / 256);
-  if (fmt == 0)
+  if (fmt == 0 || fmt == 3)  // Q4_0 and IQ4_NL: 18-byte blocks, f16 d then 16 nibble bytes
     split_blocks_kernel<18, 2, 16, 0><<<grid, 256, 0, (cudaStream_t)stream>>>(blocks, total, nb, wq, ldwq, ws);
   else if (fmt == 1)
     split_blocks_kernel<66, 0, 64, 64><<<grid, 256, 0, (cudaStream_t)stream>>>(blocks, total, nb, wq, ldwq, ws);

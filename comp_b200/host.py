@@ -17,17 +17,19 @@ import torch
 from . import _lib
 
 # weights: block values, block bytes, quant offset/bytes in the ggml block, scale offset, activation format
-# (q4_0 and tq2_0: the same table as src/komp/host.py:9-12; q8_0 is an extension beyond the reference, ggml
-# block_q8_0 weights multiplied against q8_0 activations)
+# (q4_0 and tq2_0: the same table as src/komp/host.py:9-12; q8_0 and iq4_nl are extensions beyond the reference,
+# ggml block_q8_0 / block_iq4_nl weights multiplied against q8_0 activations)
 FORMATS = {
     "q4_0": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
     "tq2_0": dict(block=256, nbytes=66, qoff=0, qbytes=64, soff=64, act="q8_K"),
     "q8_0": dict(block=32, nbytes=34, qoff=2, qbytes=32, soff=0, act="q8_0"),
+    "iq4_nl": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
 }
 MODES = {"bytes": 0, "dp4a": 2}  # src/komp/host.py:13
 ACT_BLOCK = {"q8_0": 32, "q8_K": 256}
-FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2}
-GEMV_ENTRY = {"q4_0": "b2q_gemv_q4_0", "tq2_0": "b2q_gemv_tq2_0", "q8_0": "b2q_gemv_q8_0"}
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}
+GEMV_ENTRY = {"q4_0": "b2q_gemv_q4_0", "tq2_0": "b2q_gemv_tq2_0", "q8_0": "b2q_gemv_q8_0",
+              "iq4_nl": "b2q_gemv_iq4_nl"}
 
 
 def _fmt(fmt):

@@ -45,6 +45,7 @@ typedef struct CUstream_st* b2q_stream_t;
 #define B2Q_FMT_Q4_0 0
 #define B2Q_FMT_TQ2_0 1
 #define B2Q_FMT_Q8_0 2 /* extension: ggml block_q8_0 weights (no counterpart in the reference) */
+#define B2Q_FMT_IQ4_NL 3 /* extension: ggml block_iq4_nl weights, GEMV path only (no counterpart in the reference) */
 #define B2Q_VARIANT_BYTES 0
 #define B2Q_VARIANT_DP4A 2
 
@@ -109,6 +110,18 @@ int b2q_gemv_tq2_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int
  */
 int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
                   int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
+
+/*
+ * IQ4_NL x q8_0 decode GEMV: Y[m][n] = sum_b f32(s[m][n][b]) * dw[n][b] * dx[m][b], s = sum_i level[nibble_i] * xq_i
+ * with ggml's 16 int8 levels (kvalues_iq4nl: -127, -104, ..., 89, 113). A second extension beyond the reference: the
+ * weights are ggml block_iq4_nl (f16 d, 16 bytes of nibbles laid out exactly as Q4_0's), so the planes are Q4_0's:
+ *   wq: u8 [N][ldwq] (16 bytes per 32-value block), ws: int16 [N][K/32] (f16 bits), xq: int8 [M][K], xd: f32
+ *   [M][K/32], y: f32 [M][N], s: int32 [M][N][K/32] or NULL.
+ * Every fused, split-K, pinned, no-alloc and multi-GPU entry takes fmt B2Q_FMT_IQ4_NL too; layers of 8+ columns stay
+ * on the GEMV path (there is no IQ4_NL tensor-core kernel).
+ */
+int b2q_gemv_iq4_nl(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                    int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
 
 /*
  * Fused quantizer prologue + GEMV (one launch): every CTA quantizes f32 x into shared memory with exactly the math of

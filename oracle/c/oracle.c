@@ -138,15 +138,27 @@ static int32_t dot_q8_0(const uint8_t* q, const int8_t* x) {
   return s;
 }
 
+/* ggml's IQ4_NL levels (kvalues_iq4nl): nibble -> int8 value. */
+static const int8_t kIq4nlLevels[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* Exact int32 dot of one IQ4_NL block (16 nibble bytes laid out as Q4_0's) with 32 int8 activations (an extension:
+ * ggml block_iq4_nl, level[nibble] in place of nibble - 8). */
+static int32_t dot_iq4_nl(const uint8_t* q, const int8_t* x) {
+  int32_t s = 0;
+  for (int i = 0; i < 16; ++i) s += (int32_t)kIq4nlLevels[q[i] & 15] * x[i] + (int32_t)kIq4nlLevels[q[i] >> 4] * x[i + 16];
+  return s;
+}
+
 /*
- * y[m][n] = KURN reference dot (f64, sequential over blocks; q4_0 / q8_0: (dw*dx)*s, tq2_0: (dx*dw)*s, dx of q8_0
- * activations read back as its f16), s (nullable) = int32 block dots [M][N][nb]. fmt: 0 Q4_0, 1 TQ2_0, 2 Q8_0.
+ * y[m][n] = KURN reference dot (f64, sequential over blocks; q4_0 / q8_0 / iq4_nl: (dw*dx)*s, tq2_0: (dx*dw)*s, dx of
+ * q8_0 activations read back as its f16), s (nullable) = int32 block dots [M][N][nb]. fmt: 0 Q4_0, 1 TQ2_0, 2 Q8_0,
+ * 3 IQ4_NL.
  * nthreads <= 0 uses the OpenMP default.
  */
 void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd,
               int64_t N, int64_t K, int64_t M, double* y, int32_t* s, int nthreads) {
   const int blk = fmt == 1 ? 256 : 32;
-  const int qb = fmt == 0 ? 16 : fmt == 1 ? 64 : 32;
+  const int qb = (fmt == 0 || fmt == 3) ? 16 : fmt == 1 ? 64 : 32;
   const int64_t nb = K / blk;
 #ifdef _OPENMP
   if (nthreads > 0) omp_set_num_threads(nthreads);
@@ -162,6 +174,7 @@ void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const
       for (int64_t b = 0; b < nb; ++b) {
         const int32_t d = fmt == 0   ? dot_q4_0(row + b * qb, xr + b * blk)
                           : fmt == 1 ? dot_tq2_0(row + b * qb, xr + b * blk)
+                          : fmt == 3 ? dot_iq4_nl(row + b * qb, xr + b * blk)
                                      : dot_q8_0(row + b * qb, xr + b * blk);
         if (s) s[(m * N + n) * nb + b] = d;
         const double dw = (double)orc_half_to_float((uint16_t)ws[n * nb + b]);

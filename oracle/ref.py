@@ -9,12 +9,17 @@ import numpy as np
 
 # q8_0 weights are an extension beyond the reference (which has Q4_0 and TQ2_0 only): ggml's Q8_0 block of an f16 scale
 # and 32 int8 values, against q8_0 activations, with Q4_0's multiply order; pinned to gguf-py's Q8_0 codec.
-BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32}
-ACT = {"q4_0": "q8_0", "tq2_0": "q8_K", "q8_0": "q8_0"}
-QBYTES = {"q4_0": 16, "tq2_0": 64, "q8_0": 32}
-NBYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34}
-QOFF = {"q4_0": 2, "tq2_0": 0, "q8_0": 2}
-SOFF = {"q4_0": 0, "tq2_0": 64, "q8_0": 0}
+# iq4_nl weights are a second extension: ggml's IQ4_NL block (f16 scale, 16 bytes of nibbles laid out as Q4_0's) whose
+# nibbles index a fixed table of 16 int8 levels instead of nibble - 8; q8_0 activations and Q4_0's multiply order;
+# pinned to gguf-py's IQ4_NL codec.
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32}
+ACT = {"q4_0": "q8_0", "tq2_0": "q8_K", "q8_0": "q8_0", "iq4_nl": "q8_0"}
+QBYTES = {"q4_0": 16, "tq2_0": 64, "q8_0": 32, "iq4_nl": 16}
+NBYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18}
+QOFF = {"q4_0": 2, "tq2_0": 0, "q8_0": 2, "iq4_nl": 2}
+SOFF = {"q4_0": 0, "tq2_0": 64, "q8_0": 0, "iq4_nl": 0}
+# ggml's IQ4_NL levels (kvalues_iq4nl), the codebook of the format
+IQ4_NL_LEVELS = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], dtype=np.int8)
 TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:113)
 
 F32 = np.float32
@@ -131,8 +136,17 @@ def decode_q8_0(wq, k):
     return wq[:, :k].view(np.int8).copy()
 
 
+def decode_iq4_nl(wq, k):
+    """IQ4_NL quant plane uint8 [n][k/2] -> int8 values [n][k] = level[nibble], nibbles laid out as Q4_0's (byte i
+    of a block: value i in the low nibble, value i + 16 in the high nibble)."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    n = wq.shape[0]
+    blocks = wq[:, : k // 2].reshape(n, k // 32, 16)
+    return np.concatenate([IQ4_NL_LEVELS[blocks & 15], IQ4_NL_LEVELS[blocks >> 4]], axis=-1).reshape(n, k)
+
+
 def decode(fmt, wq, k):
-    return {"q4_0": decode_q4_0, "tq2_0": decode_tq2_0, "q8_0": decode_q8_0}[fmt](wq, k)
+    return {"q4_0": decode_q4_0, "tq2_0": decode_tq2_0, "q8_0": decode_q8_0, "iq4_nl": decode_iq4_nl}[fmt](wq, k)
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -170,7 +184,7 @@ def reference_dot(fmt, ws, xd, s):
     total = np.zeros((m, n), dtype=np.float64)
     for b in range(nb):
         sb = s[:, :, b].astype(np.float64)
-        if fmt in ("q4_0", "q8_0"):
+        if fmt != "tq2_0":
             total += (dw[None, :, b] * dx[:, None, b]) * sb
         else:
             total += (dx[:, None, b] * dw[None, :, b]) * sb
@@ -218,20 +232,21 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
     """ggml weight blocks (bytes) for n rows of k values.
 
     random:  q4_0 quant bytes uniform 0..255, d = f16(|N(0, 0.02)|); tq2_0 crumbs uniform {0,1,2},
-             d = f16(|N(0, 0.05)|); q8_0 values uniform -127..127, d = f16(|N(0, 0.002)|).
-    extreme: q4_0 nibbles only 0 or 15; tq2_0 crumbs 0, 2 and 3 (3 decodes to +2); q8_0 values -128, -127 and 127;
+             d = f16(|N(0, 0.05)|); q8_0 values uniform -127..127, d = f16(|N(0, 0.002)|); iq4_nl nibbles uniform
+             0..15, d = f16(|N(0, 0.002)|).
+    extreme: q4_0 / iq4_nl nibbles only 0 or 15 (levels -127 and 113 for iq4_nl); tq2_0 crumbs 0, 2 and 3 (3 decodes to +2); q8_0 values -128, -127 and 127;
              scales include 0, f16 subnormals,
              the largest normal f16 below 2^8 and negative scales."""
     blk = BLOCK[fmt]
     nb = k // blk
     out = np.zeros((n, nb, NBYTES[fmt]), dtype=np.uint8)
-    if fmt == "q4_0":
+    if fmt in ("q4_0", "iq4_nl"):
         if extreme:
             nib = rng.choice(np.array([0, 15], dtype=np.uint8), size=(n, nb, 32))
         else:
             nib = rng.integers(0, 16, size=(n, nb, 32), dtype=np.uint8)
         q = (nib[:, :, :16] | (nib[:, :, 16:] << 4)).astype(np.uint8)
-        sd = 0.02
+        sd = 0.02 if fmt == "q4_0" else 0.002
     elif fmt == "q8_0":
         vals = rng.choice(np.array([-128, -127, 127], dtype=np.int8), size=(n, nb, 32)) if extreme else \
             rng.integers(-127, 128, size=(n, nb, 32)).astype(np.int8)
@@ -327,9 +342,9 @@ def random_split(fmt, rng, n, k):
     """Split planes directly (fast path for large synthetic layers): same distributions as weight_blocks."""
     blk = BLOCK[fmt]
     nb = k // blk
-    if fmt == "q4_0":
+    if fmt in ("q4_0", "iq4_nl"):
         wq = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
-        d = np.abs(rng.normal(0.0, 0.02, size=(n, nb))).astype(np.float16)
+        d = np.abs(rng.normal(0.0, 0.02 if fmt == "q4_0" else 0.002, size=(n, nb))).astype(np.float16)
     elif fmt == "q8_0":
         wq = rng.integers(-127, 128, size=(n, k), dtype=np.int8).view(np.uint8)
         d = np.abs(rng.normal(0.0, 0.002, size=(n, nb))).astype(np.float16)

@@ -147,6 +147,8 @@ def _layer(fmt, n, k, m, seed, dev):
     ("q8_0", 4096, 4096, 1),    # Q8_0 weights (extension beyond the reference)
     ("q8_0", 4100, 14336, 3),   # Q8_0 tall K, row tail, 3 columns
     ("q8_0", 300, 28672, 1),    # Q8_0 K = 28672: two chunks per thread
+    ("iq4_nl", 4096, 4096, 1),  # IQ4_NL weights (second extension)
+    ("iq4_nl", 4100, 14336, 3), # IQ4_NL tall K, row tail, 3 columns
 ])
 def test_gemv_full_size_matches_oracle(cuda, fmt, n, k, m):
     wq, ws, x, twq, tws, tx = _layer(fmt, n, k, m, 11, cuda)
@@ -160,7 +162,8 @@ def test_gemv_full_size_matches_oracle(cuda, fmt, n, k, m):
 
 
 @pytest.mark.parametrize("fmt,n,k", [("tq2_0", 57344, 8192), ("tq2_0", 8192, 28672), ("q4_0", 128256, 8192),
-                                     ("q4_0", 28672, 4096), ("q4_0", 6144, 4096), ("q8_0", 128256, 4096)])
+                                     ("q4_0", 28672, 4096), ("q4_0", 6144, 4096), ("q8_0", 128256, 4096),
+                                     ("iq4_nl", 28672, 4096)])
 def test_gemv_large_layers_sampled_rows(cuda, fmt, n, k):
     """Configs 3/4 at full size: every output row checked against the C oracle on a sample of rows (the row
     result does not depend on the other rows), plus the int32 dots of the sampled rows."""
@@ -180,7 +183,7 @@ def test_gemv_large_layers_sampled_rows(cuda, fmt, n, k):
 def test_gemv_many_columns_and_row_stride(cuda):
     """M > 4 (column groups) and a weight row stride larger than the quant bytes."""
     rng = np.random.default_rng(3)
-    for fmt, n, k, m in (("q4_0", 37, 416, 9), ("tq2_0", 37, 768, 6), ("q8_0", 37, 416, 7)):
+    for fmt, n, k, m in (("q4_0", 37, 416, 9), ("tq2_0", 37, 768, 6), ("q8_0", 37, 416, 7), ("iq4_nl", 37, 416, 11)):
         wq, ws = ref.random_split(fmt, rng, n, k)
         wide = np.zeros((n, wq.shape[1] + 48), np.uint8)
         wide[:, : wq.shape[1]] = wq
@@ -195,7 +198,7 @@ def test_gemv_many_columns_and_row_stride(cuda):
 
 def test_gemv_edge_sizes(cuda):
     rng = np.random.default_rng(4)
-    for fmt in ("q4_0", "tq2_0", "q8_0"):
+    for fmt in ("q4_0", "tq2_0", "q8_0", "iq4_nl"):
         blk = ref.BLOCK[fmt]
         for n, k, m in ((0, blk, 1), (3, blk, 0), (1, blk, 1), (2, 0, 2)):
             wq, ws = ref.random_split(fmt, rng, n, k)
@@ -244,7 +247,8 @@ def test_launch_counter_counts_kernels(cuda):
 
 
 @pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 1000, 4096, 1), ("tq2_0", 998, 8192, 3), ("q4_0", 301, 28672, 2),
-                                       ("tq2_0", 37, 2048, 1), ("q8_0", 1000, 4096, 1), ("q8_0", 301, 14336, 2)])
+                                       ("tq2_0", 37, 2048, 1), ("q8_0", 1000, 4096, 1), ("q8_0", 301, 14336, 2),
+                                       ("iq4_nl", 1000, 4096, 1), ("iq4_nl", 301, 14336, 2)])
 def test_ring_and_register_paths_identical(cuda, fmt, n, k, m):
     """The TMA bulk-copy ring and the register-streaming path give the same int32 dots and bit-identical Y, for every
     ring depth and rows-per-group setting; the bounded waits never fire."""
@@ -307,7 +311,8 @@ def test_allgather_receive_times_out_and_reports(cuda):
 
 
 @pytest.mark.parametrize("fmt,n,k,m", [("tq2_0", 8192, 28672, 1), ("q4_0", 4100, 14336, 1), ("q4_0", 333, 28672, 3),
-                                       ("tq2_0", 37, 28672, 2), ("q8_0", 4100, 14336, 1), ("q8_0", 333, 8192, 3)])
+                                       ("tq2_0", 37, 28672, 2), ("q8_0", 4100, 14336, 1), ("q8_0", 333, 8192, 3),
+                                       ("iq4_nl", 4100, 14336, 1)])
 def test_split_k_matches_oracle_and_is_deterministic(cuda, fmt, n, k, m):
     """Tall-K layers through the split-K schedule (workspace of partial sums + ordered combine): same quantized
     activations, Y within the rule of the exact reference, within f32 rounding of the single-launch Y, and repeatable."""
@@ -340,7 +345,7 @@ def _split_k_checks(cuda, fmt, n, k, m):
 
 @pytest.mark.parametrize("fmt,n,k", [("tq2_0", 998, 8192), ("q4_0", 1001, 4096), ("tq2_0", 8192, 28672),
                                      ("q4_0", 301, 28672), ("tq2_0", 37, 2048), ("tq2_0", 5, 4096),
-                                     ("q8_0", 1001, 4096), ("q8_0", 300, 14336)])
+                                     ("q8_0", 1001, 4096), ("q8_0", 300, 14336), ("iq4_nl", 1001, 4096)])
 def test_warp_rows_path_matches_oracle(cuda, fmt, n, k):
     """The warp-rows schedule (each warp owns whole rows, own TMA ring, one column) for several warps / rows-per-group
     / ring-depth settings: exact int32 dots, Y within the rule of the exact reference, the same Y from the fused
@@ -380,7 +385,7 @@ def test_warp_rows_path_matches_oracle(cuda, fmt, n, k):
 
 @pytest.mark.parametrize("fmt,n,k", [("tq2_0", 998, 8192), ("tq2_0", 8192, 28672), ("q4_0", 1001, 4096),
                                      ("q4_0", 300, 28672), ("tq2_0", 5, 4096), ("tq2_0", 64, 14336),
-                                     ("q8_0", 1001, 4096), ("q8_0", 300, 14336)])
+                                     ("q8_0", 1001, 4096), ("q8_0", 300, 14336), ("iq4_nl", 1001, 4096)])
 def test_cluster_shared_prologue_identical(cuda, fmt, n, k):
     """No cluster, and clusters of 2, 4 and 8 CTAs splitting the fused activation prologue (each member quantizes its share and stores
     it into every member's shared memory): the same quantized bytes written out, bit-identical Y, the bounded waits
@@ -423,7 +428,7 @@ def test_quant_gemv_into_given_output(cuda):
 
 @pytest.mark.parametrize("fmt,n,k", [("q4_0", 37, 416), ("tq2_0", 5, 768), ("q4_0", 4100, 4096), ("tq2_0", 999, 8192),
                                      ("q4_0", 1, 32), ("tq2_0", 3, 28672), ("q8_0", 37, 416), ("q8_0", 999, 4096),
-                                     ("q8_0", 1, 32)])
+                                     ("q8_0", 1, 32), ("iq4_nl", 37, 416), ("iq4_nl", 999, 4096)])
 def test_split_device_matches_host_split(cuda, fmt, n, k):
     """The on-device cut of ggml blocks into WQ / WS (b2q_split_blocks) is byte-identical to host.split, also with a
     padded row stride, an unaligned source and a partial last CTA."""
@@ -449,7 +454,7 @@ def test_gguf_file_to_gemv_matches_oracle(cuda, tmp_path):
 
     rng = np.random.default_rng(72)
     specs = [("blk.0.attn_output.weight", "q4_0", 300, 4096), ("blk.0.ffn_up.weight", "tq2_0", 200, 8192),
-             ("blk.0.ffn_down.weight", "q8_0", 150, 4096)]
+             ("blk.0.ffn_down.weight", "q8_0", 150, 4096), ("blk.0.attn_q.weight", "iq4_nl", 130, 4096)]
     w = gguf.GGUFWriter(str(tmp_path / "m.gguf"), "llama")
     raws = {}
     for name, fmt, n, k in specs:
@@ -567,3 +572,25 @@ def test_tensor_core_persistent_tiles(cuda, fmt, n, k, m):
     _lib.call("b2q_device_error", ctypes.byref(code), 1)
     assert code.value == 0
 
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("iq4_nl", 37, 416, 3), ("iq4_nl", 1000, 4096, 1), ("iq4_nl", 300, 4096, 16)])
+def test_iq4_nl_variants_and_many_columns(cuda, fmt, n, k, m):
+    """IQ4_NL (ggml's 16-level non-linear 4-bit format): the byte-wise and the byte-permute lookup variants give the
+    oracle's exact int32 block dots and the same Y; the fused call equals the separate ones; 8+ columns stay on the
+    GEMV path (no tensor-core kernel for this format) and still match; extreme nibbles (levels -127 and 113) too."""
+    for extreme in (False, True):
+        W, x = ref.problem(fmt, n, k, m, seed=31, extreme=extreme)
+        wq, ws = ref.split(fmt, W, n, k)
+        twq, tws, tx = _t(wq, cuda), _t(ws, cuda), _t(x, cuda)
+        xq, xd = host.quantize(fmt, tx)
+        oq, od = ref.quantize(fmt, x)
+        assert np.array_equal(xq.cpu().numpy(), oq) and _same_f32(xd.cpu().numpy(), od)
+        r, os_ = ref.gemv(fmt, wq, ws, oq, od, k)
+        y2, s2 = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
+        y0, s0 = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=0, store_s=True)
+        assert np.array_equal(s2.cpu().numpy(), os_) and np.array_equal(s0.cpu().numpy(), os_)
+        assert _same_f32(y0.cpu().numpy(), y2.cpu().numpy())
+        assert ref.relerr(y2.cpu().numpy(), r) <= TOL
+        assert _same_f32(host.quant_gemv(fmt, twq, tws, tx, n, k, split=False).cpu().numpy(), y2.cpu().numpy())
+        assert ref.relerr(host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy(), r) <= TOL

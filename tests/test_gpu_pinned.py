@@ -41,7 +41,8 @@ def _no_device_error():
 @pytest.mark.parametrize("fmt,n,k,m,ldx", [("q4_0", 300, 4096, 1, None), ("tq2_0", 999, 8192, 3, None),
                                            ("q8_0", 130, 4096, 2, 4100), ("tq2_0", 8192, 28672, 1, None),
                                            ("q4_0", 4100, 4096, 1, 4104), ("q4_0", 1000, 4096, 16, None),
-                                           ("tq2_0", 999, 4096, 12, None), ("q4_0", 37, 416, 5, None)])
+                                           ("tq2_0", 999, 4096, 12, None), ("q4_0", 37, 416, 5, None),
+                                           ("iq4_nl", 999, 4096, 2, None)])
 def test_pinned_matches_device_call(cuda, fmt, n, k, m, ldx):
     """Same Y as the device-memory fused call, bit for bit (GEMV schedules, and the quantizer + tensor-core GEMM for
     8+ columns), within the rule of the exact reference; two launches for the one-kernel schedules."""

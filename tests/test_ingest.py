@@ -26,7 +26,8 @@ def _write(path, tensors):
 def test_gguf_tensor_round_trip_and_split(tmp_path):
     rng = np.random.default_rng(61)
     specs = [("blk.0.ffn_down.weight", "q4_0", 37, 416), ("blk.0.ffn_gate.weight", "tq2_0", 5, 768),
-             ("output.weight", "q4_0", 64, 4096), ("blk.0.ffn_up.weight", "q8_0", 11, 1024)]
+             ("output.weight", "q4_0", 64, 4096), ("blk.0.ffn_up.weight", "q8_0", 11, 1024),
+             ("blk.0.attn_k.weight", "iq4_nl", 7, 512)]
     tensors = [(name, fmt, ref.weight_blocks(fmt, rng, n, k), n, k) for name, fmt, n, k in specs]
     path = tmp_path / "t.gguf"
     _write(path, tensors)

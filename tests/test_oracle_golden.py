@@ -105,6 +105,33 @@ def test_q8_0_gemv_oracle_pinned_to_gguf(extreme):
     assert np.array_equal(sc, s) and np.array_equal(rc.view(np.uint64), r.view(np.uint64))
 
 
+@pytest.mark.parametrize("extreme", [False, True])
+def test_iq4_nl_oracle_pinned_to_gguf(extreme):
+    """IQ4_NL weights (a second extension) against q8_0 activations: the oracle's decode equals gguf-py's IQ4_NL
+    dequantization (level[nibble] * d), its int32 block dots are the int8-level x int8 products, its f64 reference dot
+    equals the float64 product of gguf-py's dequantized operands, and the C oracle agrees bit for bit."""
+    gq = pytest.importorskip("gguf.quants")
+    gguf = pytest.importorskip("gguf")
+    n, k, m = 9, 2048, 3
+    W, x = ref.problem("iq4_nl", n, k, m, seed=13, extreme=extreme)
+    wq, ws = ref.split("iq4_nl", W, n, k)
+    T = gguf.GGMLQuantizationType.IQ4_NL
+    wdq = gq.dequantize(np.frombuffer(W, dtype=np.uint8).reshape(n, -1), T).astype(np.float64)
+    d = np.repeat(ws.view(np.float16).astype(np.float64), 32, axis=1)
+    assert np.array_equal(ref.decode("iq4_nl", wq, k) * d, wdq)
+    xq, xd = ref.quantize("iq4_nl", x)
+    r, s = ref.gemv("iq4_nl", wq, ws, xq, xd, k)
+    vals = ref.decode("iq4_nl", wq, k).astype(np.int64).reshape(n, k // 32, 32)
+    assert np.array_equal(s, np.einsum("nbv,mbv->mnb", vals, xq.astype(np.int64).reshape(m, k // 32, 32)))
+    from comp_b200 import host
+
+    xdq = gq.dequantize(np.frombuffer(host.q8_0_blocks(xq, xd), dtype=np.uint8).reshape(m, -1),
+                        gguf.GGMLQuantizationType.Q8_0).astype(np.float64)
+    assert ref.relerr(xdq @ wdq.T, r) <= 1e-9
+    rc, sc = native.gemv("iq4_nl", wq, ws, xq, xd, k, want_s=True)
+    assert np.array_equal(sc, s) and np.array_equal(rc.view(np.uint64), r.view(np.uint64))
+
+
 def test_dp4a_and_decode_probes_match_reference(golden):
     assert np.array_equal(ref.dp4a_ref(golden["dp4a/a"], golden["dp4a/b"], golden["dp4a/c"]), golden["dp4a/out"])
     assert np.array_equal(ref.decode_q4_0(golden["decode/q4_0/wq"], 32), golden["decode/q4_0/out"])
