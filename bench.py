@@ -284,10 +284,10 @@ def main():
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
     ap.add_argument("--pdl", default="on", choices=["on", "off"], help="programmatic dependent launch of the GEMVs")
-    ap.add_argument("--e2e-api", default="auto", choices=["auto", "pinned", "device"],
+    ap.add_argument("--e2e-api", default="pinned", choices=["pinned", "device"],
                     help="end-to-end leg: pinned host x in and Y stored into pinned host memory by the kernels "
                          "(N = 1: b2q_quant_gemv_pinned, N > 1: RowShardedGemv(x_host, out=y_host)), or device "
-                         "buffers with torch memcpys around each call; auto = pinned at N = 1, device at N > 1")
+                         "buffers with torch memcpys around each call")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -468,7 +468,7 @@ def main():
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
 
     y_dev = [torch.empty((m, L.n), dtype=torch.float32, device=dev) for L in layers] if world == 1 else None
-    pinned = args.e2e_api == "pinned" or (args.e2e_api == "auto" and world == 1)
+    pinned = args.e2e_api == "pinned"
     if pinned and world == 1:
         pin_ws = [torch.empty(max(256, host.pinned_workspace_size(L.fmt, L.n, L.k, m)), dtype=torch.uint8,
                               device=dev) for L in layers]
