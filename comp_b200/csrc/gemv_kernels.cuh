@@ -124,6 +124,18 @@ __device__ __forceinline__ uint32_t iq4nl_levels4(uint32_t nibs) {
   return __byte_perm(lo, hi, 0x3210u | ((nibs >> 1) & 0x4444u));
 }
 
+// IQ4_NL activation chunks are kept interleaved the way the lookups order the weight levels: a weight word's low 16
+// bits give the levels of values 4k, 16+4k, 4k+1, 16+4k+1 and its high 16 bits those of 4k+2, 16+4k+2, 4k+3,
+// 16+4k+3. Field 0 word k = bytes 0, 1 of the natural words k of fields 0 and 1, interleaved; field 1 word k = bytes
+// 2, 3. Applied once where a chunk's activations are loaded, so the per-row dot does no permutes of its own.
+__device__ __forceinline__ void iq4nl_interleave(uint4 (&x)[4]) {
+  const uint4 a = x[0], b = x[1];
+  x[0] = make_uint4(__byte_perm(a.x, b.x, 0x5140u), __byte_perm(a.y, b.y, 0x5140u), __byte_perm(a.z, b.z, 0x5140u),
+                    __byte_perm(a.w, b.w, 0x5140u));
+  x[1] = make_uint4(__byte_perm(a.x, b.x, 0x7362u), __byte_perm(a.y, b.y, 0x7362u), __byte_perm(a.z, b.z, 0x7362u),
+                    __byte_perm(a.w, b.w, 0x7362u));
+}
+
 // Base pointers of this CTA's K split (blockIdx.y); with one split every offset is zero.
 template <int FMT>
 struct Split {
@@ -356,14 +368,19 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
 template <int FMT, bool BYTES>
 __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int xsum) {
   if (FMT == 3 && !BYTES) {
-    // IQ4_NL: word k holds the nibbles of values 4k..4k+3 (low) and 16+4k..16+4k+3 (high); the lookups give the levels
-    // in nibble order (value 4k, 16+4k, 4k+1, 16+4k+1 | 4k+2, ...), so the activations are interleaved to match
+    // IQ4_NL: word k holds the nibbles of values 4k..4k+3 (low) and 16+4k..16+4k+3 (high). Table indices and
+    // half-selectors are formed once per word (iq4nl_levels4's steps, both halves at once); the lookups give the
+    // levels in nibble order, which is the order the activations are kept in (iq4nl_interleave)
     int s = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const uint32_t wk = word_of(w, k), xa = word_of(x[0], k), xb = word_of(x[1], k);
-      s = __dp4a((int)iq4nl_levels4(wk), (int)__byte_perm(xa, xb, 0x5140u), s);
-      s = __dp4a((int)iq4nl_levels4(wk >> 16), (int)__byte_perm(xa, xb, 0x7362u), s);
+      const uint32_t wk = word_of(w, k);
+      const uint32_t idx = wk & 0x77777777u, sel = 0x32103210u | ((wk >> 1) & 0x44444444u);
+      const uint32_t ih = idx >> 16;
+      const uint32_t va = __byte_perm(__byte_perm(kIq4Lv0, kIq4Lv1, idx), __byte_perm(kIq4Lv2, kIq4Lv3, idx), sel);
+      const uint32_t vb = __byte_perm(__byte_perm(kIq4Lv0, kIq4Lv1, ih), __byte_perm(kIq4Lv2, kIq4Lv3, ih), sel >> 16);
+      s = __dp4a((int)va, (int)word_of(x[0], k), s);
+      s = __dp4a((int)vb, (int)word_of(x[1], k), s);
     }
     return s;
   }
@@ -434,7 +451,10 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const uint4 (&x)[4], int
         const int wb = (int)((wk >> (8 * t)) & 0xffu);
 #pragma unroll
         for (int j = 0; j < Fmt<FMT>::kFields; ++j) {
-          const int xb = (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
+          // IQ4_NL chunks are interleaved (iq4nl_interleave): natural field j, byte t sits in word k of field t/2,
+          // byte 2 * (t % 2) + j
+          const int xb = FMT == 3 ? (int)(int8_t)((word_of(x[t >> 1], k) >> (8 * (2 * (t & 1) + j))) & 0xffu)
+                                  : (int)(int8_t)((word_of(x[j], k) >> (8 * t)) & 0xffu);
           const int val = (FMT == 3)   ? (int)(int8_t)(iq4nl_levels4((wb >> (4 * j)) & 15) & 0xffu)
                           : (FMT == 0) ? ((wb >> (4 * j)) & 15) - 8
                           : (FMT == 1) ? ((wb >> (2 * j)) & 3) - 1
@@ -465,6 +485,7 @@ __device__ __forceinline__ void load_xchunk(const GemvParams& p, const uint8_t* 
     const uint4* col = reinterpret_cast<const uint4*>(xs + (int64_t)m * p.K);
 #pragma unroll
     for (int j = 0; j < Fmt<FMT>::kFields; ++j) o.x[j] = col[j * p.C + c];
+    if (FMT == 3) iq4nl_interleave(o.x);
     o.sum = xsum[m * p.C + c];
     o.dx = xscale[m * nblk + (c >> Fmt<FMT>::kChunkShift)];
   } else {
@@ -659,6 +680,10 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
       o.x[0] = src[0];
       o.x[1] = src[1];
       o.dx = Split<FMT>::xd(p)[c];
+      if (FMT == 3) {  // no offset term; the chunk interleaved for the level lookups
+        iq4nl_interleave(o.x);
+        return;
+      }
     } else if (FMT == 2) {
       o.x[0] = *reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 16);
       o.dx = Split<FMT>::xd(p)[c >> 1];
@@ -740,6 +765,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
       dst[1] = o.x[1];
       if (p.xd_out) Split<FMT>::xd_out(p)[c] = o.dx;
     }
+    if (FMT == 3) iq4nl_interleave(o.x);  // after the natural-order XQ write-out
     return;
   }
   // TQ2_0 / q8_K: field j of chunk c holds block values (cc/2)*128 + j*32 + (cc%2)*16 + t, t = 0..15
