@@ -88,6 +88,23 @@ def test_compute_calls_refuse_cpu_tensors():
                   torch.zeros((1, 64), dtype=torch.int8), torch.zeros((1, 2)), 2, 64)
     with pytest.raises(ValueError, match="unknown weight format"):
         host.quantize("q5_K", x)
+    # the pinned-host form needs the weights on a GPU too
+    with pytest.raises(RuntimeError, match="CUDA"):
+        host.quant_gemv_pinned("q4_0", torch.zeros((2, 32), dtype=torch.uint8), torch.zeros((2, 2), dtype=torch.int16),
+                               x, 2, 64, torch.zeros((1, 2)))
+
+
+def test_workspace_sizes_need_no_gpu():
+    """Workspace queries are host arithmetic: the pinned form stages M*K f32 (rounded up to 256 bytes) in front of the
+    GEMV's own workspace; empty layers need none; an unknown format gives 0."""
+    for fmt in ("q4_0", "tq2_0", "q8_0", "iq4_nl"):
+        for n, k, m in ((4096, 4096, 1), (37, 1024, 3), (128256, 8192, 16)):
+            g = host.workspace_size(fmt, n, k, m)
+            assert host.pinned_workspace_size(fmt, n, k, m) == -(-m * k * 4 // 256) * 256 + g
+        assert host.pinned_workspace_size(fmt, 0, 4096, 1) == 0
+    # IQ4_NL has no tensor-core path, so many columns need no activation tiles
+    assert host.workspace_size("iq4_nl", 128256, 8192, 16) == 0 < host.workspace_size("q4_0", 128256, 8192, 16)
+    assert _lib.load().b2q_pinned_workspace_size(7, 64, 1024, 1) == 0
 
 
 def test_partition_covers_rows_once():
