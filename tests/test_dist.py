@@ -91,3 +91,47 @@ def test_missing_rank_ends_in_an_error_not_a_hang():
             p.kill()
     assert res[1] == "left"
     assert res[0].startswith("error"), res[0]
+
+
+def _host_buffer_checks_worker(rank, world, port, q):
+    """RowShardedGemv's host-buffer form refuses, on every rank and before any collective or launch, an output that is
+    not a pinned CPU tensor of the full shape and a host x that is not pinned (the CPU here has no pinned memory)."""
+    from comp_b200.dist import RowShardedGemv
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        n, k = 37, 416
+        row0, rows = partition(n, world)[rank]
+        wq = torch.zeros((rows, k // 2), dtype=torch.uint8)
+        ws = torch.zeros((rows, k // 32), dtype=torch.int16)
+        layer = RowShardedGemv("q4_0", wq, ws, n, k, exchange="nccl")
+        x = torch.zeros((2, k), dtype=torch.float32)
+        verdicts = []
+        for out in (torch.zeros((2, n)), torch.zeros((2, n - 1)), torch.zeros((2, n), dtype=torch.float64)):
+            try:
+                layer(x, out=out)
+                verdicts.append("accepted")
+            except ValueError as e:
+                verdicts.append("refused" if "pinned" in str(e) else f"other: {e}")
+        try:
+            layer(x)  # a host x must be pinned: refused in the staging step
+            verdicts.append("accepted")
+        except ValueError as e:
+            verdicts.append("refused" if "pinned" in str(e) else f"other: {e}")
+        q.put((rank, verdicts))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_host_buffers_refused_before_any_exchange():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_host_buffer_checks_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: ["refused"] * 4, 1: ["refused"] * 4}
