@@ -9,7 +9,9 @@
  *   gemv_tq2_0   TQ2_0 weights (WQ u8 [N][K/4], WS f16 bits [N][K/256]) x q8_K activations -> Y f32 [M][N]
  *
  * Conventions shared by every entry point:
- *   - All data pointers are DEVICE pointers of the current CUDA device; the library never allocates or frees
+ *   - All data pointers are DEVICE pointers of the current CUDA device, except the host buffers of the pinned
+ *     entry points (b2q_quant_gemv_pinned, b2q_stage_pinned, b2q_host_device_pointer), which must be page-locked
+ *     host memory mapped for that device and are checked before any launch; the library never allocates or frees
  *     device memory (the caller owns every buffer).
  *   - Sizes and strides are int64 element counts (bytes for u8/i8 planes).
  *   - Work is enqueued on `stream` (NULL = legacy default stream) and is asynchronous.
