@@ -3,6 +3,7 @@
     python -m comp_b200 check  SPEC [k=v ...]   validate a `target triton` spec (and its tune space)
     python -m comp_b200 verify SPEC [k=v ...]   every config of the spec on the GPU vs exact references
     python -m comp_b200 verify --all            the full GPU self-check set (dp4a, both GEMVs, both variants)
+    python -m comp_b200 verify --all --json     the same as JSON lines, each GEMV also timed (us, GB/s, HBM fraction)
 
 `kurn check|verify SPEC` routes here for specs with `target triton` through comp_b200.kurn_ext. COMP's `gen` and
 `mix` (PTX/SASS generation and inspection) have no counterpart: this backend ships its own compiled library.
@@ -47,7 +48,7 @@ def cmd_verify(args):
     from . import verify
 
     if "--all" in args:
-        return 1 if verify.run_all() else 0
+        return 1 if verify.run_all(as_json="--json" in args) else 0
     try:
         spec, base, tune = _spec(args)
         spec.resolve(base)

@@ -10,6 +10,9 @@ plain torch operations, independently of this package's kernels:
 The repository's parity tests additionally pin the kernels to the reference's recorded outputs.
 """
 
+import json
+import os
+
 import numpy as np
 import torch
 
@@ -32,9 +35,11 @@ def ref_quantize(fmt, x):
     if host.FORMATS[fmt]["act"] == "q8_0":
         b = x.reshape(m, k // 32, 32)
         amax = b.abs().amax(dim=-1)
-        d = amax / 127.0
+        # every division tensor by tensor: torch may evaluate a scalar divisor or dividend as a multiply by a
+        # reciprocal, which is not the correctly rounded quotient the quantizers use
+        d = amax / torch.full_like(amax, 127.0)
         nz = d != 0
-        idv = torch.where(nz, 1.0 / torch.where(nz, d, torch.ones_like(d)), torch.zeros_like(d))
+        idv = torch.where(nz, torch.ones_like(d) / torch.where(nz, d, torch.ones_like(d)), torch.zeros_like(d))
         q = _round_half_away(b * idv[..., None])
         return q.to(torch.int8).reshape(m, k), d.half().float()
     b = x.reshape(m, k // 256, 256)
@@ -44,10 +49,10 @@ def ref_quantize(fmt, x):
     first = torch.where(ax == amax[..., None], idx, torch.full_like(idx, 256)).amin(dim=-1)
     mx = torch.gather(b, -1, first.clamp(max=255)[..., None])[..., 0]
     nz = amax != 0
-    iscale = -127.0 / torch.where(nz, mx, torch.ones_like(mx))
+    iscale = torch.full_like(mx, -127.0) / torch.where(nz, mx, torch.ones_like(mx))
     q = torch.clamp(torch.round(iscale[..., None] * b), max=127.0)  # torch.round is half-to-even
     q = torch.where(nz[..., None], q, torch.zeros_like(q))
-    d = torch.where(nz, 1.0 / iscale, torch.zeros_like(iscale))
+    d = torch.where(nz, torch.ones_like(iscale) / iscale, torch.zeros_like(iscale))
     return q.to(torch.int8).reshape(m, k), d
 
 
@@ -59,7 +64,7 @@ def ref_values(fmt, wq, k):
         b = w.reshape(n, k // 32, 16)
         return torch.cat([(b & 15) - 8, (b >> 4) - 8], dim=-1).reshape(n, k)
     b = w.reshape(n, k // 256, 2, 32)  # [block][h][i] -> value h*128 + j*32 + i at bits 2j
-    v = torch.stack([((b >> (2 * j)) & 3) - 1 for j in range(4)], dim=2)  # [n][blk][h][j][i]
+    v = torch.stack([((b >> (2 * j)) & 3) - 1 for j in range(4)], dim=3)  # [n][blk][h][j][i]
     return v.reshape(n, k)
 
 
@@ -113,7 +118,23 @@ def problem(fmt, n, k, m, seed, extreme, dev):
     return wq.to(dev), ws.to(dev), x.to(dev)
 
 
-def check_gemv(fmt, n, k, m, seed=0, extreme=False, mode=2, dev=None):
+def algo_bytes(fmt, n, k, m):
+    """Algorithmic bytes of one GEMV: the weights once (ggml block bytes), the q8 activations, the f32 output."""
+    f = host.FORMATS[fmt]
+    return n * k * f["nbytes"] // f["block"] + m * (k + 4 * k // host.ACT_BLOCK[f["act"]]) + 4 * m * n
+
+
+def hbm_peak():
+    """Measured HBM GB/s of this pool (MEASURED_PEAKS.json at the repository root), or None."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def check_gemv(fmt, n, k, m, seed=0, extreme=False, mode=2, dev=None, timed=False):
     dev = dev or torch.device("cuda")
     wq, ws, x = problem(fmt, n, k, m, seed, extreme, dev)
     xq, xd = host.quantize(fmt, x)
@@ -126,8 +147,21 @@ def check_gemv(fmt, n, k, m, seed=0, extreme=False, mode=2, dev=None):
     r = ref_dot(fmt, ws, xd, exact)
     rebuilt_ok = bool(torch.equal(r_ours.view(torch.int64), r.view(torch.int64)))
     err = relerr(y, r)
-    return {"fmt": fmt, "n": n, "k": k, "m": m, "quant": quant_ok, "idots": idots_ok, "rebuilt": rebuilt_ok,
-            "relerr": err, "ok": quant_ok and idots_ok and rebuilt_ok and err <= TOL}
+    out = {"fmt": fmt, "n": n, "k": k, "m": m, "quant": quant_ok, "idots": idots_ok, "rebuilt": rebuilt_ok,
+           "relerr": err, "ok": quant_ok and idots_ok and rebuilt_ok and err <= TOL}
+    if timed:  # the GEMV alone (no S dump), event-timed on the current stream after warm-up
+        stream = torch.cuda.current_stream(dev)
+        for _ in range(3):
+            host.gemv(fmt, wq, ws, xq, xd, n, k, mode=mode)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        a.record(stream)
+        for _ in range(reps):
+            host.gemv(fmt, wq, ws, xq, xd, n, k, mode=mode)
+        b.record(stream)
+        b.synchronize()
+        out["us"] = a.elapsed_time(b) * 1e3 / reps
+    return out
 
 
 def check_dp4a(seed=0, n=1024, dev=None):
@@ -165,17 +199,35 @@ def line(r, mode, label=""):
             f"reference_dot={'bit-identical' if r['rebuilt'] else 'DIFFERS'} relerr={r['relerr']:.1e}")
 
 
-def run_all(log=print):
+def json_line(r, mode, label="", extreme=False, peak=None):
+    """The fields of `line` as one JSON object, plus (when the check was timed) us per GEMV, algorithmic GB/s and
+    the fraction of the measured HBM peak."""
+    d = {"ok": r["ok"], "fmt": r["fmt"], "op": "gemv", "mode": MODE_NAMES[mode], "config": label, "n": r["n"],
+         "k": r["k"], "m": r["m"], "extreme": extreme, "quant": "exact" if r["quant"] else "MISMATCH",
+         "idots": "exact" if r["idots"] else "MISMATCH",
+         "reference_dot": "bit-identical" if r["rebuilt"] else "DIFFERS", "relerr": float(r["relerr"])}
+    if "us" in r:
+        gbs = algo_bytes(r["fmt"], r["n"], r["k"], r["m"]) / r["us"] / 1e3
+        d.update(us=round(r["us"], 3), gbs=round(gbs, 1), hbm_frac=round(gbs / peak, 4) if peak else None)
+    return json.dumps(d)
+
+
+def run_all(log=print, as_json=False):
     fails = 0
     ok = check_dp4a(seed=3)
     fails += not ok
-    log(f"{'ok  ' if ok else 'FAIL'} dp4a.s32.s32 on the GPU == its definition (1024 edge/random words)")
+    peak = hbm_peak()
+    if as_json:
+        log(json.dumps({"ok": ok, "op": "dp4a.s32.s32", "words": 1024}))
+    else:
+        log(f"{'ok  ' if ok else 'FAIL'} dp4a.s32.s32 on the GPU == its definition (1024 edge/random words)")
     for fmt, probs in PROBLEMS.items():
         for mode in (0, 2):
             for n, k, m in probs:
                 for seed, extreme in ((1, False), (2, True)):
-                    r = check_gemv(fmt, n, k, m, seed, extreme, mode)
+                    r = check_gemv(fmt, n, k, m, seed, extreme, mode, timed=as_json)
                     fails += not r["ok"]
-                    log(line(r, mode) + (" extreme" if extreme else ""))
-    log(f"{fails} failures")
+                    log(json_line(r, mode, extreme=extreme, peak=peak) if as_json else
+                        line(r, mode) + (" extreme" if extreme else ""))
+    log(json.dumps({"failures": fails}) if as_json else f"{fails} failures")
     return fails

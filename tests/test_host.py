@@ -128,3 +128,39 @@ def test_ctypes_signatures_match_header_arity():
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), f"{name}: header has {len(params)} parameters, ctypes {len(args)}"
     assert ctypes.sizeof(ctypes.c_void_p) == 8
+
+
+def test_verify_json_line_fields():
+    """verify --all --json: COMP's per-check fields as JSON, plus us / GB/s / HBM fraction when the check was timed."""
+    import json
+
+    from comp_b200 import verify
+
+    r = {"fmt": "q4_0", "n": 4096, "k": 4096, "m": 1, "quant": True, "idots": True, "rebuilt": False,
+         "relerr": 2e-7, "ok": False, "us": 2.0}
+    d = json.loads(verify.json_line(r, 2, label="bn=32", extreme=True, peak=6000.0))
+    assert d["ok"] is False and d["mode"] == "dp4a" and d["extreme"] is True and d["config"] == "bn=32"
+    assert d["quant"] == "exact" and d["idots"] == "exact" and d["reference_dot"] == "DIFFERS"
+    want = (4096 * 4096 * 18 // 32 + 4096 + 4 * 4096 // 32 + 4 * 4096) / 2.0 / 1e3
+    assert abs(d["gbs"] - want) < 0.1 and abs(d["hbm_frac"] - want / 6000.0) < 1e-4 and d["us"] == 2.0
+    r.pop("us")
+    assert "gbs" not in json.loads(verify.json_line(r, 0))
+
+
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 37, 416, 3), ("tq2_0", 5, 1280, 2), ("tq2_0", 64, 1024, 1)])
+def test_verify_torch_references_equal_the_oracle(fmt, n, k, m):
+    """comp_b200.verify checks the kernels against torch restatements of the exact references; run here on CPU
+    tensors, they must equal the oracle (itself pinned to the reference's recorded outputs): quantizer bytes and
+    scales, decoded weights, int32 block dots and the f64 reference dot, on random and extreme data."""
+    from comp_b200 import verify
+
+    for seed, extreme in ((1, False), (2, True)):
+        wq, ws, x = verify.problem(fmt, n, k, m, seed, extreme, torch.device("cpu"))
+        xq, xd = verify.ref_quantize(fmt, x)
+        oq, od = ref.quantize(fmt, x.numpy())
+        assert np.array_equal(xq.numpy(), oq) and np.array_equal(xd.numpy().view(np.uint32), od.view(np.uint32))
+        assert np.array_equal(verify.ref_values(fmt, wq, k).numpy(), ref.decode(fmt, wq.numpy(), k))
+        r, s = ref.gemv(fmt, wq.numpy(), ws.numpy(), oq, od, k)
+        dots = verify.ref_dots(fmt, wq, xq, k)
+        assert np.array_equal(dots.numpy(), s)
+        assert np.array_equal(verify.ref_dot(fmt, ws, xd, dots).numpy().view(np.uint64), r.view(np.uint64))
