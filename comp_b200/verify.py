@@ -19,6 +19,8 @@ import torch
 from . import _lib, host
 
 TOL = 1e-5
+# ggml's IQ4_NL levels (kvalues_iq4nl)
+IQ4_NL_LEVELS = (-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113)
 MODE_NAMES = {0: "bytes", 1: "dp4a", 2: "dp4a"}
 
 
@@ -59,10 +61,16 @@ def ref_quantize(fmt, x):
 def ref_values(fmt, wq, k):
     """Decoded weight values [N][K] (int) from the quant plane."""
     n = wq.shape[0]
-    w = wq[:, : k // (2 if fmt == "q4_0" else 4)].to(torch.int32)
+    if fmt == "q8_0":  # the stored int8 values (an extension beyond the reference)
+        return wq[:, :k].view(torch.int8).to(torch.int32)
+    w = wq[:, : k // (4 if fmt == "tq2_0" else 2)].to(torch.int32)
     if fmt == "q4_0":
         b = w.reshape(n, k // 32, 16)
         return torch.cat([(b & 15) - 8, (b >> 4) - 8], dim=-1).reshape(n, k)
+    if fmt == "iq4_nl":  # Q4_0's nibble layout, each nibble a level of ggml's table (an extension)
+        lv = torch.tensor(IQ4_NL_LEVELS, dtype=torch.int32, device=wq.device)
+        b = w.reshape(n, k // 32, 16)
+        return torch.cat([lv[b & 15], lv[b >> 4]], dim=-1).reshape(n, k)
     b = w.reshape(n, k // 256, 2, 32)  # [block][h][i] -> value h*128 + j*32 + i at bits 2j
     v = torch.stack([((b >> (2 * j)) & 3) - 1 for j in range(4)], dim=3)  # [n][blk][h][j][i]
     return v.reshape(n, k)
@@ -79,11 +87,11 @@ def ref_dots(fmt, wq, xq, k):
 
 def ref_dot(fmt, ws, xd, s):
     dw = ws.view(torch.float16).double()
-    dx = (xd.half() if fmt == "q4_0" else xd).double()
+    dx = (xd.half() if fmt != "tq2_0" else xd).double()
     m, n, nb = s.shape
     total = torch.zeros((m, n), dtype=torch.float64, device=s.device)
     for b in range(nb):
-        if fmt == "q4_0":
+        if fmt != "tq2_0":  # q4_0 (and the q8_0 / iq4_nl extensions): dw * dx * s
             total += (dw[None, :, b] * dx[:, None, b]) * s[:, :, b].double()
         else:
             total += (dx[:, None, b] * dw[None, :, b]) * s[:, :, b].double()
@@ -100,11 +108,15 @@ def problem(fmt, n, k, m, seed, extreme, dev):
     g = torch.Generator(device="cpu")
     g.manual_seed(seed)
     blk = host.FORMATS[fmt]["block"]
-    if fmt == "q4_0":
+    if fmt in ("q4_0", "iq4_nl"):
         wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g)
-        if extreme:  # nibbles only 0 or 15: values -8 and +7
+        if extreme:  # nibbles only 0 or 15: values -8 and +7 (iq4_nl: levels -127 and 113)
             wq = torch.tensor([0x00, 0x0F, 0xF0, 0xFF], dtype=torch.uint8)[torch.randint(0, 4, (n, k // 2), generator=g)]
-        ws = (torch.randn((n, k // blk), generator=g) * 0.02).abs().half().view(torch.int16)
+        ws = (torch.randn((n, k // blk), generator=g) * (0.02 if fmt == "q4_0" else 0.002)).abs().half().view(torch.int16)
+    elif fmt == "q8_0":
+        lo = -128 if extreme else -127
+        wq = torch.randint(lo, 128, (n, k), dtype=torch.int16, generator=g).to(torch.int8).view(torch.uint8)
+        ws = (torch.randn((n, k // blk), generator=g) * 0.002).abs().half().view(torch.int16)
     else:
         t = torch.randint(0, 81 if not extreme else 256, (n, k // 4), dtype=torch.int64, generator=g)
         wq = ((t % 3) | ((t // 3 % 3) << 2) | ((t // 9 % 3) << 4) | ((t // 27 % 3) << 6)).to(torch.uint8) \
@@ -190,7 +202,10 @@ def check_dp4a(seed=0, n=1024, dev=None):
     return bool(np.array_equal(out.cpu().numpy().astype(np.int64), ref))
 
 
-PROBLEMS = {"q4_0": ((64, 512, 1), (37, 416, 3), (5, 96, 2)), "tq2_0": ((64, 1024, 1), (37, 768, 3), (5, 1280, 2))}
+# the reference's shapes (src/komp/verify.py PROBLEMS) for its two formats, and the same Q4_0 shapes for the two
+# extensions beyond it
+PROBLEMS = {"q4_0": ((64, 512, 1), (37, 416, 3), (5, 96, 2)), "tq2_0": ((64, 1024, 1), (37, 768, 3), (5, 1280, 2)),
+            "q8_0": ((64, 512, 1), (37, 416, 3), (5, 96, 2)), "iq4_nl": ((64, 512, 1), (37, 416, 3), (5, 96, 2))}
 
 
 def line(r, mode, label=""):

@@ -147,7 +147,8 @@ def test_verify_json_line_fields():
     assert "gbs" not in json.loads(verify.json_line(r, 0))
 
 
-@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 37, 416, 3), ("tq2_0", 5, 1280, 2), ("tq2_0", 64, 1024, 1)])
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 37, 416, 3), ("tq2_0", 5, 1280, 2), ("tq2_0", 64, 1024, 1),
+                                       ("q8_0", 37, 416, 3), ("iq4_nl", 37, 416, 3)])
 def test_verify_torch_references_equal_the_oracle(fmt, n, k, m):
     """comp_b200.verify checks the kernels against torch restatements of the exact references; run here on CPU
     tensors, they must equal the oracle (itself pinned to the reference's recorded outputs): quantizer bytes and
