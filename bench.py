@@ -13,6 +13,10 @@ output; value = sum over layers / step time. Weights random-initialised with the
 N > 1 (torchrun, one process per GPU): every layer is row-sharded across the ranks (strong scaling: the same layers at
 every N); each rank runs its rows, then the output slices are all-gathered so every rank holds the full Y.
 
+End to end (the "e2e" key): the same layers through the public API with host buffers, every step -- pinned host x
+in, Y stored into pinned host memory by the kernels, a host stream synchronize (N = 1: b2q_quant_gemv_pinned per
+layer; N > 1: RowShardedGemv(x_host, out=y_host)); --e2e-api device uses device buffers with torch memcpys instead.
+
 --impl reference: the reference's CPU path (the C + OpenMP restatement of COMP's quantizers and KURN's reference dot,
 oracle/c/oracle.c, all host threads) on the same workload; rank 0 only.
 """
