@@ -40,6 +40,17 @@ def test_library_metadata_calls_need_no_gpu():
     with pytest.raises(ValueError, match="variant|multiple|null"):
         _lib.call("b2q_gemv_tq2_0", 16, 64, 16, 16, 16, 16, None, 4, 100, 1, 2, None)
     assert "multiple" in _lib.last_error()
+    lib = _lib.load()
+    # the newer entry points validate on the host too, before any CUDA call
+    with pytest.raises(ValueError, match="multiple"):
+        _lib.call("b2q_gemv_iq4_nl", 16, 16, 16, 16, 16, 16, None, 4, 100, 1, 2, None)
+    assert lib.b2q_quant_gemv_pinned(9, None, 0, None, None, 0, None, 4, 64, 1, None, 0, None) == -1
+    assert "IQ4_NL (3)" in _lib.last_error()
+    assert lib.b2q_quant_gemv_pinned(0, None, 0, None, None, 0, None, -1, 64, 1, None, 0, None) == -1
+    assert lib.b2q_quant_gemv_pinned(0, None, 0, None, None, 0, None, 0, 64, 1, None, 0, None) == 0  # empty: no-op
+    assert lib.b2q_stage_pinned(None, 0, None, -1, 64, None) == -1
+    assert lib.b2q_stage_pinned(None, 0, None, 0, 64, None) == 0  # empty: no-op
+    assert lib.b2q_host_device_pointer(None, None) == -1
 
 
 def test_split_layout_is_kurns():
