@@ -1,10 +1,10 @@
 """TEST INFRASTRUCTURE ONLY -- the CPU oracle for the quantized decode path.
 
 This package restates, on the CPU, the reference's algorithm for the four ops (COMP's `quant_q8_0`, `quant_q8_K`,
-`q4_0_gemv`, `tq2_0_gemv`) and KURN's exact reference dot, plus the GEMVs of the two weight formats the product adds
-beyond the reference (ggml Q8_0 and IQ4_NL, against q8_0 activations). It is the checker, never the product: only `tests/`,
-`__graft_entry__.smoke()` and `bench.py`'s CPU-baseline / reference arm may import or run it. The product
-(`comp_b200`) never imports it and has no CPU path.
+`q4_0_gemv`, `tq2_0_gemv`) and KURN's exact reference dot, plus the GEMVs of the two weight formats the product
+adds beyond the reference (ggml Q8_0 and IQ4_NL, against q8_0 activations). It is the checker, never the product:
+only `tests/`, `__graft_entry__.smoke()` and `bench.py`'s CPU-baseline / reference arm may import or run it. The
+product (`comp_b200`) never imports it and has no CPU path.
 
   oracle.ref     numpy restatement (bit-exact quantizer bytes, exact int64 block dots, f64 reference dot in
                  KURN's order); also the seeded input generators.
