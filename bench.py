@@ -13,18 +13,31 @@ output; value = sum over layers / step time. Weights random-initialised with the
 N > 1 (torchrun, one process per GPU): every layer is row-sharded across the ranks (strong scaling: the same layers at
 every N); each rank runs its rows, then the output slices are all-gathered so every rank holds the full Y.
 
-End to end (the "e2e" key): the same layers through the public API with host buffers, every step -- pinned host x
-in, Y stored into pinned host memory by the kernels, a host stream synchronize (N = 1: b2q_quant_gemv_pinned per
-layer; N > 1: RowShardedGemv(x_host, out=y_host)); --e2e-api device uses device buffers with torch memcpys instead.
+Also in the line:
+  per_layer  every layer alone, launched back to back over rotating weight copies (>= 4x L2 of distinct weights),
+             event-timed on the launching stream (max over ranks): us per GEMV, GB/s, fraction of the HBM peak.
+  parity     N = 1: the first 512 rows of every layer against the C oracle (quantized bytes and int32 block dots
+             bit-exact, Y within 1e-5 of the exact reference), inside the CPU-baseline leg. N > 1: every rank's
+             gathered Y of every layer bit-identical to the unsharded GEMV of the full layer on its own GPU.
+  e2e        the same layers through the public API with host buffers, every step -- pinned host x in, Y stored into
+             pinned host memory by the kernels, a host stream synchronize (N = 1: b2q_quant_gemv_pinned per layer;
+             N > 1: RowShardedGemv(x_host, out=y_host)); --e2e-api device uses device buffers with torch memcpys.
+  e2e_dropin N = 1: COMP's own call sequence, host.quantize + host.gemv (the reference's signatures), x copied in
+             from pinned host memory and Y copied back every step.
+  clocks     NVML samples over a window of at least one second of steps that runs straight into the timed region
+             (the timed region itself is short), with the count of samples taken inside it.
 
---impl reference: the reference's CPU path (the C + OpenMP restatement of COMP's quantizers and KURN's reference dot,
-oracle/c/oracle.c, all host threads) on the same workload; rank 0 only.
+--impl reference: the reference's CPU path on the same workload, rank 0 only: the C + OpenMP restatement of COMP's
+quantizers and KURN's reference dot (oracle/c/oracle.c, all host cores) is the line's value; next to it COMP itself
+(baseline/_ref, installed by baseline/install_ref.sh) under TRITON_INTERPRET=1 on a row sample, extrapolated, and
+COMP's Triton kernels JIT-compiled on this B200 (best of the spec tune space) as the GPU bar.
 """
 
 import argparse
 import json
 import os
 import statistics
+import subprocess
 import sys
 import threading
 import time
@@ -53,6 +66,10 @@ BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18}  # ggml block 
 FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}
 METRIC = "weight-stream GB/s and us/GEMV (% of HBM peak) at 1/2/4/8 B200 vs host CPU ref"
 L2_BYTES = 126 * 2**20
+TOL = 1e-5  # KURN's relative-error rule (src/komp/verify.py:28)
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+# COMP's spec tune space per weight format (block_n, nb), mode dp4a, 4 warps (examples/*_gemv_triton.kurn)
+KOMP_TUNE = {"q4_0": [(32, 4), (32, 8), (64, 4), (64, 8)], "tq2_0": [(32, 1), (32, 2), (64, 1), (64, 2)]}
 
 
 def weight_bytes(fmt, n, k):
@@ -90,8 +107,24 @@ def profiled_traffic(kernel_tag):
     return None
 
 
+def select_layers(args):
+    layers_def = WORKLOADS[args.workload]
+    if args.layers:
+        keep = set(args.layers.split(","))
+        layers_def = [d for d in layers_def if d[3] in keep]
+    return layers_def
+
+
+def bench_config(workload, layers_def, m):
+    """The workload as both arms name it (the same dict, so the two lines compare)."""
+    return {"workload": workload, "layers": [f"{f} {n}x{k} ({nm})" for f, n, k, nm in layers_def], "m": m,
+            "l2": "inputs larger than L2: >= 4x the 126 MiB L2 of distinct weights per GPU per step (rotating "
+                  "copies where a GPU's share is smaller), no flush"}
+
+
 class ClockSampler:
-    """Polls NVML (SM clock, max SM clock, throttle reasons) on a thread while the timed region runs."""
+    """Polls NVML (SM clock, max SM clock, throttle reasons) on a thread; mark() brackets the timed region so the
+    summary can say how many samples fell inside it."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
                "hw_power_brake_slowdown": 0x80}
@@ -99,8 +132,10 @@ class ClockSampler:
     def __init__(self, dev, period=0.005):
         self.period = period
         self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.t_begin = self.t_end = None
         self._stop = threading.Event()
         self._t = None
+        self._t0 = None
         try:
             import pynvml
             import torch
@@ -120,7 +155,7 @@ class ClockSampler:
     def _poll(self):
         sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
         r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-        self.samples.append(sm)
+        self.samples.append((time.perf_counter(), sm))
         for name, bit in self.REASONS.items():
             if r & bit:
                 self.reasons.add(name)
@@ -133,7 +168,14 @@ class ClockSampler:
                 return
             time.sleep(self.period)
 
+    def mark(self, begin):
+        if begin:
+            self.t_begin = time.perf_counter()
+        else:
+            self.t_end = time.perf_counter()
+
     def __enter__(self):
+        self._t0 = time.perf_counter()
         if self.nv:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
@@ -151,8 +193,13 @@ class ClockSampler:
     def summary(self):
         if not self.nv:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        mhz = [s for _, s in self.samples]
+        timed = [s for t, s in self.samples if self.t_begin is not None and self.t_begin <= t <= (self.t_end or t)]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(mhz), "samples_in_timed_region": len(timed),
+                "sm_mhz_timed_region": statistics.median(timed) if timed else None,
+                "window_s": round(time.perf_counter() - self._t0, 3) if self._t0 else None,
+                "window": "steps run for >= 1 s straight into the timed region, then the timed region"}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -191,6 +238,11 @@ def make_x(k, m, seed):
     return rng.standard_normal((m, k)).astype(np.float32)
 
 
+def copies_for(nbytes):
+    """Rotating copies so that a loop over them streams >= 4x L2 of distinct weights."""
+    return 1 if nbytes >= 4 * L2_BYTES else -(-4 * L2_BYTES // max(1, nbytes))
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # CPU reference path (oracle/c/oracle.c) -- the reference arm and the cpu_baseline leg
 # ---------------------------------------------------------------------------------------------------------------
@@ -204,7 +256,7 @@ def cpu_reference_run(layers_np, steps, warmup):
 
     def one():
         for fmt, wq, ws, x, k in layers_np:
-            if fmt in ("q4_0", "q8_0"):
+            if fmt in ("q4_0", "q8_0", "iq4_nl"):
                 xq, xd = native.quant_q8_0(x)
             else:
                 xq, xd, _ = native.quant_q8_K(x)
@@ -218,53 +270,214 @@ def cpu_reference_run(layers_np, steps, warmup):
     return (time.perf_counter() - t0) / steps, threads
 
 
-def cpu_layers(workload, m, budget_rows=None):
+def cpu_layers(layers_def, m, budget_rows=None):
     """Host copies of the workload's layers for the CPU path; budget_rows limits each layer to its first rows."""
-    import torch
+    from oracle import ref
 
     out, meta = [], []
-    for i, (fmt, n, k, name) in enumerate(WORKLOADS[workload]):
+    for i, (fmt, n, k, name) in enumerate(layers_def):
         rows = n if budget_rows is None else min(n, budget_rows)
         rng = np.random.default_rng(100 + i)
-        from oracle import ref
-
         wq, ws = ref.random_split(fmt, rng, rows, k)
         out.append((fmt, wq, ws, make_x(k, m, 200 + i), k))
         meta.append((fmt, rows, k))
-    del torch
     return out, meta
 
 
-def run_reference_arm(args, rank):
+def _komp_env():
+    env = dict(os.environ)
+    env["KOMP_PATCHES"] = os.path.join(REF_DIR, "patches")
+    env.setdefault("KOMP_CACHE", os.path.join(ROOT, "gpurun_out", "komp_cache"))
+    env["PYTHONPATH"] = REF_DIR + os.pathsep + env.get("PYTHONPATH", "")
+    return env
+
+
+def _run_komp_worker(kind, args, timeout, extra=()):
+    """Runs `bench.py --komp-worker kind` (the reference's own code from baseline/_ref) in a subprocess, because
+    TRITON_INTERPRET must be set (interpreter) or unset (compiled kernels) before triton is imported. Returns the
+    worker's JSON dict, or {"unavailable": reason}."""
+    if not os.path.exists(os.path.join(REF_DIR, "komp", "host.py")) or \
+            not os.path.exists(os.path.join(REF_DIR, "patches", "0001-language-extra-kurn.patch")):
+        return {"unavailable": "the reference is not installed under baseline/_ref (run baseline/install_ref.sh)"}
+    env = _komp_env()
+    if kind == "interp":
+        env["TRITON_INTERPRET"] = "1"
+    else:
+        env.pop("TRITON_INTERPRET", None)
+    cmd = [sys.executable, os.path.abspath(__file__), "--komp-worker", kind, "--workload", args.workload,
+           "--m", str(args.m), *extra]
+    if args.layers:
+        cmd += ["--layers", args.layers]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env, cwd=ROOT)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"komp {kind} worker did not finish within {timeout} s"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            return json.loads(line)
+    tail = (r.stderr.strip().splitlines() or ["no output"])[-1]
+    return {"unavailable": f"komp {kind} worker exited {r.returncode}: {tail[:300]}"}
+
+
+def komp_interp_worker(args):
+    """COMP itself on the host cores: host.quantize + host.gemv (mode 1, the interpreter's dp4a) under
+    TRITON_INTERPRET=1 on the first rows of each layer; the GEMV time is scaled to the full layer (each row is an
+    independent program of the same cost), the quantizer (one pass over K) is timed whole."""
+    import torch
+    from komp import host as khost
+
+    from oracle import ref  # the reference arm's data generator (seeded split planes)
+
+    rows = args.komp_rows
+    m = args.m
+    # one small call first: module imports and the interpreter's first-use costs stay out of the timing
+    wq, ws = ref.random_split("q4_0", np.random.default_rng(0), 4, 64)
+    xq, xd = khost.quantize("q4_0", torch.from_numpy(make_x(64, 1, 0)))
+    khost.gemv("q4_0", torch.from_numpy(wq), torch.from_numpy(ws), xq, xd, 4, 64, mode=1)
+    per = []
+    step_s = 0.0
+    for i, (fmt, n, k, name) in enumerate(select_layers(args)):
+        r = min(n, rows)
+        wq, ws = ref.random_split(fmt, np.random.default_rng(100 + i), r, k)
+        x = torch.from_numpy(make_x(k, m, 200 + i))
+        t0 = time.perf_counter()
+        xq, xd = khost.quantize(fmt, x)
+        t1 = time.perf_counter()
+        khost.gemv(fmt, torch.from_numpy(wq), torch.from_numpy(ws), xq, xd, r, k, mode=1)
+        t2 = time.perf_counter()
+        full = (t1 - t0) + (t2 - t1) * n / r
+        step_s += full
+        per.append({"name": name, "rows_run": r, "quant_s": round(t1 - t0, 4), "gemv_s": round(t2 - t1, 4),
+                    "full_layer_s_extrapolated": round(full, 3)})
+    total = sum(algo_bytes(f, n, k, m) for f, n, k, _ in select_layers(args))
+    print(json.dumps({"value": total / step_s / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
+                      "extrapolated": True, "step_s_extrapolated": round(step_s, 2), "per_layer": per,
+                      "torch_threads": torch.get_num_threads(),
+                      "sample": f"COMP (baseline/_ref) host.quantize + host.gemv mode 1 under TRITON_INTERPRET=1 on the "
+                                f"first {rows} rows of each layer, GEMV time scaled by N/rows; the interpreter runs "
+                                f"the grid's programs one after another in one Python thread"}), flush=True)
+
+
+def komp_triton_worker(args):
+    """COMP's Triton kernels JIT-compiled for this B200 (mode 2, dp4a in inline PTX): per layer, the best of the spec
+    tune space, quantize + GEMV captured in a CUDA graph per rotating weight copy and replayed, event-timed. Only the
+    reference's code runs here (its outputs are compared with this library's in tests/test_gpu_vs_komp.py)."""
+    import torch
+    from komp import host as khost
+
+    dev = torch.device("cuda", args.device)
+    torch.cuda.set_device(dev)
+    m = args.m
+    peak, _ = peaks()
+    per, step_us, notes = [], 0.0, []
+    for i, (fmt, n, k, name) in enumerate(select_layers(args)):
+        if fmt not in KOMP_TUNE:
+            per.append({"name": name, "unavailable": f"COMP has no {fmt} kernel"})
+            continue
+        wq0, ws0 = make_layer_gpu(fmt, n, k, 100 + i, dev)
+        copies = copies_for(weight_bytes(fmt, n, k))
+        ws_list = [(wq0, ws0)] + [(wq0.clone(), ws0.clone()) for _ in range(copies - 1)]
+        x = torch.from_numpy(make_x(k, m, 200 + i)).to(dev)
+        best = None
+        for block_n, nb in KOMP_TUNE[fmt]:
+            def call(c, block_n=block_n, nb=nb):
+                xq, xd = khost.quantize(fmt, x)
+                khost.gemv(fmt, ws_list[c][0], ws_list[c][1], xq, xd, n, k, block_n=block_n, nb=nb, mode=2)
+
+            try:
+                for c in range(copies):
+                    call(c)  # compile + warm
+                torch.cuda.synchronize()
+                graphs = []
+                s = torch.cuda.Stream(dev)
+                s.wait_stream(torch.cuda.current_stream(dev))
+                try:
+                    for c in range(copies):
+                        g = torch.cuda.CUDAGraph()
+                        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+                            call(c)
+                        graphs.append(g)
+                    run = lambda r: graphs[r % copies].replay()  # noqa: E731
+                    how = "CUDA graph replays"
+                except Exception as e:  # noqa: BLE001 -- fall back to eager launches
+                    graphs = []
+                    run = lambda r: call(r % copies)  # noqa: E731
+                    how = f"eager launches (graph capture failed: {str(e)[:80]})"
+                torch.cuda.current_stream(dev).wait_stream(s)
+                reps = max(20, 4 * copies)
+                for r in range(2 * copies):
+                    run(r)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for r in range(reps):
+                    run(r)
+                e1.record()
+                e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                del graphs
+            except Exception as e:  # noqa: BLE001 -- a config that does not compile is skipped, and said so
+                notes.append(f"{name} block_n={block_n} nb={nb}: {str(e).splitlines()[0][:120]}")
+                continue
+            if best is None or us < best[0]:
+                best = (us, block_n, nb, how)
+        del ws_list, wq0, ws0
+        torch.cuda.empty_cache()
+        if best is None:
+            per.append({"name": name, "unavailable": "no tune config ran"})
+            continue
+        us, block_n, nb, how = best
+        step_us += us
+        gbs = algo_bytes(fmt, n, k, m) / (us * 1e-6) / 1e9
+        per.append({"name": name, "us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                    "best": {"block_n": block_n, "nb": nb, "num_warps": 4, "mode": "dp4a (2)"}, "timing": how})
+    total = sum(algo_bytes(f, n, k, m) for f, n, k, _ in select_layers(args) if f in KOMP_TUNE)
+    out = {"value": round(total / (step_us * 1e-6) / 1e9, 2) if step_us else None, "unit": "GB/s",
+           "us_per_step": round(step_us, 2), "per_layer": per,
+           "what": "COMP's Triton kernels (baseline/_ref, triton " + __import__("triton").__version__ +
+                   ") JIT-compiled on this B200, mode 2; per layer the best of the spec tune space; quantize + GEMV "
+                   "per layer, graph-replayed over rotating weight copies (>= 4x L2)"}
+    if notes:
+        out["skipped_configs"] = notes
+    print(json.dumps(out), flush=True)
+
+
+def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     m = args.m
-    full = WORKLOADS[args.workload]
-    full_bytes = sum(algo_bytes(f, n, k, m) for f, n, k, _ in full)
+    layers_def = select_layers(args)
+    full_bytes = sum(algo_bytes(f, n, k, m) for f, n, k, _ in layers_def)
     # bound the run: a step is a row sample sized so warmup + steps stay within ~90 s of host time
-    probe_layers, _ = cpu_layers(args.workload, m, budget_rows=512)
+    probe_layers, _ = cpu_layers(layers_def, m, budget_rows=512)
     probe_s, _ = cpu_reference_run(probe_layers, 1, 1)
-    probe_bytes = sum(algo_bytes(f, 512 if n > 512 else n, k, m) for f, n, k, _ in full)
+    probe_bytes = sum(algo_bytes(f, min(n, 512), k, m) for f, n, k, _ in layers_def)
     est_full = probe_s * full_bytes / probe_bytes
     budget = 90.0 / max(1, args.steps + args.warmup)
     frac = min(1.0, budget / est_full) if est_full > 0 else 1.0
-    rows = max(64, int(max(n for _, n, _, _ in full) * frac))
-    layers, meta = cpu_layers(args.workload, m, budget_rows=rows)
+    rows = max(64, int(max(n for _, n, _, _ in layers_def) * frac))
+    layers, meta = cpu_layers(layers_def, m, budget_rows=rows)
     step_bytes = sum(algo_bytes(f, r, k, m) for f, r, k in meta)
     sec, threads = cpu_reference_run(layers, args.steps, args.warmup)
     gbs = step_bytes / sec / 1e9
-    full_rows = all(r == n for (f, r, k), (_, n, _, _) in zip(meta, full))
+    full_rows = all(r == n for (f, r, k), (_, n, _, _) in zip(meta, layers_def))
     what = "full layers" if full_rows else f"first {rows} rows of each layer"
     sample = (f"{what} ({', '.join(f'{f} {r}x{k}' for f, r, k in meta)}), M={m}; quantize + GEMV + f64 reference dot "
-              f"per layer, each step")
+              f"per layer, each step (oracle/c/oracle.c, C + OpenMP, one thread per core this process may use)")
+    interp = {"unavailable": "skipped (--no-komp)"} if args.no_komp else \
+        _run_komp_worker("interp", args, timeout=300, extra=["--komp-rows", str(args.komp_rows)])
+    triton_gpu = {"unavailable": "skipped (--no-komp)"} if args.no_komp else \
+        _run_komp_worker("triton", args, timeout=600, extra=["--device", os.environ.get("LOCAL_RANK", "0")])
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3 * full_bytes / step_bytes, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8/int32 dots, f64 sum",
         "data": "synthetic (BASELINE distributions, seeded)",
-        "config": {"workload": args.workload, "layers": [f"{f} {n}x{k}" for f, n, k, _ in full], "m": m,
-                   "parallelism": "host cores"},
+        "config": bench_config(args.workload, layers_def, m),
+        "setup": {"parallelism": "host cores, rank 0 only", "world": world},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "reference_interpreter": interp,
+        "triton_b200": triton_gpu,
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -282,9 +495,11 @@ def main():
     ap.add_argument("--workload", default="config4", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=1, help="activation columns")
-    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps)")
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end legs (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end legs (profiling runs)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip per-layer timing, parity and the clock window (profiling runs)")
     ap.add_argument("--layers", default=None, help="comma-separated layer names of the workload to keep (profiling)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="N > 1 output all-gather")
     ap.add_argument("--pdl", default="on", choices=["on", "off"], help="programmatic dependent launch of the GEMVs")
@@ -292,16 +507,26 @@ def main():
                     help="end-to-end leg: pinned host x in and Y stored into pinned host memory by the kernels "
                          "(N = 1: b2q_quant_gemv_pinned, N > 1: RowShardedGemv(x_host, out=y_host)), or device "
                          "buffers with torch memcpys around each call")
+    ap.add_argument("--no-komp", action="store_true", help="reference arm: skip COMP's interpreter and Triton legs")
+    ap.add_argument("--komp-rows", type=int, default=16, help="reference arm: rows per layer run by the interpreter")
+    ap.add_argument("--komp-worker", default=None, choices=["interp", "triton"], help=argparse.SUPPRESS)
+    ap.add_argument("--device", type=int, default=0, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.layers and not select_layers(args):
+        ap.error(f"--layers {args.layers}: no such layer in {args.workload}")
+    if args.komp_worker == "interp":
+        return komp_interp_worker(args)
+    if args.komp_worker == "triton":
+        return komp_triton_worker(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        run_reference_arm(args, rank)
+        run_reference_arm(args, rank, world)
         return
 
     import datetime
@@ -310,7 +535,7 @@ def main():
     import torch.distributed as dist
 
     from comp_b200 import _lib, host
-    from comp_b200.dist import RowShardedGemv, partition
+    from comp_b200.dist import RowShardedGemv, partition, slice_rows
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -320,17 +545,13 @@ def main():
     if args.pdl == "off":
         _lib.call("b2q_set_pipeline", 4, 0)
     m = args.m
-    layers_def = WORKLOADS[args.workload]
-    if args.layers:
-        keep = set(args.layers.split(","))
-        layers_def = [d for d in layers_def if d[3] in keep]
-        if not layers_def:
-            ap.error(f"--layers {args.layers}: no such layer in {args.workload}")
+    layers_def = select_layers(args)
     total_bytes = sum(algo_bytes(f, n, k, m) for f, n, k, _ in layers_def)
     weights_total = sum(weight_bytes(f, n, k) for f, n, k, _ in layers_def)
     # every step must stream its weights from HBM: keep >= 4x L2 of distinct weights per GPU, rotating copies
     per_gpu = max(1, weights_total // world)
-    copies = 1 if per_gpu >= 4 * L2_BYTES else -(-4 * L2_BYTES // per_gpu)
+    copies = copies_for(per_gpu)
+    peak, peak_kind = peaks()
 
     class Layer:
         pass
@@ -348,30 +569,36 @@ def main():
         L.wsb = host.workspace_size(fmt, n, k, m) if world == 1 else 0
         L.work = torch.empty(max(16, L.wsb), dtype=torch.uint8, device=dev)
         if world > 1:
-            L.objs = [RowShardedGemv(fmt, wq, ws, n, k, exchange=args.exchange) for wq, ws in L.w]
+            L.obj = RowShardedGemv(fmt, L.w[0][0], L.w[0][1], n, k, exchange=args.exchange)
         layers.append(L)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     dominant = max(range(len(layers)), key=lambda i: weight_bytes(layers[i].fmt, layers[i].n, layers[i].k))
-    exchange_name = None if world == 1 else layers[0].objs[0].exchange
+    exchange_name = None if world == 1 else layers[0].obj.exchange
 
-    def launch(L, c):
-        """N = 1: fused quantize + GEMV straight through the C ABI (tall-K layers: split-K, two launches)."""
-        wq, ws = L.w[c]
+    def launch(L, wq, ws, y=None):
+        """N = 1: fused quantize + GEMV straight through the C ABI."""
+        y = L.y if y is None else y
         rc = lib.b2q_quant_gemv_ws(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x.data_ptr(), L.x.stride(0),
-                                   None, None, L.y.data_ptr(), L.rows, L.k, m, L.work.data_ptr(), L.wsb, sptr)
+                                   None, None, y.data_ptr(), L.rows, L.k, m, L.work.data_ptr(), L.wsb, sptr)
         if rc != 0:
             raise RuntimeError(_lib.last_error())
+
+    def sharded(L, wq, ws):
+        """N > 1: the layer's fused GEMV + all-gather on the given weight slice (one RowShardedGemv per layer, so one
+        set of receive buffers; its weights are swapped per rotating copy)."""
+        L.obj.wq, L.obj.ws = wq, ws
+        return L.obj(L.x)
 
     def step(c, ev=None):
         for i, L in enumerate(layers):
             if ev is not None and i == dominant:
                 ev[0].record(stream)
             if world == 1:
-                launch(L, c)
+                launch(L, *L.w[c])
             else:
-                L.objs[c](L.x)
+                sharded(L, *L.w[c])
             if ev is not None and i == dominant:
                 ev[1].record(stream)
 
@@ -379,46 +606,74 @@ def main():
         step(w % copies)
     torch.cuda.synchronize()
 
+    def capture(fn, count):
+        """count CUDA graphs, graph j = fn(j), captured on a side stream."""
+        gs = []
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        for j in range(count):
+            gs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.stream(cs), torch.cuda.graph(gs[-1], stream=cs):
+                fn(j)
+        stream.wait_stream(cs)
+        return gs
+
     # N > 1: the step is captured once per weight copy as a CUDA graph (three fused GEMV + all-gather launches, or
     # GEMV + NCCL all-gather), so host launch time does not bound the multi-GPU step
     graphs = []
     launches_per_graph = 0
     if world > 1:
-        cs = torch.cuda.Stream(dev)
-        cs.wait_stream(stream)
-        for c in range(copies):
-            graphs.append(torch.cuda.CUDAGraph())
-            n0 = _lib.launch_count()
-            with torch.cuda.stream(cs), torch.cuda.graph(graphs[-1], stream=cs):
-                step(c)
-            launches_per_graph = _lib.launch_count() - n0
-        stream.wait_stream(cs)
+        n0 = _lib.launch_count()
+        graphs = capture(step, copies)
+        launches_per_graph = (_lib.launch_count() - n0) // copies
         for c in range(copies):
             graphs[c].replay()
         torch.cuda.synchronize()
         dist.barrier()
 
-    # ---- device-timed region: inputs resident in HBM ----
+    def run_step(s, ev=None):
+        if world == 1:
+            step(s % copies, ev)
+        else:
+            graphs[s % copies].replay()
+
+    # ---- device-timed region: inputs resident in HBM; NVML sampled from >= 1 s of steps before it through it ----
     dom_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(args.steps if world == 1 else 0)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = _lib.launch_count()
+    # the window's step count comes from a short timing, max over ranks, so every rank makes the same calls
+    n_soak = 0
+    if not args.no_extras:
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        for s in range(20):
+            run_step(s)
+        p1.record(stream)
+        p1.synchronize()
+        tp = torch.tensor([p0.elapsed_time(p1) / 20], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+        n_soak = int(min(200000, -(-1000.0 // max(1e-3, float(tp.item())))))
     with ClockSampler(dev) as clocks:
+        for s in range(n_soak):
+            run_step(s)
+            if s % 64 == 63:
+                stream.synchronize()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+        launches0 = _lib.launch_count()
+        clocks.mark(True)
         start.record(stream)
         for s in range(args.steps):
-            if world == 1:
-                step(s % copies, dom_events[s])
-            else:
-                graphs[s % copies].replay()
+            run_step(s, dom_events[s] if world == 1 else None)
         end.record(stream)
         end.synchronize()
         torch.cuda.synchronize()
+        clocks.mark(False)
+        launches = _lib.launch_count() - launches0 if world == 1 else launches_per_graph * args.steps
     if world > 1:
         dist.barrier()
-    launches = _lib.launch_count() - launches0 if world == 1 else launches_per_graph * args.steps
     ms = start.elapsed_time(end)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -426,51 +681,95 @@ def main():
     ms = float(t.item())
     sec = ms / 1e3
     value = total_bytes * args.steps / sec / 1e9
+    if world > 1:
+        for L in layers:
+            if L.obj.status_code() != 0:
+                raise RuntimeError(f"rank {rank}: fused all-gather poll timed out on {L.name} ({L.obj.status_code()})")
+
+    # ---- every layer alone, back to back over rotating copies (>= 4x L2), event-timed, max over ranks ----
+    per_layer = []
+    dom_alone_ms = None
+    if not args.no_extras:
+        for i, L in enumerate(layers):
+            nc = copies_for(weight_bytes(L.fmt, slice_rows(L.n, world), L.k))  # the same on every rank
+            ws_list = [L.w[c % copies] if c < copies else (L.w[0][0].clone(), L.w[0][1].clone()) for c in range(nc)]
+            if world == 1:
+                run = lambda r, L=L, ws_list=ws_list, nc=nc: launch(L, *ws_list[r % nc])  # noqa: E731
+                lg = None
+            else:
+                lg = capture(lambda j, L=L, ws_list=ws_list: sharded(L, *ws_list[j]), nc)
+                run = lambda r, lg=lg, nc=nc: lg[r % nc].replay()  # noqa: E731
+            reps = max(4 * nc, min(400, max(50, args.steps)))
+            for r in range(2 * nc):
+                run(r)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for r in range(reps):
+                run(r)
+            e1.record(stream)
+            e1.synchronize()
+            td = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(td, op=dist.ReduceOp.MAX)
+            us = float(td.item()) * 1e3
+            gbs = algo_bytes(L.fmt, L.n, L.k, m) / (us * 1e-6) / 1e9
+            per_layer.append({"name": L.name, "shape": f"{L.fmt} {L.n}x{L.k}", "rows_per_gpu": L.rows,
+                              "us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / world / peak, 4),
+                              "copies": nc, "launches_timed": reps})
+            if i == dominant:
+                dom_alone_ms = us / 1e3
+            if lg is not None:
+                lg.clear()
+            del ws_list, lg
+        torch.cuda.empty_cache()
+        if world > 1:
+            for L in layers:
+                L.obj.wq, L.obj.ws = L.w[0]
+
     dom = layers[dominant]
     if world == 1:
         dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_events)
         dom_note = "mean CUDA-event duration of its launches inside the timed steps"
+    elif dom_alone_ms is not None:
+        dom_ms = dom_alone_ms
+        dom_note = "dominant layer alone (graph replays over rotating copies after the timed steps), max over ranks"
     else:
-        # the dominant layer alone (its fused GEMV + all-gather), graph-replayed, event-timed on its stream
-        dg = []
-        cs2 = torch.cuda.Stream(dev)
-        cs2.wait_stream(stream)
-        for c in range(copies):
-            dg.append(torch.cuda.CUDAGraph())
-            with torch.cuda.stream(cs2), torch.cuda.graph(dg[-1], stream=cs2):
-                dom.objs[c](dom.x)
-        stream.wait_stream(cs2)
-        reps = max(20, min(400, args.steps))
-        for r in range(4):
-            dg[r % copies].replay()
-        torch.cuda.synchronize()
-        dist.barrier()
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record(stream)
-        for r in range(reps):
-            dg[r % copies].replay()
-        d1.record(stream)
-        d1.synchronize()
-        td = torch.tensor([d0.elapsed_time(d1) / reps], dtype=torch.float64, device=dev)
-        dist.all_reduce(td, op=dist.ReduceOp.MAX)
-        dom_ms = float(td.item())
-        dom_note = f"dominant layer alone, {reps} graph replays after the timed steps, max over ranks"
-        dg.clear()
-        del dg
-        for L in layers:
-            for o in L.objs:
-                if o.status_code() != 0:
-                    raise RuntimeError(f"rank {rank}: all-gather barrier timed out ({o.status_code()})")
+        dom_ms = ms / args.steps
+        dom_note = "whole step (per-layer timing skipped)"
     dom_bytes = algo_bytes(dom.fmt, dom.rows, dom.k, m)
-    peak, peak_kind = peaks()
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     tag = f"{dom.fmt}_{dom.rows}x{dom.k}"
     traffic = profiled_traffic(tag)
 
+    # ---- N > 1 parity: every rank's gathered Y == the unsharded GEMV of the full layer on its own GPU ----
+    parity = None
+    if world > 1 and not args.no_extras:
+        mism, checked = 0, 0
+        for i, L in enumerate(layers):
+            wq_f, ws_f = make_layer_gpu(L.fmt, L.n, L.k, 100 + i, dev)  # copy 0, all rows
+            want = host.quant_gemv(L.fmt, wq_f, ws_f, L.x, L.n, L.k, split=False)
+            got = sharded(L, *L.w[0]).clone()
+            torch.cuda.synchronize()
+            mism += int((got.view(torch.int32) != want.view(torch.int32)).sum().item())
+            checked += got.numel()
+            del wq_f, ws_f, want, got
+        torch.cuda.empty_cache()
+        bad = torch.tensor([mism, 0 if all(L.obj.status_code() == 0 for L in layers) else 1], dtype=torch.int64,
+                           device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+        parity = {"bitexact": int(bad[0].item()) == 0 and int(bad[1].item()) == 0,
+                  "mismatched_values": int(bad[0].item()), "ranks_with_timeouts": int(bad[1].item()),
+                  "values_checked_per_rank": checked,
+                  "check": "every layer, after the timed region: the full Y gathered on every rank (its own rows and "
+                           "the rows received from its peers) bit-identical to the unsharded fused GEMV of the full "
+                           "layer on the same GPU (rows are independent: src/komp/kernels.py:55-56, 94)"}
+
     # ---- end to end through the public API: pinned host x -> device, quantize + gemv, Y -> host ----
     e2e_steps = 0 if args.no_e2e else (args.e2e_steps or args.steps)
     y_host = [torch.empty((m, L.n), dtype=torch.float32).pin_memory() for L in layers]
-
     y_dev = [torch.empty((m, L.n), dtype=torch.float32, device=dev) for L in layers] if world == 1 else None
     pinned = args.e2e_api == "pinned"
     if pinned and world == 1:
@@ -483,7 +782,7 @@ def main():
         # the results
         for i, L in enumerate(layers):
             if world > 1:
-                L.objs[0](L.x_host, out=y_host[i])
+                L.obj(L.x_host, out=y_host[i])
                 continue
             wq, ws = L.w[0]
             rc = lib.b2q_quant_gemv_pinned(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), L.x_host.data_ptr(),
@@ -493,9 +792,7 @@ def main():
                 raise RuntimeError(_lib.last_error())
         stream.synchronize()  # the step's results are read on the host
 
-    def e2e_step():
-        if pinned:
-            return e2e_step_pinned()
+    def e2e_step_device():
         # every step: the layers' inputs from pinned host memory, the GEMVs back to back through the public API (so
         # each one's weight stream can start while the previous one finishes), every layer's output back to pinned
         # host memory, then the host waits for all of it
@@ -507,28 +804,40 @@ def main():
                 ys.append(host.quant_gemv(L.fmt, wq, ws, xs[i], L.n, L.k, out=y_dev[i]))
             else:
                 # the fused exchange reuses its output buffer on the layer's next call
-                ys.append(L.objs[0](xs[i]) if i + 1 == len(layers) else L.objs[0](xs[i]).clone())
+                ys.append(L.obj(xs[i]) if i + 1 == len(layers) else L.obj(xs[i]).clone())
         for i, y in enumerate(ys):
             y_host[i].copy_(y, non_blocking=True)
         stream.synchronize()  # the step's results are read on the host
 
-    e2e_gbs = None
-    if e2e_steps:
+    def e2e_step_dropin():
+        # COMP's call sequence with the reference's signatures (src/komp/host.py:63-85): x copied in from pinned host
+        # memory, host.quantize, host.gemv (dp4a), Y copied back to pinned host memory; the host waits every step
+        for i, L in enumerate(layers):
+            x = L.x_host.to(dev, non_blocking=True)
+            xq, xd = host.quantize(L.fmt, x)
+            y, _ = host.gemv(L.fmt, L.w[0][0], L.w[0][1], xq, xd, L.n, L.k, mode=host.MODES["dp4a"])
+            y_host[i].copy_(y, non_blocking=True)
+        stream.synchronize()
+
+    def time_e2e(fn, steps):
         for _ in range(3):
-            e2e_step()
+            fn()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
+        for _ in range(steps):
+            fn()
         e1.record(stream)
         e1.synchronize()
         te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_gbs = round(total_bytes * e2e_steps / (float(te.item()) / 1e3) / 1e9, 3)
+        return round(total_bytes * steps / (float(te.item()) / 1e3) / 1e9, 3)
+
+    e2e_gbs = time_e2e(e2e_step_pinned if pinned else e2e_step_device, e2e_steps) if e2e_steps else None
+    dropin_gbs = time_e2e(e2e_step_dropin, e2e_steps) if (e2e_steps and world == 1) else None
     h2d = sum(L.x_host.numel() * 4 for L in layers)
     d2h = sum(L.n * m * 4 for L in layers)
     # graphs that hold NCCL calls must be released before the process group is destroyed
@@ -537,19 +846,47 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         for L in layers:
-            for o in L.objs:
-                o.close()
+            L.obj.close()
 
-    # ---- CPU baseline (rank 0, N = 1): bounded sample of the same workload ----
+    # ---- CPU baseline (rank 0, N = 1): bounded sample of the same layers; the oracle also checks the GPU here ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import native, ref
+
         rows = 8192
-        cl, meta = cpu_layers(args.workload, m, budget_rows=rows)
+        cl, meta = [], []
+        for L in layers:
+            r = min(rows, L.n)
+            cl.append((L.fmt, L.w[0][0][:r].cpu().numpy(), L.w[0][1][:r].cpu().numpy(), L.x_host.numpy(), L.k))
+            meta.append((L.fmt, r, L.k))
         csec, threads = cpu_reference_run(cl, 3, 1)
         cbytes = sum(algo_bytes(f, r, k, m) for f, r, k in meta)
         cpu = {"value": round(cbytes / csec / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"first {rows} rows of each layer, M={m}, 3 steps of quantize + GEMV + f64 reference dot "
-                         f"(oracle/c/oracle.c, OpenMP)"}
+               "sample": f"first {rows} rows of each layer (the GPU's weights and activations), M={m}, 3 steps of "
+                        f"quantize + GEMV + f64 reference dot (oracle/c/oracle.c, OpenMP)"}
+        # parity at N = 1: the first 512 rows of every layer, the bench's own fused launch against the oracle
+        checks = []
+        for L, (fmt, wq, ws, x, k) in zip(layers, cl):
+            r = min(512, L.n)
+            launch(L, *L.w[0])
+            xq, xd = host.quantize(fmt, L.x)
+            _, s = host.gemv(fmt, L.w[0][0][:r], L.w[0][1][:r], xq, xd, r, k, mode=2, store_s=True)
+            y = L.y[:, :r].cpu().numpy()
+            if fmt in ("q4_0", "q8_0", "iq4_nl"):
+                oq, od = native.quant_q8_0(x)
+            else:
+                oq, od, _ = native.quant_q8_K(x)
+            ry, rs = native.gemv(fmt, wq[:r], ws[:r], oq, od, k, want_s=True)
+            q_ok = bool(np.array_equal(xq.cpu().numpy(), oq) and
+                        np.array_equal(xd.cpu().numpy().view(np.uint32), od.view(np.uint32)))
+            s_ok = bool(np.array_equal(s.cpu().numpy(), rs))
+            err = ref.relerr(y, ry)
+            checks.append({"name": L.name, "rows": r, "quant_bytes": q_ok, "int32_block_dots": s_ok,
+                           "relerr": err, "ok": q_ok and s_ok and err <= TOL})
+        parity = {"bitexact": all(c["quant_bytes"] and c["int32_block_dots"] for c in checks),
+                  "ok": all(c["ok"] for c in checks), "layers": checks,
+                  "check": "first 512 rows of every layer against the C oracle (oracle/c/oracle.c): quantized bytes "
+                           "and int32 block dots bit-exact, the bench's fused Y within 1e-5 of the exact reference"}
 
     # the dominant layer runs as quantizer + tensor-core GEMM when it has 8+ columns and a workspace for them
     L_tc = world == 1 and m >= 8 and getattr(layers[dominant], "wsb", 0) > 0
@@ -560,21 +897,23 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 dp4a dots, f32 scale+sum",
             "data": "synthetic (BASELINE distributions, seeded, random-init weights)",
-            "config": {"workload": args.workload, "layers": [f"{f} {n}x{k} ({nm})" for f, n, k, nm in layers_def],
-                       "m": m, "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
-                       "exchange": {None: None, "p2p": "fused all-gather: (value, flag) peer stores from the GEMV epilogue",
-                                    "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
-                       "graph": world > 1, "pdl": args.pdl,
-                       "l2": f"weights {per_gpu / 2**20:.0f} MiB per GPU x {copies} rotating copies >= 4x L2 "
-                             f"(no flush needed)"},
+            "config": bench_config(args.workload, layers_def, m),
+            "setup": {"parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+                      "exchange": {None: None,
+                                   "p2p": "fused all-gather: 64-bit (flag, value) peer stores from the GEMV epilogue",
+                                   "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
+                      "graph": world > 1, "pdl": args.pdl,
+                      "weights_per_gpu_mib": round(per_gpu / 2**20), "rotating_copies": copies},
             "us_per_gemv": round(ms * 1e3 / args.steps / len(layers), 3),
             "hbm_frac": round(value / world / peak, 4),
+            "per_layer": per_layer,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": (f"quantizer + tcgen05 GEMM {tag} (2 launches, timed together)" if L_tc else
                                     f"gemv {tag} (quant prologue fused{', all-gather fused' if world > 1 else ''})"),
                          "timing": dom_note, "peak_source": f"{peak_kind} hbm_gbs",
                          "us_per_launch": round(dom_ms * 1e3, 3), "algorithmic_bytes_per_launch": dom_bytes},
+            "parity": parity,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps,
@@ -584,6 +923,11 @@ def main():
                     if world == 1 else f"comp_b200.dist.RowShardedGemv ({exchange_name}" +
                     ("; pinned host x in, Y stored into pinned host memory)" if pinned else
                      "; torch memcpy of x in, Y out)")},
+            "e2e_dropin": None if dropin_gbs is None else {
+                "value": dropin_gbs, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps,
+                "api": "comp_b200.host.quantize + comp_b200.host.gemv(mode=dp4a), COMP's signatures "
+                       "(src/komp/host.py:63-85); torch memcpy of x in from pinned memory, Y out; host sync every step"},
             "gpu_launches": launches,
             "clocks": cs,
         }

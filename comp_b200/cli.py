@@ -3,7 +3,9 @@
     python -m comp_b200 check  SPEC [k=v ...]   validate a `target triton` spec (and its tune space)
     python -m comp_b200 verify SPEC [k=v ...]   every config of the spec on the GPU vs exact references
     python -m comp_b200 verify --all            the full GPU self-check set (dp4a, both GEMVs, both variants)
-    python -m comp_b200 verify --all --json     the same as JSON lines, each GEMV also timed (us, GB/s, HBM fraction)
+    python -m comp_b200 verify --all --json [--hbm-gbs G]
+                                                the same as JSON lines, each GEMV also timed (us, GB/s, and the
+                                                fraction of G, or of $COMP_B200_HBM_GBS, when one is given)
 
 `kurn check|verify SPEC` routes here for specs with `target triton` through comp_b200.kurn_ext. COMP's `gen` and
 `mix` (PTX/SASS generation and inspection) have no counterpart: this backend ships its own compiled library.
@@ -48,7 +50,13 @@ def cmd_verify(args):
     from . import verify
 
     if "--all" in args:
-        return 1 if verify.run_all(as_json="--json" in args) else 0
+        peak = args[args.index("--hbm-gbs") + 1] if "--hbm-gbs" in args[:-1] else None
+        try:
+            peak = verify.hbm_peak(peak)
+        except ValueError as e:
+            print(f"comp_b200 verify: {e}", file=sys.stderr)
+            return 2
+        return 1 if verify.run_all(as_json="--json" in args, peak=peak) else 0
     try:
         spec, base, tune = _spec(args)
         spec.resolve(base)
@@ -82,7 +90,7 @@ def main(argv=None):
 
 
 def spec_command(cmd, argv):
-    """Entry for kurn.hooks.TARGET_BACKENDS["triton"] (the role of komp.cli.spec_command, src/komp/cli.py:274-279)."""
+    """Entry for kurn.hooks.TARGET_BACKENDS["triton"] (the role of komp.cli.spec_command, src/komp/cli.py:195-200)."""
     if cmd not in ("check", "verify"):
         print(f"kurn {cmd}: not available for target triton on comp_b200 (supports check, verify)", file=sys.stderr)
         return 2

@@ -417,8 +417,8 @@ struct LaunchArgs {
   int64_t ldy;
   int64_t row0;
   int32_t* s;
-  uint2* const* rx_peers;
-  uint2* rx;
+  unsigned long long* const* rx_peers;
+  unsigned long long* rx;
   int64_t rx_stride;
   unsigned long long* done;
   int32_t* status;
@@ -785,7 +785,7 @@ int b2q_gemv_allgather(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* 
   a.fmt = fmt;
   a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.x_f32 = x, a.ldx = ldx;
   a.y = y, a.ldy = N_total, a.row0 = row0;
-  a.rx = reinterpret_cast<uint2*>(rx), a.rx_peers = reinterpret_cast<uint2* const*>(rx_peers);
+  a.rx = reinterpret_cast<unsigned long long*>(rx), a.rx_peers = reinterpret_cast<unsigned long long* const*>(rx_peers);
   a.rx_stride = rx_stride, a.done = done, a.status = status;
   a.rank = rank, a.nranks = nranks, a.spin_limit = spin_limit;
   a.N = n_local, a.K = K, a.M = M;

@@ -60,8 +60,8 @@ struct GemvParams {
   int32_t* s;             // [M][N][nblk] int32 block dots (nullable)
   // fused all-gather (multi-GPU): own rows go to y; every output value is also sent to each peer's receive buffer as
   // one 8-byte (value, flag) store; each CTA then collects its slice of the peers' rows from its own receive buffer
-  uint2* const* rx_peers; // device array [nranks] of the ranks' receive buffers (peer-mapped), or null
-  uint2* rx;              // this rank's receive buffer: 2 parities x rx_stride entries ((m, row) -> m*ldy + row)
+  unsigned long long* const* rx_peers;  // device array [nranks] of the ranks' receive buffers (peer-mapped), or null
+  unsigned long long* rx;  // this rank's receive buffer: 2 parities x rx_stride entries ((m, row) -> m*ldy + row)
   int64_t rx_stride;      // entries per parity
   unsigned long long* done;  // CTAs completed over all calls of this layer (call index = done / gridDim.x)
   int64_t N_total;
@@ -555,6 +555,20 @@ __device__ __forceinline__ float warp_sum_scatter(float (&v)[V], int lane) {
   return s;
 }
 
+// Fused all-gather entries: one naturally aligned 64-bit word, flag (1) in the high half, the f32 value's bits in the
+// low half, written and read as 64-bit scalars (relaxed, system scope), so the pair is single-copy atomic.
+__device__ __forceinline__ unsigned long long rx_word(float v) {
+  return (1ull << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void rx_store(unsigned long long* dst, unsigned long long w) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long rx_load(const unsigned long long* src) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+  return w;
+}
+
 // Group reduction: warp reduce-scatter, cross-warp sum in fixed warp order, store of R x M outputs. Contains one
 // __syncthreads. red is double-buffered so the next group's writes never race this group's reads.
 template <int R, int MC>
@@ -577,19 +591,17 @@ __device__ __forceinline__ void reduce_store(const GemvParams& p, int64_t g, flo
       p.y[idx + (int64_t)blockIdx.y * p.y_split] = v;
       if (p.rx_peers != nullptr) {  // fused all-gather: (value, flag 1) into every other rank's receive buffer
         const int64_t off = (int64_t)parity * p.rx_stride + idx;
+        const unsigned long long word = rx_word(v);
         for (int q = 0; q < p.nranks; ++q)
-          if (q != p.rank) {
-            uint2* dst = p.rx_peers[q] + off;
-            asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(__float_as_uint(v)), "r"(1u)
-                         : "memory");
-          }
+          if (q != p.rank) rx_store(p.rx_peers[q] + off, word);
       }
     }
   }
 }
 
-// Fused all-gather, receive side. Every value a peer sends is one 8-byte (value, flag) store, single-copy atomic, so
-// the value is visible together with its flag and no fence is needed. Each CTA collects a contiguous slice of the
+// Fused all-gather, receive side. Every value a peer sends is one naturally aligned 64-bit scalar store of the word
+// (flag << 32 | value bits); a 64-bit scalar access is single-copy atomic, so a reader that sees the flag also sees
+// the value, and no fence is needed. Each CTA collects a contiguous slice of the
 // entries of the peers' rows: it polls each entry (bounded) until the flag is set, copies the value into y and clears
 // the flag for the call after next. The receive buffer alternates between two parities per call, so a fast peer's
 // next call never overwrites entries of this call that are still unread: a rank starts call t+2 only after it has
@@ -606,25 +618,25 @@ __device__ __forceinline__ void allgather_collect(const GemvParams& p, int parit
   const int64_t peer_rows = p.N_total - p.N;
   const int64_t total = (int64_t)p.M * peer_rows;
   const int64_t e_begin = (total * blockIdx.x) / gridDim.x, e_end = (total * (blockIdx.x + 1)) / gridDim.x;
-  uint2* rx = p.rx + (int64_t)parity * p.rx_stride;
+  unsigned long long* rx = p.rx + (int64_t)parity * p.rx_stride;
   int err = 0;
-  for (int64_t e = e_begin + threadIdx.x; e < e_end && !err; e += blockDim.x) {
+  for (int64_t e = e_begin + threadIdx.x; e < e_end; e += blockDim.x) {
     const int64_t m = e / peer_rows, r = e - m * peer_rows;
     const int64_t row = r < p.row0 ? r : r + p.N;
     const int64_t idx = m * p.ldy + row;
-    uint2* src = rx + idx;
-    uint32_t val, flag;
+    unsigned long long* src = rx + idx;
+    // after a timeout the thread stops polling but still clears the rest of its entries, so values that arrived
+    // in time are not left flagged for a later call of the same parity
     long long spins = 0;
-    for (;;) {
-      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(val), "=r"(flag) : "l"(src) : "memory");
-      if (flag != 0u) break;
-      if (++spins > p.spin_limit) {
-        err = 1;
+    while (!err) {
+      const unsigned long long word = rx_load(src);
+      if ((word >> 32) != 0ull) {
+        p.y[idx] = __uint_as_float((uint32_t)word);
         break;
       }
+      if (++spins > p.spin_limit) err = 1;
     }
-    p.y[idx] = __uint_as_float(val);
-    asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(&src->y), "r"(0u) : "memory");
+    rx_store(src, 0ull);
   }
   if (err && p.status) atomicExch(p.status, 1);
   __syncthreads();

@@ -9,6 +9,8 @@
 // The array is a file-scope __device__ variable: every GPU that loads the library holds it (kStaticScratchBytes)
 // until the process exits. Host code cannot use the array's name as a device address, so its address is taken once
 // per device with cudaGetSymbolAddress (on the first call made with that device current) and passed to the kernels.
+// The address is kept per device ordinal for the life of the process: a cudaDeviceReset (or another teardown of the
+// device's primary context) may reload the module elsewhere, after which this entry point must not be called again.
 #include <mutex>
 
 #include "b2q_internal.h"

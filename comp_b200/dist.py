@@ -8,8 +8,8 @@ output slices are all-gathered so every rank holds the full Y [M][N], ready to b
 result does not depend on which rank computes it: the sharded Y is bit-identical to the single-GPU Y.
 
 Exchange paths:
-  "p2p"   fused into the GEMV kernel (b2q_gemv_allgather): every output value is sent to each peer as one 8-byte
-          (value, flag) store into its receive buffer (CUDA IPC mappings over NVLink), and each CTA collects its
+  "p2p"   fused into the GEMV kernel (b2q_gemv_allgather): every output value is sent to each peer as one 64-bit
+          (flag, value) word store into its receive buffer (CUDA IPC mappings over NVLink), and each CTA collects its
           slice of the peers' rows with bounded polls -- no fences, no grid-wide barrier. One launch per layer,
           graph-capturable. The returned Y is this layer's output buffer: call t's result stays valid until the
           layer's next call. Given a pinned host `out`, the kernel stores Y there instead (b2q_host_device_pointer).
@@ -120,7 +120,8 @@ class RowShardedGemv:
         with torch.cuda.device(dev):
             self.y = torch.zeros((self.max_m, self.n), dtype=torch.float32, device=dev)
             self.rx_stride = self.max_m * self.n
-            self.rx = torch.zeros((2, self.rx_stride, 2), dtype=torch.int32, device=dev)  # (value bits, flag)
+            # 64-bit entries: low 32 bits the value's bits, high 32 bits the flag
+            self.rx = torch.zeros((2, self.rx_stride), dtype=torch.int64, device=dev)
             self.done = torch.zeros(1, dtype=torch.int64, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
             torch.cuda.synchronize(dev)
@@ -163,6 +164,21 @@ class RowShardedGemv:
     def status_code(self):
         """0, or 1 if a receive poll timed out (synchronizes)."""
         return int(self.status.item()) if self.exchange == "p2p" else 0
+
+    def reset(self):
+        """Restores the fused exchange after a timed-out call (status_code() == 1), when a late value may still sit
+        in a receive buffer: every rank waits for its own work, the ranks meet, each zeroes its receive buffer, call
+        counter and status, and the ranks meet again before anyone calls the layer. Collective: every rank calls it."""
+        if self.exchange != "p2p":
+            return
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.dev):
+            self.rx.zero_()
+            self.done.zero_()
+            self.status.zero_()
+            torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
 
     # ---- NCCL exchange ----
     def local(self, x):

@@ -136,14 +136,15 @@ def algo_bytes(fmt, n, k, m):
     return n * k * f["nbytes"] // f["block"] + m * (k + 4 * k // host.ACT_BLOCK[f["act"]]) + 4 * m * n
 
 
-def hbm_peak():
-    """Measured HBM GB/s of this pool (MEASURED_PEAKS.json at the repository root), or None."""
-    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+def hbm_peak(value=None):
+    """The HBM bandwidth (GB/s) the --json lines divide by: the given value, else the COMP_B200_HBM_GBS environment
+    variable, else None (no fraction is reported)."""
+    if value is None:
+        value = os.environ.get("COMP_B200_HBM_GBS")
     try:
-        with open(path) as fh:
-            return float(json.load(fh)["hbm_gbs"])
-    except (OSError, KeyError, ValueError):
-        return None
+        return float(value) if value is not None else None
+    except ValueError:
+        raise ValueError(f"HBM peak {value!r} is not a number (GB/s)") from None
 
 
 def check_gemv(fmt, n, k, m, seed=0, extreme=False, mode=2, dev=None, timed=False):
@@ -177,7 +178,7 @@ def check_gemv(fmt, n, k, m, seed=0, extreme=False, mode=2, dev=None, timed=Fals
 
 
 def check_dp4a(seed=0, n=1024, dev=None):
-    """The GPU dp4a.s32.s32 against its definition (src/komp/verify.py:122-139) on edge and random words."""
+    """The GPU dp4a.s32.s32 against its definition (src/komp/verify.py:37-54) on edge and random words."""
     dev = dev or torch.device("cuda")
     rng = np.random.default_rng(seed)
     edge = np.array([0, -1, 0x7F7F7F7F, -0x7F7F7F80, 0x01010101, 0x0F0F0F0F, 0x03030303, 2**31 - 1, -(2**31)],
@@ -200,6 +201,43 @@ def check_dp4a(seed=0, n=1024, dev=None):
         ref += np.where(sa >= 128, sa - 256, sa) * np.where(sb >= 128, sb - 256, sb)
     ref = (ref + 2**31) % 2**32 - 2**31
     return bool(np.array_equal(out.cpu().numpy().astype(np.int64), ref))
+
+
+def check_decode(seed=0, extreme=False, dev=None):
+    """The decode probes against the weight values (the role of verify.check_decode, src/komp/verify.py:70-91):
+    b2q_decode_q4_0 on [37][16] quant bytes and b2q_decode_tq2_0 on [5][64] against the integer decode above, every
+    value; and for TQ2_0 the dot through the probe's values, scaled and summed in KURN's order, bit-identical to the
+    reference dot through the exact block dots. Random data: uniform nibbles / trits; extreme: nibbles 0 and 15 only,
+    and every crumb value (3 included) for TQ2_0."""
+    dev = dev or torch.device("cuda")
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    res = {}
+    if extreme:
+        q4 = torch.tensor([0x00, 0x0F, 0xF0, 0xFF], dtype=torch.uint8)[torch.randint(0, 4, (37, 16), generator=g)]
+        tq = torch.randint(0, 256, (5, 64), dtype=torch.int64, generator=g).to(torch.uint8)
+    else:
+        q4 = torch.randint(0, 256, (37, 16), dtype=torch.int64, generator=g).to(torch.uint8)
+        t = torch.randint(0, 81, (5, 64), dtype=torch.int64, generator=g)
+        tq = ((t % 3) | ((t // 3 % 3) << 2) | ((t // 9 % 3) << 4) | ((t // 27 % 3) << 6)).to(torch.uint8)
+    q4, tq = q4.to(dev), tq.to(dev)
+    out = torch.zeros((37, 32), dtype=torch.int32, device=dev)
+    _lib.call("b2q_decode_q4_0", q4.data_ptr(), out.data_ptr(), 37, stream)
+    res["q4_0"] = bool(torch.equal(out, ref_values("q4_0", q4, 32)))
+    out = torch.zeros((5, 256), dtype=torch.int32, device=dev)
+    _lib.call("b2q_decode_tq2_0", tq.data_ptr(), out.data_ptr(), 5, stream)
+    vals_ok = bool(torch.equal(out, ref_values("tq2_0", tq.reshape(1, 5 * 64), 5 * 256).reshape(5, 256)))
+    # one weight row of 5 blocks against one q8_K column: dots through the probe's values == exact dots
+    x = torch.randn((1, 5 * 256), generator=g).to(dev)
+    xq, xd = host.quantize("tq2_0", x)
+    ws = (torch.randn((1, 5), generator=g) * 0.05).abs().half().view(torch.int16).to(dev)
+    s_probe = (out.long() * xq.long().reshape(5, 256)).sum(dim=1).reshape(1, 1, 5)
+    exact = ref_dots("tq2_0", tq.reshape(1, 5 * 64), xq, 5 * 256)
+    same = torch.equal(ref_dot("tq2_0", ws, xd, s_probe).view(torch.int64),
+                       ref_dot("tq2_0", ws, xd, exact).view(torch.int64))
+    res["tq2_0"] = vals_ok and bool(same)
+    return res
 
 
 # the reference's shapes (src/komp/verify.py PROBLEMS) for its two formats, and the same Q4_0 shapes for the two
@@ -227,15 +265,25 @@ def json_line(r, mode, label="", extreme=False, peak=None):
     return json.dumps(d)
 
 
-def run_all(log=print, as_json=False):
+def run_all(log=print, as_json=False, peak=None):
+    """dp4a probe, decode probes (random and extreme), then every GEMV problem in both variants, random and extreme
+    data (src/komp/verify.py:152-170). peak: HBM GB/s for the --json fractions (hbm_peak)."""
     fails = 0
     ok = check_dp4a(seed=3)
     fails += not ok
-    peak = hbm_peak()
+    peak = hbm_peak(peak)
     if as_json:
         log(json.dumps({"ok": ok, "op": "dp4a.s32.s32", "words": 1024}))
     else:
         log(f"{'ok  ' if ok else 'FAIL'} dp4a.s32.s32 on the GPU == its definition (1024 edge/random words)")
+    for extreme in (False, True):
+        for f, ok in check_decode(seed=7, extreme=extreme).items():
+            fails += not ok
+            kind = "extreme" if extreme else "random"
+            if as_json:
+                log(json.dumps({"ok": ok, "op": "decode", "fmt": f, "data": kind}))
+            else:
+                log(f"{'ok  ' if ok else 'FAIL'} decode {f:5} {kind:7} (values == integer decode)")
     for fmt, probs in PROBLEMS.items():
         for mode in (0, 2):
             for n, k, m in probs:

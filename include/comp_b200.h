@@ -211,8 +211,10 @@ int b2q_split_blocks(int fmt, const uint8_t* blocks, int64_t n, int64_t k, uint8
  * b2q_quant_gemv_ws with exactly `splits` K splits (2..16, dividing the blocks of a row) whose partial sums live in
  * a fixed scratch array inside the library: b2q_noalloc_scratch_bytes() bytes (4 MiB) on every GPU that loads the
  * library, held until the process exits. splits * M * N * 4 must fit in it (else B2Q_ERANGE), M <= 4.
- * The first call on a device, with that device current, looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture. Every call shares the one array, which keeps the last call's
+ * The first call on a device, with that device current, looks up the array's device address (cudaGetSymbolAddress)
+ * and keeps it for the life of the process; make that first call before any stream capture. A cudaDeviceReset (or
+ * any teardown of the device's primary context) can move the array, so after one this entry point must not be used
+ * again in the process. Every call shares the one array, which keeps the last call's
  * partial sums (each call overwrites all the sums it reads, so nothing has to start at zero); calls whose work
  * overlaps on the GPU (other streams, other host threads) race on it. No counterpart in the reference.
  */
@@ -225,17 +227,22 @@ int b2q_quant_gemv_splitk_noalloc(int fmt, const uint8_t* wq, int64_t ldwq, cons
  * Row-sharded GEMV with the output all-gather fused into the kernel (multi-GPU, one process per GPU).
  * This rank owns rows [row0, row0 + n_local) of a layer with N_total rows; wq/ws hold only those rows. The kernel
  * quantizes the replicated f32 activations x [M][ldx] in its prologue (as b2q_quant_gemv), computes its rows into
- * y [M][N_total], and sends every value to every other rank as one 8-byte (value bits, flag 1) store into that
- * rank's receive buffer (rx_peers[q], peer-mapped). Each CTA then collects a slice of the other ranks' rows from its
- * own rx: it polls each entry (at most spin_limit times) until its flag is set, copies the value into y and clears
- * the flag. When the kernel completes, y holds all N_total rows. No fences and no grid-wide barrier are needed.
- *   rx:        this rank's receive buffer, 2 x rx_stride entries of 8 bytes (uint32 value bits, uint32 flag),
- *              zeroed once before the first call; entry (m, row) of a call sits at parity * rx_stride + m*N_total + row.
+ * y [M][N_total], and sends every value to every other rank as one 64-bit scalar store of the word
+ * (1 << 32 | value bits) into that rank's receive buffer (rx_peers[q], peer-mapped); a naturally aligned 64-bit access
+ * is single-copy atomic, so the flag is never seen without its value. Each CTA then collects a slice of the other
+ * ranks' rows from its own rx: it polls each entry (at most spin_limit times) until its flag is set, copies the value
+ * into y and clears the entry. When the kernel completes, y holds all N_total rows. No fences and no grid-wide barrier
+ * are needed.
+ *   rx:        this rank's receive buffer, 2 x rx_stride 8-byte-aligned uint64 entries (low 32 bits: value bits,
+ *              high 32 bits: flag), zeroed once before the first call; entry (m, row) of a call sits at
+ *              parity * rx_stride + m*N_total + row.
  *   rx_peers:  device array [nranks] of the ranks' rx base pointers (rx_peers[rank] == rx).
  *   done:      uint64 counter of completed CTAs, zeroed once; the call index is done / grid, its parity selects
  *              the half of rx, so consecutive calls (also as CUDA-graph replays) alternate halves.
  *   status:    device int32 set to 1 if a poll gave up (the output is then invalid); the call returns B2Q_OK once
- *              launched.
+ *              launched. After status 1 the exchange state is no longer consistent (a late value may still land in
+ *              rx): before the next call every rank must wait for its stream, meet the others (a host barrier), zero
+ *              rx, done and status, and meet again (comp_b200.dist.RowShardedGemv.reset does this).
  *   Every rank must make the same sequence of calls with the same shapes. M <= 4.
  * No reference counterpart (the reference has no multi-GPU path); replaces host.gemv + an NCCL all-gather.
  */

@@ -5,8 +5,8 @@
  * Restates (paths inside the komp project):
  *   orc_quant_q8_0   ktl.q8_0_quantize   patches/0001-language-extra-kurn.patch:104-114, kernels.py:22-33
  *   orc_quant_q8_K   ktl.q8_K_quantize   patch:117-131, kernels.py:36-45, bsums as host.q8_K_blocks host.py:43-52
- *   orc_gemv         exact int block dots (verify.exact_idots, verify.py:179-185) and KURN's reference dot rebuilt
- *                    in f64 in block order (verify.rebuild_reference, verify.py:188-205)
+ *   orc_gemv         exact int block dots (verify.exact_idots, verify.py:94-100) and KURN's reference dot rebuilt
+ *                    in f64 in block order (verify.rebuild_reference, verify.py:103-120)
  *
  * Build (oracle/build.py): gcc -O2 -fopenmp -ffp-contract=off -shared -fPIC. No fast-math, no FMA contraction:
  * every float operation is the correctly rounded IEEE operation the reference specifies.
@@ -186,6 +186,17 @@ void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const
       y[m * N + n] = total;
     }
   }
+}
+
+/* Sets the OpenMP team size of every later call (the quantizers' and the GEMV's parallel loops). Callers pass the
+ * number of cores this process may run on, so an inherited OMP_NUM_THREADS=1 (torchrun sets it) does not serialize
+ * the baseline. */
+void orc_set_threads(int nthreads) {
+#ifdef _OPENMP
+  if (nthreads > 0) omp_set_num_threads(nthreads);
+#else
+  (void)nthreads;
+#endif
 }
 
 int orc_max_threads(void) {

@@ -23,6 +23,9 @@ def load():
         lib.orc_quant_q8_K.argtypes = [P, I64, I64, P, P, P]
         lib.orc_gemv.argtypes = [ctypes.c_int, P, I64, P, P, P, I64, I64, I64, P, P, ctypes.c_int]
         lib.orc_max_threads.restype = ctypes.c_int
+        lib.orc_set_threads.argtypes = [ctypes.c_int]
+        # one thread per core this process may use, whatever OMP_NUM_THREADS says (torchrun sets it to 1)
+        lib.orc_set_threads(len(os.sched_getaffinity(0)))
         lib.orc_half_to_float.argtypes = [ctypes.c_uint16]
         lib.orc_half_to_float.restype = ctypes.c_float
         lib.orc_float_to_half.argtypes = [ctypes.c_float]

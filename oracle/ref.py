@@ -20,7 +20,7 @@ QOFF = {"q4_0": 2, "tq2_0": 0, "q8_0": 2, "iq4_nl": 2}
 SOFF = {"q4_0": 0, "tq2_0": 64, "q8_0": 0, "iq4_nl": 0}
 # ggml's IQ4_NL levels (kvalues_iq4nl), the codebook of the format
 IQ4_NL_LEVELS = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], dtype=np.int8)
-TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:113)
+TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:28)
 
 F32 = np.float32
 
@@ -101,7 +101,7 @@ def quantize(fmt, x):
 
 
 # ---------------------------------------------------------------------------------------------------------------
-# Weight decode (patch:16-19, 39-63; verify.py:142-152)
+# Weight decode (patch:16-19, 39-63; verify.py:57-67)
 # ---------------------------------------------------------------------------------------------------------------
 
 
@@ -122,7 +122,7 @@ _TQ2_SHIFT = np.array([2 * ((v % 128) // 32) for v in range(256)], dtype=np.uint
 
 def decode_tq2_0(wq, k):
     """TQ2_0 quant plane uint8 [n][k/4] -> int8 values [n][k] = crumb - 1: value v of a block sits in byte
-    (v/128)*32 + v%32 at bits 2*((v%128)/32) (patch:18-19, 58-63; verify.py:147-152). Crumb 3 decodes to +2."""
+    (v/128)*32 + v%32 at bits 2*((v%128)/32) (patch:18-19, 58-63; verify.py:62-67). Crumb 3 decodes to +2."""
     wq = np.asarray(wq, dtype=np.uint8)
     n = wq.shape[0]
     blocks = wq[:, : k // 4].reshape(n, k // 256, 64)
@@ -156,7 +156,7 @@ def decode(fmt, wq, k):
 
 def idots(fmt, wq, xq, k):
     """Exact block dots int64 [M][N][K/block] of the decoded weight values with the int8 activations
-    (verify.exact_idots, src/komp/verify.py:179-185). Computed as f64 matmuls, exact since |dot| < 2^53."""
+    (verify.exact_idots, src/komp/verify.py:94-100). Computed as f64 matmuls, exact since |dot| < 2^53."""
     blk = BLOCK[fmt]
     vals = decode(fmt, wq, k).astype(np.float64)
     n = vals.shape[0]
@@ -174,7 +174,7 @@ def idots(fmt, wq, xq, k):
 def reference_dot(fmt, ws, xd, s):
     """KURN's kurn.formats.reference_dot for every output, from the int block dots s [M][N][nb]: per output a
     sequential Python-float (f64) sum over blocks of d_w * d_x * s (q4_0) or d_x * d_w * s (tq2_0), the exact
-    float operations and order of verify.rebuild_reference (src/komp/verify.py:188-205). -> f64 [M][N]."""
+    float operations and order of verify.rebuild_reference (src/komp/verify.py:103-120). -> f64 [M][N]."""
     dw = np.asarray(ws, dtype=np.int16).view(np.float16).astype(np.float64)  # [n][nb]
     xd = np.asarray(xd, dtype=np.float32)
     # q8_0 blocks carry an f16 scale (the stored xd is already f16-exact); q8_K blocks carry the f32 scale
@@ -210,7 +210,7 @@ def relerr(y, ref):
 
 def dp4a_ref(a, b, c):
     """PTX dp4a.s32.s32: c + sum of the products of the four signed bytes of a and b, int32 wraparound
-    (src/komp/verify.py:122-126). Vectorized over int arrays."""
+    (src/komp/verify.py:37-41). Vectorized over int arrays."""
     a = np.asarray(a, dtype=np.int64) & 0xFFFFFFFF
     b = np.asarray(b, dtype=np.int64) & 0xFFFFFFFF
     r = np.asarray(c, dtype=np.int64).copy()

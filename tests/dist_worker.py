@@ -1,6 +1,7 @@
 """Worker for tests/test_gpu_dist.py (run by torch.distributed.run, one process per GPU): row-sharded GEMVs with the
 fused P2P all-gather and with NCCL, checked bit-for-bit against the unsharded GEMV of the same layer on this GPU,
-over repeated calls and CUDA-graph replays. Prints one line `RESULT <rank> ok|FAIL <details>`."""
+over repeated calls and CUDA-graph replays, and against the C oracle (exact block dots, f64 reference dot) on sampled
+rows of every rank's slice. Prints one line `RESULT <rank> ok|FAIL <details>`."""
 
 import datetime
 import os
@@ -9,11 +10,29 @@ import sys
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from comp_b200 import host  # noqa: E402
 from comp_b200.dist import RowShardedGemv, partition  # noqa: E402
+from oracle import native, ref  # noqa: E402
+
+TOL = 1e-5  # KURN's rule (src/komp/verify.py:28)
+
+
+def oracle_rows(fmt, wq, ws, x, n, k, world, seed):
+    """Sampled rows (up to 64 of every rank's slice, plus each slice's first and last row) and the oracle's exact
+    reference Y for them, f64 [M][rows]."""
+    rng = np.random.default_rng(seed)
+    picks = []
+    for r0, cnt in partition(n, world):
+        if cnt:
+            picks += [r0, r0 + cnt - 1, *rng.choice(np.arange(r0, r0 + cnt), min(cnt, 64), replace=False)]
+    rows = np.unique(np.array(picks))
+    oq, od = ref.quantize(fmt, x.cpu().numpy())
+    r, _ = native.gemv(fmt, wq.cpu().numpy()[rows], ws.cpu().numpy()[rows], oq, od, k)
+    return rows, r
 
 
 def layer(fmt, n, k, dev, seed):
@@ -42,6 +61,7 @@ def main():
         g.manual_seed(200 + ci)
         x = torch.randn((m, k), device=dev, generator=g)
         want = host.quant_gemv(fmt, wq, ws, x, n, k)
+        rows_o, r_o = oracle_rows(fmt, wq, ws, x, n, k, world, 300 + ci)
         row0, rows = partition(n, world)[rank]
         shard = (wq[row0 : row0 + rows].contiguous(), ws[row0 : row0 + rows].contiguous())
         for exchange in ("p2p", "nccl"):
@@ -50,6 +70,9 @@ def main():
                 y = L(x).clone()
                 if not torch.equal(y.view(torch.int32), want.view(torch.int32)):
                     fails.append(f"{fmt} {n}x{k} m={m} {exchange} call {t}: max diff {(y - want).abs().max().item()}")
+                err = ref.relerr(y.cpu().numpy()[:, rows_o], r_o)
+                if not err <= TOL:
+                    fails.append(f"{fmt} {n}x{k} m={m} {exchange} call {t}: relerr {err:.2e} vs the oracle")
             # host buffers: pinned x copied in by a kernel, Y stored into pinned host memory (two calls in a row)
             xh = x.cpu().pin_memory()
             outs = [torch.full((m, n), float("nan")).pin_memory() for _ in range(2)]

@@ -8,10 +8,10 @@ Run in a container that has the reference checked out (it is read, never modifie
 What is recorded (every array is the reference's own output for the stored input):
   quant/*     config-2 quantizer input x f32 [4][14336]; komp host.quantize("q4_0") -> q8_0 (xq, xd) and
               host.quantize("tq2_0") -> q8_K (xq, xd)
-  gemv/<id>/* for each problem of src/komp/verify.py:226 (plus two config-0/1 row slices), random and extreme data:
+  gemv/<id>/* for each problem of src/komp/verify.py:141 (plus two config-0/1 row slices), random and extreme data:
               ggml weight bytes W, activations x, komp quantize -> (xq, xd), komp gemv store_s=True in mode 0
               (bytes) and mode 1 (dp4a fallback) -> (y0, s0), (y1, s1)
-  dp4a/*      the check_dp4a word mix of src/komp/verify.py:129-139 and kernels.dp4a_probe(MODE=1) outputs
+  dp4a/*      the check_dp4a word mix of src/komp/verify.py:44-54 and kernels.dp4a_probe(MODE=1) outputs
   decode/*    kernels.q4_0_decode / tq2_0_decode outputs on random quant planes (tq2_0 includes crumb 3)
 
 Inputs come from oracle.ref's seeded generators (numpy PCG64); the arrays themselves are stored, so the tests do not
@@ -28,7 +28,7 @@ import tempfile
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 
-PROBLEMS = {  # src/komp/verify.py:226, plus a 32-row slice of BASELINE configs 0 and 1 (K=4096)
+PROBLEMS = {  # src/komp/verify.py:141, plus a 32-row slice of BASELINE configs 0 and 1 (K=4096)
     "q4_0": ((64, 512, 1), (37, 416, 3), (5, 96, 2), (32, 4096, 1)),
     "tq2_0": ((64, 1024, 1), (37, 768, 3), (5, 1280, 2), (32, 4096, 3)),
 }
@@ -81,7 +81,7 @@ def main():
                 manifest["gemv"].append(dict(id=cid, fmt=fmt, n=n, k=k, m=m, seed=seed, extreme=extreme))
                 print("gemv", cid, flush=True)
 
-    # dp4a word mix (src/komp/verify.py:129-139)
+    # dp4a word mix (src/komp/verify.py:44-54)
     rng = random.Random(3)
     edge = [0, -1, 0x7F7F7F7F, -0x7F7F7F80, 0x01010101, 0x0F0F0F0F, 0x03030303, 2**31 - 1, -(2**31), 0x80000000 - 2**32]
     n = 1024

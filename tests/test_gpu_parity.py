@@ -16,7 +16,7 @@ from .conftest import golden_case_ids
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-5  # KURN's rule (src/komp/verify.py:113)
+TOL = 1e-5  # KURN's rule (src/komp/verify.py:28)
 
 
 def _t(a, dev):
@@ -61,7 +61,7 @@ def test_quantizer_bytes_match_reference(cuda, golden, fmt):
     act = ref.ACT[fmt]
     assert np.array_equal(xq.cpu().numpy(), golden[f"quant/{act}/xq"])
     assert _same_f32(xd.cpu().numpy(), golden[f"quant/{act}/xd"])
-    # ggml block bytes, as verify.check_gemv compares them (src/komp/verify.py:212-215)
+    # ggml block bytes, as verify.check_gemv compares them (src/komp/verify.py:128-130)
     oq, od = ref.quantize(fmt, x)
     assert host.act_blocks(fmt, xq.cpu().numpy(), xd.cpu().numpy()) == host.act_blocks(fmt, oq, od)
 
@@ -165,18 +165,26 @@ def test_gemv_full_size_matches_oracle(cuda, fmt, n, k, m):
                                      ("q4_0", 28672, 4096), ("q4_0", 6144, 4096), ("q8_0", 128256, 4096),
                                      ("iq4_nl", 28672, 4096)])
 def test_gemv_large_layers_sampled_rows(cuda, fmt, n, k):
-    """Configs 3/4 at full size: every output row checked against the C oracle on a sample of rows (the row
-    result does not depend on the other rows), plus the int32 dots of the sampled rows."""
+    """Configs 3/4 at full size, through the fused call (the bench's path) and the separate quantize + GEMV with the
+    int32 block-dot dump: on a sample of rows (a row's result does not depend on the other rows) the block dots equal
+    the C oracle's bit for bit, Y is within the rule of the oracle's exact reference, and the fused Y equals the
+    separate call's."""
     rng = np.random.default_rng(23)
     wq, ws = ref.random_split(fmt, rng, n, k)
     x = rng.standard_normal((1, k)).astype(np.float32)
     twq, tws = _t(wq, cuda), _t(ws, cuda)
     y = host.quant_gemv(fmt, twq, tws, _t(x, cuda), n, k).cpu().numpy()
+    xq, xd = host.quantize(fmt, _t(x, cuda))
+    y2, s = host.gemv(fmt, twq, tws, xq, xd, n, k, mode=2, store_s=True)
     rows = np.unique(np.concatenate([rng.choice(n, 512, replace=False), [0, n - 1]]))
+    s = s[:, torch.from_numpy(rows).to(cuda)].cpu().numpy()
     oq, od = ref.quantize(fmt, x)
-    r, _ = native.gemv(fmt, wq[rows], ws[rows], oq, od, k)
+    assert np.array_equal(xq.cpu().numpy(), oq) and _same_f32(xd.cpu().numpy(), od)
+    r, os_ = native.gemv(fmt, wq[rows], ws[rows], oq, od, k, want_s=True)
+    assert np.array_equal(s, os_)
     assert ref.relerr(y[:, rows], r) <= TOL
-    del twq, tws
+    assert _same_f32(y, y2.cpu().numpy())
+    del twq, tws, y2
     torch.cuda.empty_cache()
 
 
@@ -286,12 +294,16 @@ def test_ring_and_register_paths_identical(cuda, fmt, n, k, m):
 def test_allgather_receive_times_out_and_reports(cuda):
     """The fused all-gather's receive polls are bounded: with a 'peer' that never runs (its rows never arrive), every
     poll gives up after spin_limit tries, the kernel sets the status word and completes, and the context stays usable.
-    Everything lives on this GPU: the peer's receive buffer is a plain local buffer, so no GPU waits on another."""
+    Everything lives on this GPU: the peer's receive buffer is a plain local buffer, so no GPU waits on another.
+    Entries are 64-bit words (high half flag, low half value bits). Some of the peer's entries are planted as already
+    arrived: after a timeout a thread stops polling but still clears its remaining entries, so none stays flagged."""
     n_total, k, rows = 64, 512, 32
     wq, ws, x, twq, tws, tx = _layer("q4_0", rows, k, 1, 21, cuda)
     y = torch.zeros((1, n_total), device=cuda)
-    rx = torch.zeros((2, n_total, 2), dtype=torch.int32, device=cuda)        # this rank's receive buffer
-    rx_peer = torch.zeros((2, n_total, 2), dtype=torch.int32, device=cuda)   # stands in for rank 1's
+    rx = torch.zeros((2, n_total), dtype=torch.int64, device=cuda)        # this rank's receive buffer
+    rx_peer = torch.zeros((2, n_total), dtype=torch.int64, device=cuda)   # stands in for rank 1's
+    planted = np.arange(rows, n_total)[::3]                               # peer rows that "arrived" (value 2.5)
+    rx[0, torch.from_numpy(planted).to(cuda)] = (1 << 32) | int(np.float32(2.5).view(np.uint32))
     done = torch.zeros(1, dtype=torch.int64, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     rxp = torch.tensor([rx.data_ptr(), rx_peer.data_ptr()], dtype=torch.int64, device=cuda)
@@ -302,9 +314,10 @@ def test_allgather_receive_times_out_and_reports(cuda):
     assert int(status.item()) == 1                        # rank 1's rows never arrived
     want = host.quant_gemv("q4_0", twq, tws, tx, rows, k).cpu().numpy()
     assert _same_f32(y[:, :rows].cpu().numpy(), want)      # own rows computed
-    sent = rx_peer[0, :rows].cpu().numpy()                 # and sent to the 'peer' as (value, flag 1), parity 0
-    assert np.array_equal(sent[:, 1], np.ones(rows, np.int32))
-    assert _same_f32(sent[:, 0].view(np.float32), want[0])
+    sent = rx_peer[0, :rows].cpu().numpy()                 # and sent to the 'peer' as (flag 1, value), parity 0
+    assert np.array_equal(sent >> 32, np.ones(rows, np.int64))
+    assert _same_f32((sent & 0xFFFFFFFF).astype(np.uint32).view(np.float32), want[0])
+    assert not rx.cpu().numpy().any()                      # every receive entry cleared, planted ones included
     assert int(done.item()) > 0                            # every CTA counted itself in
     # the context is still usable
     assert _same_f32(host.quant_gemv("q4_0", twq, tws, tx, rows, k).cpu().numpy(), want)

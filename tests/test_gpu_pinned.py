@@ -16,7 +16,7 @@ from oracle import native, ref
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-5  # KURN's rule (src/komp/verify.py:113)
+TOL = 1e-5  # KURN's rule (src/komp/verify.py:28)
 
 
 def _same_f32(a, b):
