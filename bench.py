@@ -24,8 +24,9 @@ Also in the line:
              N > 1: RowShardedGemv(x_host, out=y_host)); --e2e-api device uses device buffers with torch memcpys.
   e2e_dropin N = 1: COMP's own call sequence, host.quantize + host.gemv (the reference's signatures), x copied in
              from pinned host memory and Y copied back every step.
-  clocks     NVML samples over a window of at least one second of steps that runs straight into the timed region
-             (the timed region itself is short), with the count of samples taken inside it.
+  clocks     NVML sampled every millisecond during the timed region (the count of samples inside it is given).
+  sustained  >= 1 s of the same steps right after the timed region, event-timed, with its own NVML record: the rate
+             once the 1 kW power cap has acted (the timed region itself is short and starts from cool clocks).
 
 --impl reference: the reference's CPU path on the same workload, rank 0 only: the C + OpenMP restatement of COMP's
 quantizers and KURN's reference dot (oracle/c/oracle.c, all host cores) is the line's value; next to it COMP itself
@@ -199,7 +200,7 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(mhz), "samples_in_timed_region": len(timed),
                 "sm_mhz_timed_region": statistics.median(timed) if timed else None,
                 "window_s": round(time.perf_counter() - self._t0, 3) if self._t0 else None,
-                "window": "steps run for >= 1 s straight into the timed region, then the timed region"}
+                "period_ms": self.period * 1e3}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -591,16 +592,12 @@ def main():
         L.obj.wq, L.obj.ws = wq, ws
         return L.obj(L.x)
 
-    def step(c, ev=None):
-        for i, L in enumerate(layers):
-            if ev is not None and i == dominant:
-                ev[0].record(stream)
+    def step(c):
+        for L in layers:
             if world == 1:
                 launch(L, *L.w[c])
             else:
                 sharded(L, *L.w[c])
-            if ev is not None and i == dominant:
-                ev[1].record(stream)
 
     for w in range(args.warmup):
         step(w % copies)
@@ -631,34 +628,16 @@ def main():
         torch.cuda.synchronize()
         dist.barrier()
 
-    def run_step(s, ev=None):
+    def run_step(s):
         if world == 1:
-            step(s % copies, ev)
+            step(s % copies)
         else:
             graphs[s % copies].replay()
 
-    # ---- device-timed region: inputs resident in HBM; NVML sampled from >= 1 s of steps before it through it ----
-    dom_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps if world == 1 else 0)]
+    # ---- device-timed region: inputs resident in HBM, nothing but the steps between the two events (an event
+    # between two kernels would end their programmatic overlap); NVML sampled every millisecond inside it ----
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # the window's step count comes from a short timing, max over ranks, so every rank makes the same calls
-    n_soak = 0
-    if not args.no_extras:
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record(stream)
-        for s in range(20):
-            run_step(s)
-        p1.record(stream)
-        p1.synchronize()
-        tp = torch.tensor([p0.elapsed_time(p1) / 20], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
-        n_soak = int(min(200000, -(-1000.0 // max(1e-3, float(tp.item())))))
-    with ClockSampler(dev) as clocks:
-        for s in range(n_soak):
-            run_step(s)
-            if s % 64 == 63:
-                stream.synchronize()
+    with ClockSampler(dev, period=0.001) as clocks:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -666,7 +645,7 @@ def main():
         clocks.mark(True)
         start.record(stream)
         for s in range(args.steps):
-            run_step(s, dom_events[s] if world == 1 else None)
+            run_step(s)
         end.record(stream)
         end.synchronize()
         torch.cuda.synchronize()
@@ -685,6 +664,30 @@ def main():
         for L in layers:
             if L.obj.status_code() != 0:
                 raise RuntimeError(f"rank {rank}: fused all-gather poll timed out on {L.name} ({L.obj.status_code()})")
+
+    # ---- sustained: >= 1 s of the same steps right after, event-timed, with its own clock record (a short timed
+    # region starts from cool clocks; this shows the rate once the power cap has had time to act). The step count
+    # comes from the timed region's rate, max over ranks, so every rank makes the same calls ----
+    sustained = None
+    if not args.no_extras:
+        n_sus = int(min(200000, -(-1000.0 // max(1e-3, ms / args.steps))))
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev, period=0.005) as sclocks:
+            if world > 1:
+                dist.barrier()
+            sclocks.mark(True)
+            q0.record(stream)
+            for s in range(n_sus):
+                run_step(s)
+            q1.record(stream)
+            q1.synchronize()
+            sclocks.mark(False)
+        ts = torch.tensor([q0.elapsed_time(q1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        sms = float(ts.item())
+        sustained = {"value": round(total_bytes * n_sus / (sms / 1e3) / 1e9, 2), "unit": "GB/s", "steps": n_sus,
+                     "ms_per_step": round(sms / n_sus, 5), "clocks": sclocks.summary()}
 
     # ---- every layer alone, back to back over rotating copies (>= 4x L2), event-timed, max over ranks ----
     per_layer = []
@@ -730,12 +733,11 @@ def main():
                 L.obj.wq, L.obj.ws = L.w[0]
 
     dom = layers[dominant]
-    if world == 1:
-        dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_events)
-        dom_note = "mean CUDA-event duration of its launches inside the timed steps"
-    elif dom_alone_ms is not None:
+    if dom_alone_ms is not None:
         dom_ms = dom_alone_ms
-        dom_note = "dominant layer alone (graph replays over rotating copies after the timed steps), max over ranks"
+        dom_note = ("dominant kernel alone: CUDA events around back-to-back launches of it over rotating weight copies "
+                    "(>= 4x L2), on its launching stream, after the timed steps" +
+                    (" (graph replays), max over ranks" if world > 1 else ""))
     else:
         dom_ms = ms / args.steps
         dom_note = "whole step (per-layer timing skipped)"
@@ -930,6 +932,7 @@ def main():
                        "(src/komp/host.py:63-85); torch memcpy of x in from pinned memory, Y out; host sync every step"},
             "gpu_launches": launches,
             "clocks": cs,
+            "sustained": sustained,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -33,6 +33,7 @@
 //     TMA ring, activations in shared memory). Both are slower on the B200 layer shapes measured so far.
 #include <algorithm>
 #include <cmath>
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -117,12 +118,16 @@ static int occupancy(KernelFn fn, int threads, size_t smem, int max_smem_optin) 
   return blocks;
 }
 
+// Process-wide tuning state below is written by the b2q_set_* hooks and read by every launch: atomics, so a hook
+// called from one host thread while another launches is no data race (that launch sees the old or the new setting;
+// results are the same either way, up to the f32 summation order of a different schedule).
+
 // Programmatic dependent launch of the GEMV kernels (on by default; b2q_set_pipeline path 3/4 toggles it).
-static int g_pdl = 1;
+static std::atomic<int> g_pdl{1};
 bool pdl_enabled() { return g_pdl != 0; }
 
 // Tuning overrides (benchmark hook): 0 = planner's choice.
-static int g_tune_rows = 0, g_tune_cpt = 0, g_tune_grid = 0, g_tune_stages = 0, g_tune_path = 0;
+static std::atomic<int> g_tune_rows{0}, g_tune_cpt{0}, g_tune_grid{0}, g_tune_stages{0}, g_tune_path{0};
 
 struct Plan {
   int R, T, CPT, grid, stages;
@@ -137,7 +142,7 @@ struct Plan {
 // pairs whenever every CTA slot of the grid can still be filled by whole clusters: measured on B200 (same box), pairs
 // are 4-5% faster on the TQ2_0 config4 layers and up to 14% on the 8-GPU slices, where the prologue weighs most;
 // clusters of 4 or 8 lose on the layers with several CTAs per SM.
-static int g_tune_cluster = 0;
+static std::atomic<int> g_tune_cluster{0};
 
 // Clusters of `cs` CTAs of this kernel and launch shape that can be resident at once on the device.
 static int max_active_clusters(KernelFn fn, int threads, size_t smem, int cs) {
@@ -257,11 +262,11 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
         // Measured on B200 (weight-streaming sweeps over the BASELINE layer shapes): two stages -- one group in
         // flight while one is computed -- with the most CTAs per SM beats deeper rings at lower occupancy.
         sb = ring_stage_bytes(fmt, K, C, R);
-        stages = g_tune_stages > 0 ? g_tune_stages : 2;
+        stages = g_tune_stages > 0 ? g_tune_stages.load() : 2;
         smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
       }
       int cs = 1;
-      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster : (g_tune_cluster == 0 ? 2 : 1);
+      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster.load() : (g_tune_cluster == 0 ? 2 : 1);
       const size_t slot = fmt_slot_bytes(fmt, C);
       if (cs > 1 && smem + slot > (size_t)di.max_smem_optin && g_tune_cluster == 0) cs = 1;
       if (cs > 1) smem += slot;
@@ -309,7 +314,7 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
 }
 
 // Warp-rows path (one column): W warps per CTA, one CTA per SM, each warp with its own S-stage ring of R-row groups.
-static int g_tune_warps = 0;
+static std::atomic<int> g_tune_warps{0};
 
 static int make_warp_plan(int fmt, int64_t N, int64_t K, Plan* out) {
   DeviceInfo di;
@@ -357,7 +362,7 @@ static int make_warp_plan(int fmt, int64_t N, int64_t K, Plan* out) {
 // need CTAs of more than 256 threads are split until each split's row fits 256 threads; b2q_set_splitk(n) forces n.
 // Every split keeps 16-byte aligned whole scale rows (ring path) and whole quads of TQ2_0 chunks. One column group
 // (M <= 4) only.
-static int g_splitk_mode = 0;  // 0: never split (default; measured slower on B200), 1: automatic rule, n>=2: force n
+static std::atomic<int> g_splitk_mode{0};  // 0: never split (default; measured slower on B200), 1: automatic rule, n>=2: force n
 
 static int choose_splits(int fmt, int64_t K, int64_t M) {
   if (g_splitk_mode == 0 || M < 1 || M > kMaxColumns || K == 0) return 1;
@@ -442,9 +447,9 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
 
 // Columns from which a layer runs on the tensor-core GEMM (0 = never). Below it the GEMV kernels, which re-read the
 // weights per group of 4 columns, are the better fit.
-static int g_tc_min_m = 8;
+static std::atomic<int> g_tc_min_m{8};
 // Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
-static int g_tc_schedule = 0;
+static std::atomic<int> g_tc_schedule{0};
 
 // Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD (per-block
 // schedule), or the warp-specialized schedule's activation tiles -- whichever is larger.
