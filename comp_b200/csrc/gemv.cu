@@ -139,9 +139,9 @@ struct Plan {
 };
 
 // CTAs per cluster for the shared activation prologue: 0 = planner, 1 = off, 2 / 4 / 8 = forced. The planner uses
-// pairs whenever every CTA slot of the grid can still be filled by whole clusters: measured on B200 (same box), pairs
-// are 4-5% faster on the TQ2_0 config4 layers and up to 14% on the 8-GPU slices, where the prologue weighs most;
-// clusters of 4 or 8 lose on the layers with several CTAs per SM.
+// pairs whenever every CTA slot of the grid can still be filled by whole clusters, except for short TQ2_0 rows (see
+// make_plan_uncached): measured on B200, pairs win on K = 28672 rows and on the Q4_0 lm_head (88 vs 96 us), lose on
+// K = 8192 TQ2_0 rows since the register prologue got cheaper; clusters of 4 or 8 lose everywhere.
 static std::atomic<int> g_tune_cluster{0};
 
 // Clusters of `cs` CTAs of this kernel and launch shape that can be resident at once on the device.
@@ -266,7 +266,11 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
         smem = (size_t)stages * sb + 8 * (size_t)((stages + 1) & ~1) + xb;
       }
       int cs = 1;
-      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster.load() : (g_tune_cluster == 0 ? 2 : 1);
+      // pairs by default, except TQ2_0 rows of at most 128 chunks (K <= 8192), where each CTA's own prologue is
+      // short and the pair's exchange and barrier cost more than they save (measured on B200: gate_up 57344x8192
+      // 23.6 vs 24.3 us, its 8-GPU slice 7168x8192 6.3 vs 7.5 us; K = 28672 rows and Q4_0 keep pairs)
+      const int auto_cs = (fmt == 1 && C <= 128) ? 1 : 2;
+      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster.load() : (g_tune_cluster == 0 ? auto_cs : 1);
       const size_t slot = fmt_slot_bytes(fmt, C);
       if (cs > 1 && smem + slot > (size_t)di.max_smem_optin && g_tune_cluster == 0) cs = 1;
       if (cs > 1) smem += slot;

@@ -11,8 +11,8 @@
 //     t, t+T, ... (CPT of them) of every row. Each CTA takes a contiguous range of row groups (persistent grid).
 //   * Weight streaming, "ring" path: the R rows' quant bytes and scale bytes of a group are bulk-copied by the TMA
 //     engine (cp.async.bulk, one elected thread) into a ring of S shared-memory stages, each completing on its own
-//     mbarrier; S-1 groups are in flight while one is computed, and the first S-1 are issued before the activation
-//     prologue so the HBM stream starts at once. Stage release needs no extra barrier: the per-group reduction's
+//     mbarrier; S-1 groups are in flight while one is computed, and all S are issued before the activation prologue
+//     so the HBM stream starts at once. Stage release needs no extra barrier: the per-group reduction's
 //     __syncthreads orders every read of a stage before it is refilled. Every mbarrier wait is bounded.
 //   * "register" path (unaligned scale rows, or the byte-wise variant): 128-bit streaming loads straight into
 //     registers, double-buffered one group ahead.
@@ -799,57 +799,70 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
 #pragma unroll
       for (int t = 0; t < 16; ++t) v[j][t] = 0.f;
   }
-  // Local largest magnitude (0 when there is none: NaN never wins), by a balanced tree rather than a 64-step chain.
-  float mx16[16];
-#pragma unroll
-  for (int t = 0; t < 16; ++t)
-    mx16[t] = fmaxf(fmaxf(fabsf(v[0][t]), fabsf(v[1][t])), fmaxf(fabsf(v[2][t]), fabsf(v[3][t])));
-#pragma unroll
-  for (int n = 8; n >= 1; n >>= 1)
-#pragma unroll
-    for (int t = 0; t < n; ++t) mx16[t] = fmaxf(mx16[t], mx16[t + n]);
-  float amax = fmaxf(mx16[0], 0.0f);
-  // The lowest value index whose magnitude is amax, with that value's sign bit: key = index * 2 + sign, minimum over
-  // the values (a tree again); no match leaves 0x7fffffff (an all-NaN chunk, where amax is 0).
-  int key16[16];
+  // Signed maximum and minimum of the chunk (balanced trees; fmaxf / fminf ignore NaN), then of the block over its
+  // 4 threads. The quantizer divides by the signed value of largest magnitude, the first one on ties (ggml scans
+  // with a strict >): when one sign alone reaches the largest magnitude that value is the maximum or the minimum;
+  // when both signs reach it, the lower index decides -- an exact search, run only by warps that hold such a block.
+  float mx16[16], mn16[16];
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
-    key16[t] = 0x7fffffff;
-#pragma unroll
-    for (int j = 3; j >= 0; --j)  // lower field = lower index: it overrides
-      if (fabsf(v[j][t]) == amax) key16[t] = ((vbase + j * 32 + t) << 1) | (int)(__float_as_uint(v[j][t]) >> 31);
+    mx16[t] = fmaxf(fmaxf(v[0][t], v[1][t]), fmaxf(v[2][t], v[3][t]));
+    mn16[t] = fminf(fminf(v[0][t], v[1][t]), fminf(v[2][t], v[3][t]));
   }
 #pragma unroll
   for (int n = 8; n >= 1; n >>= 1)
 #pragma unroll
-    for (int t = 0; t < n; ++t) key16[t] = min(key16[t], key16[t + n]);
-  int first = key16[0] == 0x7fffffff ? 256 : key16[0] >> 1;
-  float cand = (key16[0] & 1) ? -amax : amax;  // the signed value at `first`: its magnitude is amax
-  // combine over the 4 threads of the block: larger magnitude wins, equal magnitudes keep the lower index
+    for (int t = 0; t < n; ++t) {
+      mx16[t] = fmaxf(mx16[t], mx16[t + n]);
+      mn16[t] = fminf(mn16[t], mn16[t + n]);
+    }
+  float mx = mx16[0], mn = mn16[0];
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
-    const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-    const int of = __shfl_xor_sync(0xffffffffu, first, off);
-    const float oc = __shfl_xor_sync(0xffffffffu, cand, off);
-    if (oa > amax || (oa == amax && of < first)) {
-      amax = oa;
-      first = of;
-      cand = oc;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+  }
+  const float amax = fmaxf(fmaxf(mx, -mn), 0.0f);  // 0 for an all-zero (or all-NaN) block
+  float cand = mx >= -mn ? mx : mn;
+  const bool tie = mx == -mn && amax != 0.0f;
+  if (__any_sync(0xffffffffu, tie)) {
+    // the lowest value index whose magnitude is amax, with its sign bit: key = index * 2 + sign, minimum over the
+    // chunk (a tree) and over the block's 4 threads
+    int key16[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      key16[t] = 0x7fffffff;
+#pragma unroll
+      for (int j = 3; j >= 0; --j)  // lower field = lower index: it overrides
+        if (fabsf(v[j][t]) == amax) key16[t] = ((vbase + j * 32 + t) << 1) | (int)(__float_as_uint(v[j][t]) >> 31);
     }
+#pragma unroll
+    for (int n = 8; n >= 1; n >>= 1)
+#pragma unroll
+      for (int t = 0; t < n; ++t) key16[t] = min(key16[t], key16[t + n]);
+    int key = key16[0];
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) key = min(key, __shfl_xor_sync(0xffffffffu, key, off));
+    if (tie) cand = (key & 1) ? -amax : amax;
   }
   const bool nz = amax != 0.0f;
   const float iscale = __fdiv_rn(-127.0f, nz ? cand : 1.0f);
-  // q = min(127, rint(iscale * x)) through q8_K_bits (no conversion unit), bytes packed with prmt, summed with dp4a
+  // q = min(127, rint(iscale * x)) through q8_K_bits' exact add (no conversion unit), two values per packed f32x2
+  // multiply and add (each lane rounded as the scalar operation), bytes packed with prmt, summed with dp4a
+  const float2 is2 = make_float2(iscale, iscale), mg2 = make_float2(12582912.0f, 12582912.0f);
   int sum = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      uint32_t b4[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) b4[e] = q8_K_bits(__fmul_rn(iscale, v[j][k * 4 + e]));
-      w[k] = nz ? pack_low_bytes(b4[0], b4[1], b4[2], b4[3]) : 0u;
+      float2 p01 = __fmul2_rn(make_float2(v[j][k * 4 + 0], v[j][k * 4 + 1]), is2);
+      float2 p23 = __fmul2_rn(make_float2(v[j][k * 4 + 2], v[j][k * 4 + 3]), is2);
+      p01 = __fadd2_rn(make_float2(fminf(p01.x, 127.0f), fminf(p01.y, 127.0f)), mg2);
+      p23 = __fadd2_rn(make_float2(fminf(p23.x, 127.0f), fminf(p23.y, 127.0f)), mg2);
+      w[k] = nz ? pack_low_bytes(__float_as_uint(p01.x), __float_as_uint(p01.y), __float_as_uint(p23.x),
+                                 __float_as_uint(p23.y))
+                : 0u;
       sum = __dp4a((int)w[k], 0x01010101, sum);
     }
     o.x[j] = make_uint4(w[0], w[1], w[2], w[3]);

@@ -282,6 +282,7 @@ int b2q_set_gemm_schedule(int schedule);
  * memory; 1 = off, 0 = planner's choice. Results do not change (identical bytes, identical summation order). */
 int b2q_set_cluster(int ctas);
 
+
 /* Reads (and with clear != 0 resets) the library's device error word: nonzero if a kernel's bounded wait on an
  * mbarrier gave up (the kernel then returned early; its outputs are invalid). Synchronizes with the device. */
 int b2q_device_error(int* code, int clear);
