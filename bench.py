@@ -615,23 +615,33 @@ def main():
         stream.wait_stream(cs)
         return gs
 
-    # N > 1: the step is captured once per weight copy as a CUDA graph (three fused GEMV + all-gather launches, or
-    # GEMV + NCCL all-gather), so host launch time does not bound the multi-GPU step
-    graphs = []
-    launches_per_graph = 0
+    # N > 1: steps are captured as CUDA graphs (fused GEMV + all-gather launches, or GEMV + NCCL all-gather), so host
+    # launch time does not bound the multi-GPU step: one graph of G consecutive steps (whole cycles over the weight
+    # copies, >= 8 steps, so launches inside it keep their programmatic overlap) and one graph per single step for
+    # the remainder of a step count
+    graphs, big = [], None
+    launches_per_step = 0
+    G = copies * -(-8 // copies)
     if world > 1:
         n0 = _lib.launch_count()
         graphs = capture(step, copies)
-        launches_per_graph = (_lib.launch_count() - n0) // copies
+        launches_per_step = (_lib.launch_count() - n0) // copies
+        big = capture(lambda j: [step(s % copies) for s in range(G)], 1)[0]
         for c in range(copies):
             graphs[c].replay()
+        big.replay()
         torch.cuda.synchronize()
         dist.barrier()
 
-    def run_step(s):
+    def run_steps(n):
+        """n consecutive steps (the same calls on every rank)."""
         if world == 1:
-            step(s % copies)
-        else:
+            for s in range(n):
+                step(s % copies)
+            return
+        for _ in range(n // G):
+            big.replay()
+        for s in range(n % G):
             graphs[s % copies].replay()
 
     # ---- device-timed region: inputs resident in HBM, nothing but the steps between the two events (an event
@@ -644,13 +654,12 @@ def main():
         launches0 = _lib.launch_count()
         clocks.mark(True)
         start.record(stream)
-        for s in range(args.steps):
-            run_step(s)
+        run_steps(args.steps)
         end.record(stream)
         end.synchronize()
         torch.cuda.synchronize()
         clocks.mark(False)
-        launches = _lib.launch_count() - launches0 if world == 1 else launches_per_graph * args.steps
+        launches = _lib.launch_count() - launches0 if world == 1 else launches_per_step * args.steps
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
@@ -677,8 +686,7 @@ def main():
                 dist.barrier()
             sclocks.mark(True)
             q0.record(stream)
-            for s in range(n_sus):
-                run_step(s)
+            run_steps(n_sus)
             q1.record(stream)
             q1.synchronize()
             sclocks.mark(False)
@@ -697,20 +705,24 @@ def main():
             nc = copies_for(weight_bytes(L.fmt, slice_rows(L.n, world), L.k))  # the same on every rank
             ws_list = [L.w[c % copies] if c < copies else (L.w[0][0].clone(), L.w[0][1].clone()) for c in range(nc)]
             if world == 1:
+                per_run = 1
                 run = lambda r, L=L, ws_list=ws_list, nc=nc: launch(L, *ws_list[r % nc])  # noqa: E731
                 lg = None
-            else:
-                lg = capture(lambda j, L=L, ws_list=ws_list: sharded(L, *ws_list[j]), nc)
-                run = lambda r, lg=lg, nc=nc: lg[r % nc].replay()  # noqa: E731
-            reps = max(4 * nc, min(400, max(50, args.steps)))
-            for r in range(2 * nc):
+            else:  # one graph of whole cycles over the copies (>= 16 launches, chained as in a step)
+                per_run = nc * -(-16 // nc)
+                lg = capture(lambda j, L=L, ws_list=ws_list, nc=nc, per_run=per_run:
+                             [sharded(L, *ws_list[r % nc]) for r in range(per_run)], 1)
+                run = lambda r, lg=lg: lg[0].replay()  # noqa: E731
+            runs = max(-(-4 * nc // per_run), -(-min(400, max(50, args.steps)) // per_run))
+            reps = runs * per_run
+            for r in range(max(2, -(-2 * nc // per_run))):
                 run(r)
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            for r in range(reps):
+            for r in range(runs):
                 run(r)
             e1.record(stream)
             e1.synchronize()
@@ -844,7 +856,7 @@ def main():
     d2h = sum(L.n * m * 4 for L in layers)
     # graphs that hold NCCL calls must be released before the process group is destroyed
     graphs.clear()
-    del graphs
+    del graphs, big
     torch.cuda.synchronize()
     if world > 1:
         for L in layers:
@@ -901,6 +913,7 @@ def main():
             "data": "synthetic (BASELINE distributions, seeded, random-init weights)",
             "config": bench_config(args.workload, layers_def, m),
             "setup": {"parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
+                      "graph_steps": G if world > 1 else None,
                       "exchange": {None: None,
                                    "p2p": "fused all-gather: 64-bit (flag, value) peer stores from the GEMV epilogue",
                                    "nccl": "NCCL all_gather_into_tensor"}[exchange_name],
