@@ -25,7 +25,7 @@ Also in the line:
   e2e_dropin N = 1: COMP's own call sequence, host.quantize + host.gemv (the reference's signatures), x copied in
              from pinned host memory and Y copied back every step.
   clocks     NVML sampled every millisecond during the timed region (the count of samples inside it is given).
-  sustained  >= 1 s of the same steps right after the timed region, event-timed, with its own NVML record: the rate
+  sustained  >= 1 s of the same steps after the per-layer timing, event-timed, with its own NVML record: the rate
              once the 1 kW power cap has acted (the timed region itself is short and starts from cool clocks).
 
 --impl reference: the reference's CPU path on the same workload, rank 0 only: the C + OpenMP restatement of COMP's
@@ -674,30 +674,8 @@ def main():
             if L.obj.status_code() != 0:
                 raise RuntimeError(f"rank {rank}: fused all-gather poll timed out on {L.name} ({L.obj.status_code()})")
 
-    # ---- sustained: >= 1 s of the same steps right after, event-timed, with its own clock record (a short timed
-    # region starts from cool clocks; this shows the rate once the power cap has had time to act). The step count
-    # comes from the timed region's rate, max over ranks, so every rank makes the same calls ----
-    sustained = None
-    if not args.no_extras:
-        n_sus = int(min(200000, -(-1000.0 // max(1e-3, ms / args.steps))))
-        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(dev, period=0.005) as sclocks:
-            if world > 1:
-                dist.barrier()
-            sclocks.mark(True)
-            q0.record(stream)
-            run_steps(n_sus)
-            q1.record(stream)
-            q1.synchronize()
-            sclocks.mark(False)
-        ts = torch.tensor([q0.elapsed_time(q1)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
-        sms = float(ts.item())
-        sustained = {"value": round(total_bytes * n_sus / (sms / 1e3) / 1e9, 2), "unit": "GB/s", "steps": n_sus,
-                     "ms_per_step": round(sms / n_sus, 5), "clocks": sclocks.summary()}
-
-    # ---- every layer alone, back to back over rotating copies (>= 4x L2), event-timed, max over ranks ----
+    # ---- every layer alone, back to back over rotating copies (>= 4x L2), event-timed, max over ranks; right after
+    # the timed steps, before the sustained window heats the GPU, so both see the same clocks ----
     per_layer = []
     dom_alone_ms = None
     if not args.no_extras:
@@ -743,6 +721,29 @@ def main():
         if world > 1:
             for L in layers:
                 L.obj.wq, L.obj.ws = L.w[0]
+
+    # ---- sustained: >= 1 s of the same steps after the per-layer timing, event-timed, with its own clock record (a
+    # short timed region starts from cool clocks; this shows the rate once the power cap has had time to act). The
+    # step count comes from the timed region's rate, max over ranks, so every rank makes the same calls ----
+    sustained = None
+    if not args.no_extras:
+        n_sus = int(min(200000, -(-1000.0 // max(1e-3, ms / args.steps))))
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev, period=0.005) as sclocks:
+            if world > 1:
+                dist.barrier()
+            sclocks.mark(True)
+            q0.record(stream)
+            run_steps(n_sus)
+            q1.record(stream)
+            q1.synchronize()
+            sclocks.mark(False)
+        ts = torch.tensor([q0.elapsed_time(q1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        sms = float(ts.item())
+        sustained = {"value": round(total_bytes * n_sus / (sms / 1e3) / 1e9, 2), "unit": "GB/s", "steps": n_sus,
+                     "ms_per_step": round(sms / n_sus, 5), "clocks": sclocks.summary()}
 
     dom = layers[dominant]
     if dom_alone_ms is not None:
