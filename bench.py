@@ -61,10 +61,15 @@ WORKLOADS = {
     # IQ4_NL weights (a second extension): the same shapes, all IQ4_NL
     "iq4_nl": [("iq4_nl", 6144, 4096, "qkv"), ("iq4_nl", 4096, 4096, "o_proj"), ("iq4_nl", 28672, 4096, "gate_up"),
                ("iq4_nl", 4096, 14336, "down"), ("iq4_nl", 128256, 4096, "lm_head")],
+    # Q4_K weights (a third extension): the same shapes, all Q4_K
+    "q4_k": [("q4_k", 6144, 4096, "qkv"), ("q4_k", 4096, 4096, "o_proj"), ("q4_k", 28672, 4096, "gate_up"),
+             ("q4_k", 4096, 14336, "down"), ("q4_k", 128256, 4096, "lm_head")],
 }
-BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32}
-BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18}  # ggml block bytes (quant bytes + f16 scale)
-FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32, "q4_k": 256}
+# ggml block bytes (quant bytes + scales); Q4_K's split planes carry 148 bytes per block (4 more than ggml's 144: the
+# scale record unpacked), and only ggml's 144 count as algorithmic bytes
+BLOCK_BYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18, "q4_k": 144}
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3, "q4_k": 4}
 METRIC = "weight-stream GB/s and us/GEMV (% of HBM peak) at 1/2/4/8 B200 vs host CPU ref"
 L2_BYTES = 126 * 2**20
 TOL = 1e-5  # KURN's relative-error rule (src/komp/verify.py:28)
@@ -223,6 +228,15 @@ def make_layer_gpu(fmt, n, k, seed, dev, rows=None):
     elif fmt == "q8_0":
         wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g).view(torch.uint8)
         ws = (torch.randn((n, nb), device=dev, generator=g) * 0.002).abs().half().view(torch.int16)
+    elif fmt == "q4_k":  # the split planes: nibbles, and 20-byte records (f16 d, f16 dmin, sc/m bytes 0..63)
+        wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+        rec = torch.empty((n, nb, 20), dtype=torch.uint8, device=dev)
+        rec[:, :, 0:2] = (torch.randn((n, nb), device=dev, generator=g) * 0.002).abs().half().view(torch.uint8) \
+            .reshape(n, nb, 2)
+        rec[:, :, 2:4] = (torch.randn((n, nb), device=dev, generator=g) * 0.004).abs().half().view(torch.uint8) \
+            .reshape(n, nb, 2)
+        rec[:, :, 4:] = torch.randint(0, 64, (n, nb, 16), dtype=torch.uint8, device=dev, generator=g)
+        ws = rec.reshape(n, nb * 20).view(torch.int16)
     else:
         t = torch.randint(0, 81, (n, k // 4), dtype=torch.uint8, device=dev, generator=g)
         wq = (t % 3) | (((t // 3) % 3) << 2) | (((t // 9) % 3) << 4) | (((t // 27) % 3) << 6)

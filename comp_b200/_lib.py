@@ -28,6 +28,7 @@ SIGNATURES = {
     "b2q_gemv_tq2_0": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
     "b2q_gemv_q8_0": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
     "b2q_gemv_iq4_nl": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
+    "b2q_gemv_q4_k": (INT, [P, I64, P, P, P, P, P, I64, I64, I64, INT, P]),
     "b2q_quant_gemv": (INT, [INT, P, I64, P, P, I64, P, P, P, I64, I64, I64, P]),
     "b2q_workspace_size": (ctypes.c_size_t, [INT, I64, I64, I64]),
     "b2q_pinned_workspace_size": (ctypes.c_size_t, [INT, I64, I64, I64]),

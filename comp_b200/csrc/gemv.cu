@@ -42,16 +42,19 @@
 namespace b2q {
 
 // Weight formats: 0 Q4_0, 1 TQ2_0, 2 Q8_0, 3 IQ4_NL (2 and 3: extensions beyond the reference).
-static inline int fmt_block(int fmt) { return fmt == 1 ? 256 : 32; }  // values per block
-static inline int fmt_chunk_values(int fmt) {                         // per 16-byte chunk
-  return (fmt == 0 || fmt == 3) ? 32 : fmt == 1 ? 64 : 16;
+static inline int fmt_block(int fmt) { return (fmt == 1 || fmt == 4) ? 256 : 32; }  // values per block
+static inline int fmt_chunk_values(int fmt) {                                       // per 16-byte chunk
+  return (fmt == 0 || fmt == 3 || fmt == 4) ? 32 : fmt == 1 ? 64 : 16;
 }
-static inline bool fmt_ok(int fmt) { return fmt >= 0 && fmt <= 3; }
+static inline int fmt_scale_bytes(int fmt) { return fmt == 4 ? 20 : 2; }  // scale-plane bytes per block
+static inline bool fmt_act_q8K(int fmt) { return fmt == 1 || fmt == 4; }  // q8_K activations (else q8_0)
+static inline bool fmt_ok(int fmt) { return fmt >= 0 && fmt <= 4; }
 static inline size_t fmt_slot_bytes(int fmt, int C) {
   return fmt == 0 ? cluster_slot_bytes<0>(C) : fmt == 1 ? cluster_slot_bytes<1>(C)
-                  : fmt == 2 ? cluster_slot_bytes<2>(C) : cluster_slot_bytes<3>(C);
+                  : fmt == 2 ? cluster_slot_bytes<2>(C) : fmt == 3 ? cluster_slot_bytes<3>(C)
+                                                                   : cluster_slot_bytes<4>(C);
 }
-static const char* fmt_list = "Q4_0 (0), TQ2_0 (1), Q8_0 (2) or IQ4_NL (3)";
+static const char* fmt_list = "Q4_0 (0), TQ2_0 (1), Q8_0 (2), IQ4_NL (3) or Q4_K (4)";
 
 // ------------------------------------------------------------------------------------------------------------------
 // ------------------------------------------------------------------------------------------------------------------
@@ -238,7 +241,8 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
   const int T = std::min(kMaxThreads, ((C + CPT - 1) / CPT + 31) / 32 * 32);
   if ((int64_t)T * CPT < C)
     return fail(B2Q_ERANGE, "gemv: K=%lld needs more than %d chunks per thread", (long long)K, CPT);
-  bool use_ring = ring_ok && !bytes && g_tune_path != 2;
+  // Q4_K has a ring kernel only: its byte-wise variant is the dp4a kernel (identical results)
+  bool use_ring = ring_ok && (!bytes || fmt == 4) && (g_tune_path != 2 || fmt == 4);
   if (g_tune_path == 1 && !use_ring) return fail(B2Q_EINVAL, "gemv: ring path forced but not applicable");
   Plan best{};
   double best_score = -1.0;
@@ -246,7 +250,7 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
   const bool xreg = (M == 1) && CPT == 1;
   for (int pass = 0; pass < 2 && best_score < 0; ++pass) {
     const bool ring = use_ring && pass == 0;
-    if (pass == 1 && g_tune_path == 1) break;
+    if (pass == 1 && (g_tune_path == 1 || fmt == 4)) break;  // Q4_K: ring only
     for (int ci = 0; ci < 5; ++ci) {
       const int R = cand[ci];
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
@@ -370,13 +374,14 @@ static std::atomic<int> g_splitk_mode{0};  // 0: never split (default; measured 
 
 static int choose_splits(int fmt, int64_t K, int64_t M) {
   if (g_splitk_mode == 0 || M < 1 || M > kMaxColumns || K == 0) return 1;
+  if (fmt == 4 && (K / 256) % 4) return 1;  // Q4_K: every split must keep whole 16-byte units of scale records
   const int blk = fmt_block(fmt);
   const int64_t nblk = K / blk, C = K / fmt_chunk_values(fmt);
   if (C <= 256) return 1;
   for (int s = 2; s <= 16; s *= 2) {
     if (nblk % s) continue;
     const int64_t nblk_s = nblk / s;
-    if ((nblk_s * 2) % 16) continue;
+    if ((nblk_s * fmt_scale_bytes(fmt)) % 16) continue;
     if (g_splitk_mode >= 2 ? s == g_splitk_mode : C / s <= 256) return s;
   }
   return 1;
@@ -393,11 +398,14 @@ static int check_gemv_args(const char* who, int fmt, const uint8_t* wq, int64_t 
   if (!aligned(y, 4)) return fail(B2Q_EALIGN, "%s: y must be 4-byte aligned", who);
   if (K == 0) return B2Q_OK;  // empty sums: only Y (= 0) is written
   if (!wq || !ws || !x || (!f32_input && !xd)) return fail(B2Q_EINVAL, "%s: null pointer", who);
-  const int64_t qbytes = (fmt == 0 || fmt == 3) ? K / 2 : fmt == 1 ? K / 4 : K;
+  const int64_t qbytes = (fmt == 0 || fmt == 3 || fmt == 4) ? K / 2 : fmt == 1 ? K / 4 : K;
   if (ldwq < qbytes) return fail(B2Q_EINVAL, "%s: ldwq=%lld < %lld quant bytes per row", who, (long long)ldwq,
                                  (long long)qbytes);
   if (!aligned(wq, 16) || (ldwq % 16)) return fail(B2Q_EALIGN, "%s: wq must be 16-byte aligned, ldwq %% 16 == 0", who);
   if (!aligned(ws, 2)) return fail(B2Q_EALIGN, "%s: ws must be 2-byte aligned", who);
+  // Q4_K runs on the TMA ring only: its 20-byte scale records must form whole 16-byte units per row
+  if (fmt == 4 && (((K / 256) * 20) % 16 || !aligned(ws, 16)))
+    return fail(B2Q_EALIGN, "%s: Q4_K needs K a multiple of 1024 and ws 16-byte aligned", who);
   if (!aligned(x, 16)) return fail(B2Q_EALIGN, "%s: activations must be 16-byte aligned", who);
   if (xd && !aligned(xd, 4)) return fail(B2Q_EALIGN, "%s: xd must be 4-byte aligned", who);
   if (K > (int64_t)1 << 30 || N > ((int64_t)1 << 40)) return fail(B2Q_ERANGE, "%s: size too large", who);
@@ -483,7 +491,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
                        ((a.N + 127) / 128) * ((a.M + tc_nt - 1) / tc_nt) >= (int64_t)tc_di.sms;
   // (IQ4_NL has no tensor-core kernel: its many-column layers stay on the GEMV path)
   if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || g_tc_min_m < 8) && !a.rx_peers && aligned(a.wq, 16) &&
-      a.ldwq % 16 == 0 && a.fmt != 3) {
+      a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
     // Measured on B200 (same box, lm_head-sized layers, M = 16..128): the warp-specialized schedule is faster everywhere
@@ -505,7 +513,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
         dq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + ((size_t)a.M * a.K + 15) / 16 * 16);
       }
       if (qo) {
-        const int rc = a.fmt != 1 ? b2q_quant_q8_0(a.x_f32, a.ldx, qo, dq, a.M, a.K, stream)
+        const int rc = !fmt_act_q8K(a.fmt) ? b2q_quant_q8_0(a.x_f32, a.ldx, qo, dq, a.M, a.K, stream)
                                   : b2q_quant_q8_K(a.x_f32, a.ldx, qo, dq, nullptr, a.M, a.K, stream);
         if (rc) return rc;
         xq = qo;
@@ -541,11 +549,15 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   const int64_t Ks = a.K / splits, nblk_s = nblk / splits;
   const int C = (int)(Ks / fmt_chunk_values(a.fmt));
   // ring path: every row's scale bytes (and so every group's) must be a whole number of 16-byte units, 16-aligned
-  const bool ring_ok = ((nblk * 2) % 16 == 0) && ((nblk_s * 2) % 16 == 0) && aligned(a.ws, 16);
+  const int sbytes = fmt_scale_bytes(a.fmt);
+  const bool ring_ok = ((nblk * sbytes) % 16 == 0) && ((nblk_s * sbytes) % 16 == 0) && aligned(a.ws, 16);
+  if (a.fmt == 4 && !ring_ok)
+    return fail(B2Q_EINVAL, "gemv: Q4_K runs on the TMA ring only: K (and each split's K) a multiple of 1024, ws "
+                            "16-byte aligned");
   for (int64_t m0 = 0; m0 < a.M; m0 += kMaxColumns) {
     const int Mc = (int)std::min<int64_t>(kMaxColumns, a.M - m0);
     Plan pl;
-    const bool warp_ok = Mc == 1 && a.M == 1 && splits == 1 && !a.rx_peers && ring_ok && !a.bytes;
+    const bool warp_ok = Mc == 1 && a.M == 1 && splits == 1 && !a.rx_peers && ring_ok && !a.bytes && a.fmt != 4;
     if (g_tune_path == 5 && !warp_ok) return fail(B2Q_EINVAL, "gemv: warp-rows path forced but not applicable");
     int rc = (warp_ok && g_tune_path == 5) ? make_warp_plan(a.fmt, a.N, Ks, &pl)
                                            : make_plan(a.fmt, a.bytes, ring_ok, a.N, Ks, Mc, &pl, splits);
@@ -554,7 +566,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     p.wq = a.wq;
     p.ldwq = a.ldwq;
     p.ws = a.ws;
-    p.ldws = nblk;
+    p.ldws = nblk * (fmt_scale_bytes(a.fmt) / 2);
     p.xq = a.xq ? a.xq + m0 * a.K : nullptr;
     p.ldxq = a.K;
     p.xd = a.xd ? a.xd + m0 * nblk : nullptr;
@@ -614,7 +626,11 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
       cudaGetLastError();
       return fail(B2Q_ECUDA, "gemv: launch failed: %s", cudaGetErrorString(le));
     }
-    rc = after_launch(a.fmt == 0 ? "gemv_q4_0" : a.fmt == 1 ? "gemv_tq2_0" : a.fmt == 2 ? "gemv_q8_0" : "gemv_iq4_nl");
+    rc = after_launch(a.fmt == 0   ? "gemv_q4_0"
+                      : a.fmt == 1 ? "gemv_tq2_0"
+                      : a.fmt == 2 ? "gemv_q8_0"
+                      : a.fmt == 3 ? "gemv_iq4_nl"
+                                   : "gemv_q4_k");
     if (rc) return rc;
     if (splits > 1) {
       DeviceInfo di;
@@ -714,6 +730,19 @@ int b2q_gemv_iq4_nl(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const in
   return launch_gemv(a, (cudaStream_t)stream);
 }
 
+int b2q_gemv_q4_k(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
+  int rc = check_gemv_args("b2q_gemv_q4_k", 4, wq, ldwq, ws, xq, xd, y, N, K, M, false);
+  if (rc) return rc;
+  if (variant < 0 || variant > 2) return fail(B2Q_EINVAL, "b2q_gemv_q4_k: variant %d not in 0..2", variant);
+  if (s && !aligned(s, 4)) return fail(B2Q_EALIGN, "b2q_gemv_q4_k: s must be 4-byte aligned");
+  LaunchArgs a{};
+  a.fmt = 4;
+  a.wq = wq, a.ldwq = ldwq, a.ws = ws, a.xq = xq, a.xd = xd, a.y = y, a.ldy = N, a.s = s;
+  a.N = N, a.K = K, a.M = M;
+  return launch_gemv(a, (cudaStream_t)stream);
+}
+
 int b2q_gemv_q8_0(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
                   int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream) {
   int rc = check_gemv_args("b2q_gemv_q8_0", 2, wq, ldwq, ws, xq, xd, y, N, K, M, false);
@@ -747,7 +776,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
-  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3) return tc_act_bytes(fmt, K, M);  // the GEMV path ignores it
+  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, K, M);  // GEMV ignores it
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
 }

@@ -91,26 +91,55 @@ struct Fmt;
 // kQBytes: quant bytes per block; kOffset: the weights' stored offset (value = field - kOffset), folded in as
 // -kOffset * sum(x); kActQ80: the activations are q8_0 (32-value blocks, f16-exact scales), else q8_K; kLayout: the
 // format whose quant-plane and activation layout this one shares (IQ4_NL is laid out exactly as Q4_0).
+// kScaleBytes: bytes of the scale plane per block (an f16 scale, or Q4_K's 20-byte record).
 template <>
 struct Fmt<0> {  // Q4_0: 32-value blocks, 1 chunk per block, 2 bit-fields (nibbles)
   static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 8, kLayout = 0;
+  static constexpr int kScaleBytes = 2;
   static constexpr bool kActQ80 = true;
 };
 template <>
 struct Fmt<1> {  // TQ2_0: 256-value blocks, 4 chunks per block, 4 bit-fields (crumbs)
   static constexpr int kBlock = 256, kChunkShift = 2, kFields = 4, kQBytes = 64, kOffset = 1, kLayout = 1;
+  static constexpr int kScaleBytes = 2;
   static constexpr bool kActQ80 = false;
 };
 template <>
 struct Fmt<2> {  // Q8_0 (an extension beyond the reference: ggml block_q8_0): 32 int8 values, 2 chunks per block
   static constexpr int kBlock = 32, kChunkShift = 1, kFields = 1, kQBytes = 32, kOffset = 0, kLayout = 2;
+  static constexpr int kScaleBytes = 2;
   static constexpr bool kActQ80 = true;
 };
 template <>
 struct Fmt<3> {  // IQ4_NL (an extension: ggml block_iq4_nl): Q4_0's layout (kLayout 0), nibbles index 16 int8 levels
   static constexpr int kBlock = 32, kChunkShift = 0, kFields = 2, kQBytes = 16, kOffset = 0, kLayout = 0;
+  static constexpr int kScaleBytes = 2;
   static constexpr bool kActQ80 = true;
 };
+// Q4_K (an extension: ggml block_q4_K) in this backend's split planes: 256-value super-blocks of eight 32-value
+// sub-blocks; each 16-byte chunk is one sub-block laid out as a Q4_0 block (kLayout 0: the same activation layout),
+// nibbles 0..15 with no offset; the scale plane holds per super-block f16 d, f16 dmin and the bytes (sc_j, m_j).
+// Value = d * sc_j * q - dmin * m_j; q8_K activations. The chunk sums (kOffset 1: the plain sum) feed the min term.
+template <>
+struct Fmt<4> {
+  static constexpr int kBlock = 256, kChunkShift = 3, kFields = 2, kQBytes = 128, kOffset = 1, kLayout = 0;
+  static constexpr int kScaleBytes = 20;
+  static constexpr bool kActQ80 = false;
+};
+
+// A weight row's scale for one chunk: the f32 block scale; Q4_K: d, dmin and its sub-block's sc, m.
+template <int FMT>
+struct RowScale {
+  float d;
+};
+template <>
+struct RowScale<4> {
+  float d, dmin;
+  int sc, mn;
+};
+// From the block's scale bytes in shared memory (rec: the row's scale plane in the stage, c: the chunk).
+template <int FMT>
+__device__ __forceinline__ RowScale<FMT> row_scale_smem(uint32_t rec, int c);
 
 // ggml's IQ4_NL levels (kvalues_iq4nl) as little-endian int8 bytes: levels 0-3, 4-7, 8-11, 12-15.
 constexpr uint32_t kIq4Lv0 = 0xBFAD9881u, kIq4Lv1 = 0xF6EADDCFu, kIq4Lv2 = 0x26190D01u, kIq4Lv3 = 0x71594535u;
@@ -144,7 +173,7 @@ struct Split {
     return p.wq + (int64_t)blockIdx.y * (p.K / Fmt<FMT>::kBlock * Fmt<FMT>::kQBytes);
   }
   static __device__ __forceinline__ const int16_t* ws(const GemvParams& p) {
-    return p.ws + (int64_t)blockIdx.y * nblk(p);
+    return p.ws + (int64_t)blockIdx.y * nblk(p) * (Fmt<FMT>::kScaleBytes / 2);
   }
   static __device__ __forceinline__ const int8_t* xq(const GemvParams& p) { return p.xq + (int64_t)blockIdx.y * p.K; }
   static __device__ __forceinline__ const float* xd(const GemvParams& p) { return p.xd + (int64_t)blockIdx.y * nblk(p); }
@@ -228,6 +257,25 @@ __device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+template <int FMT>
+__device__ __forceinline__ RowScale<FMT> row_scale_smem(uint32_t rec, int c) {
+  return RowScale<FMT>{f16_bits_to_f32(lds_u16(rec + (uint32_t)(c >> Fmt<FMT>::kChunkShift) * 2u))};
+}
+template <>
+__device__ __forceinline__ RowScale<4> row_scale_smem<4>(uint32_t rec, int c) {
+  const uint32_t base = rec + (uint32_t)(c >> 3) * 20u;
+  const uint32_t dd = lds_u32(base);                              // f16 d, f16 dmin
+  const uint32_t sm = lds_u16(base + 4u + 2u * (uint32_t)(c & 7));  // sc_j, m_j
+  return RowScale<4>{f16_bits_to_f32((uint16_t)(dd & 0xffffu)), f16_bits_to_f32((uint16_t)(dd >> 16)),
+                     (int)(sm & 0xffu), (int)(sm >> 8)};
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -329,9 +377,10 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
           uint32_t qlo, qhi;
           const float d = q8_K_quant8(v, lane, &qlo, &qhi);
           const int o = lane >> 1;  // 16-value piece within the block
-          const int j = (o >> 1) & 3, c = 2 * (o >> 3) + (o & 1);
-          *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + 4 * b + c) * 16 + (lane & 1) * 8) =
-              make_uint2(qlo, qhi);
+          // TQ2_0: field (o / 2) % 4 of chunk 4b + 2 (o / 8) + o % 2; Q4_K: field o % 2 of chunk 8b + o / 2
+          const int j = FMT == 4 ? (o & 1) : ((o >> 1) & 3);
+          const int cc = FMT == 4 ? 8 * b + (o >> 1) : 4 * b + 2 * (o >> 3) + (o & 1);
+          *reinterpret_cast<uint2*>(xs + (int64_t)m * K + (j * C + cc) * 16 + (lane & 1) * 8) = make_uint2(qlo, qhi);
           if (lane == 0) xscale[m * nblk + b] = d;
           if (writer) {
             *reinterpret_cast<uint2*>(Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq + b * 256 + lane * 8) =
@@ -503,9 +552,12 @@ __device__ __forceinline__ void load_xchunk(const GemvParams& p, const uint8_t* 
 //   TQ2_0 (a block spans 4 chunks on 4 adjacent threads): each thread adds its own chunk's exact partial dot,
 //     acc += (dx * dw) * f32(s_chunk) (the reference's dx * dw * s order, kernels.py:141, applied per quarter block),
 //     so the 4 threads need no exchange; with STORE the exact block dot is assembled with two xor-shuffles for S.
+//   Q4_K (a super-block spans 8 chunks): s = the sub-block's exact dot (nibbles 0..15), S = sc * s and the min term
+//     M = m * sum(x) as exact ints, acc += dx * (d * f32(S) - dmin * f32(M)); S is what the block dot dump adds up.
 template <int FMT, int R, int MC, bool BYTES, bool STORE>
 __device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, int c, bool valid, const uint4 (&w)[R],
-                                              const float (&dw)[R], const XChunk (&xc)[MC], float (&acc)[R * MC]) {
+                                              const RowScale<FMT> (&rs)[R], const XChunk (&xc)[MC],
+                                              float (&acc)[R * MC]) {
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   const int blk = c >> Fmt<FMT>::kChunkShift;
 #pragma unroll
@@ -513,11 +565,25 @@ __device__ __forceinline__ void compute_chunk(const GemvParams& p, int64_t g, in
     if (MC == 1 || m < p.M) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const int s = chunk_dot<FMT, BYTES>(w[r], xc[m].x, xc[m].sum);
-        if (FMT != 1)  // Q4_0, Q8_0: f32(s) * dw * dx
-          acc[r * MC + m] = __fmaf_rn(__fmul_rn((float)s, dw[r]), xc[m].dx, acc[r * MC + m]);
-        else  // TQ2_0: dx * dw * f32(s)
-          acc[r * MC + m] = __fmaf_rn(__fmul_rn(xc[m].dx, dw[r]), (float)s, acc[r * MC + m]);
+        int s;
+        if constexpr (FMT == 4) {
+          int lo = 0, hi = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t wk = word_of(w[r], k);
+            lo = dp4a_ss((int)(wk & 0x0F0F0F0Fu), (int)word_of(xc[m].x[0], k), lo);
+            hi = dp4a_us(wk & 0xF0F0F0F0u, (int)word_of(xc[m].x[1], k), hi);
+          }
+          s = rs[r].sc * (lo + (hi >> 4));
+          const float t = __fsub_rn(__fmul_rn(rs[r].d, (float)s), __fmul_rn(rs[r].dmin, (float)(rs[r].mn * xc[m].sum)));
+          acc[r * MC + m] = __fmaf_rn(xc[m].dx, t, acc[r * MC + m]);
+        } else {
+          s = chunk_dot<FMT, BYTES>(w[r], xc[m].x, xc[m].sum);
+          if (FMT != 1)  // Q4_0, Q8_0: f32(s) * dw * dx
+            acc[r * MC + m] = __fmaf_rn(__fmul_rn((float)s, rs[r].d), xc[m].dx, acc[r * MC + m]);
+          else  // TQ2_0: dx * dw * f32(s)
+            acc[r * MC + m] = __fmaf_rn(__fmul_rn(xc[m].dx, rs[r].d), (float)s, acc[r * MC + m]);
+        }
         if (STORE) {  // the block dot: the partial dots of the block's chunks (adjacent lanes) added up
           int sb = s;
 #pragma unroll
@@ -691,7 +757,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
       const uint4* src = reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 32);
       o.x[0] = src[0];
       o.x[1] = src[1];
-      o.dx = Split<FMT>::xd(p)[c];
+      o.dx = Split<FMT>::xd(p)[c >> Fmt<FMT>::kChunkShift];
       if (FMT == 3) {  // no offset term; the chunk interleaved for the level lookups
         iq4nl_interleave(o.x);
         return;
@@ -742,6 +808,89 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     if (writer) {
       *reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 16) = o.x[0];
       if ((c & 1) == 0 && p.xd_out) Split<FMT>::xd_out(p)[c >> 1] = o.dx;
+    }
+    return;
+  }
+  if (FMT == 4) {
+    // q8_K for Q4_K: chunk c holds values 32c .. 32c+31 (fields: the first and last 16); the 256-value block spans
+    // the 8 chunks (threads) c & ~7 .. c | 7, so the block's signed maximum and minimum, and on a tie between signs
+    // the lowest index, are combined over those 8 threads by xor-shuffles (all lanes of the warp take part). Same
+    // arithmetic as the q8_K quantizer and the TQ2_0 prologue.
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = valid ? *reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 32 + 4 * i)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+    }
+    float mx8[8], mn8[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      mx8[t] = fmaxf(fmaxf(v[t], v[t + 8]), fmaxf(v[t + 16], v[t + 24]));
+      mn8[t] = fminf(fminf(v[t], v[t + 8]), fminf(v[t + 16], v[t + 24]));
+    }
+#pragma unroll
+    for (int n = 4; n >= 1; n >>= 1)
+#pragma unroll
+      for (int t = 0; t < n; ++t) {
+        mx8[t] = fmaxf(mx8[t], mx8[t + n]);
+        mn8[t] = fminf(mn8[t], mn8[t + n]);
+      }
+    float mx = mx8[0], mn = mn8[0];
+#pragma unroll
+    for (int off = 1; off <= 4; off <<= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    }
+    const float amax = fmaxf(fmaxf(mx, -mn), 0.0f);  // 0 for an all-zero (or all-NaN) block
+    float cand = mx >= -mn ? mx : mn;
+    const bool tie = mx == -mn && amax != 0.0f;
+    if (__any_sync(0xffffffffu, tie)) {
+      const int vb = (c & 7) * 32;  // this chunk's first value index within the block
+      int key8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        key8[t] = 0x7fffffff;
+#pragma unroll
+        for (int j = 3; j >= 0; --j)  // value t + 8j: lower j = lower index, it overrides
+          if (fabsf(v[t + 8 * j]) == amax)
+            key8[t] = ((vb + t + 8 * j) << 1) | (int)(__float_as_uint(v[t + 8 * j]) >> 31);
+      }
+#pragma unroll
+      for (int n = 4; n >= 1; n >>= 1)
+#pragma unroll
+        for (int t = 0; t < n; ++t) key8[t] = min(key8[t], key8[t + n]);
+      int key = key8[0];
+#pragma unroll
+      for (int off = 1; off <= 4; off <<= 1) key = min(key, __shfl_xor_sync(0xffffffffu, key, off));
+      if (tie) cand = (key & 1) ? -amax : amax;
+    }
+    const bool nz = amax != 0.0f;
+    const float iscale = __fdiv_rn(-127.0f, nz ? cand : 1.0f);
+    const float2 is2 = make_float2(iscale, iscale), mg2 = make_float2(12582912.0f, 12582912.0f);
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float2 p01 = __fmul2_rn(make_float2(v[4 * k], v[4 * k + 1]), is2);
+      float2 p23 = __fmul2_rn(make_float2(v[4 * k + 2], v[4 * k + 3]), is2);
+      p01 = __fadd2_rn(make_float2(fminf(p01.x, 127.0f), fminf(p01.y, 127.0f)), mg2);
+      p23 = __fadd2_rn(make_float2(fminf(p23.x, 127.0f), fminf(p23.y, 127.0f)), mg2);
+      w[k] = nz ? pack_low_bytes(__float_as_uint(p01.x), __float_as_uint(p01.y), __float_as_uint(p23.x),
+                                 __float_as_uint(p23.y))
+                : 0u;
+      sum = __dp4a((int)w[k], 0x01010101, sum);
+    }
+    if (!valid) return;
+    o.x[0] = make_uint4(w[0], w[1], w[2], w[3]);  // values 32c .. 32c+15
+    o.x[1] = make_uint4(w[4], w[5], w[6], w[7]);  // values 32c+16 .. 32c+31
+    o.sum = sum;
+    o.dx = nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
+    if (writer) {
+      uint4* dst = reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 32);
+      dst[0] = o.x[0];
+      dst[1] = o.x[1];
+      if ((c & 7) == 0 && p.xd_out) Split<FMT>::xd_out(p)[c >> 3] = o.dx;
     }
     return;
   }
@@ -1001,9 +1150,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
 
     const int c = (int)threadIdx.x + i * (int)blockDim.x;
     const bool valid = c < C;
-    float dw[R];
+    RowScale<FMT> dw[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) dw[r] = f16_bits_to_f32(cur.sc[r]);
+    for (int r = 0; r < R; ++r) dw[r].d = f16_bits_to_f32(cur.sc[r]);
     XChunk xc[MC];
     get_x<FMT, MC, XREG>(p, xs, xsum, xscale, xr, c, valid, xc);
     if (p.s)
@@ -1028,7 +1177,7 @@ template <int FMT, int R>
 __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint32_t stage, uint32_t bar,
                                             uint64_t pol) {
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const uint32_t qrow = (uint32_t)p.C * 16u, srow = (uint32_t)nblk * 2u;
+  const uint32_t qrow = (uint32_t)p.C * 16u, srow = (uint32_t)nblk * (uint32_t)Fmt<FMT>::kScaleBytes;
   const int64_t r0 = g * R;
   const int rows = (int)min((int64_t)R, p.N - r0);
   mbar_expect_tx(bar, (uint32_t)rows * (qrow + srow));
@@ -1039,7 +1188,7 @@ __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint
   } else {
     for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, wq + (r0 + r) * p.ldwq, qrow, bar, pol);
   }
-  if (p.ldws == nblk) {  // contiguous scale rows: one copy
+  if (p.ldws == (int64_t)nblk * (Fmt<FMT>::kScaleBytes / 2)) {  // contiguous scale rows: one copy
     bulk_g2s(stage + R * qrow, ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
   } else {
     for (int r = 0; r < rows; ++r) bulk_g2s(stage + R * qrow + r * srow, ws + (r0 + r) * p.ldws, srow, bar, pol);
@@ -1059,7 +1208,7 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   const int C = p.C, S = p.stages;
   const int Mx = XREG ? 0 : p.M;  // XREG: activations never touch shared memory
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
+  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * (uint32_t)Fmt<FMT>::kScaleBytes;
   uint8_t* ring = smem;                                                          // [S][stage_bytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.stage_bytes);  // [S]
   uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((S + 1) & ~1));               // 16-byte aligned
@@ -1129,15 +1278,15 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
       const bool valid = c < C;
       const int blk = c >> Fmt<FMT>::kChunkShift;
       uint4 w[R];
-      float dw[R];
+      RowScale<FMT> dw[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         if (valid) {
           w[r] = lds_v4(stage + r * qrow + (uint32_t)c * 16u);
-          dw[r] = f16_bits_to_f32(lds_u16(stage + R * qrow + r * srow + (uint32_t)blk * 2u));
+          dw[r] = row_scale_smem<FMT>(stage + R * qrow + r * srow, c);
         } else {
           w[r] = make_uint4(0u, 0u, 0u, 0u);
-          dw[r] = 0.f;
+          dw[r] = RowScale<FMT>{};
         }
       }
       XChunk xc[MC];
@@ -1187,7 +1336,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_warp_kernel(const GemvPar
   const int C = p.C, S = p.stages, W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * 2u;
+  const uint32_t qrow = (uint32_t)C * 16u, srow = (uint32_t)nblk * (uint32_t)Fmt<FMT>::kScaleBytes;
   uint8_t* ring = smem;                                                                   // [W][S][stage_bytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)W * S * p.stage_bytes);    // [W][S]
   uint8_t* xs = reinterpret_cast<uint8_t*>(bars + ((W * S + 1) & ~1));                   // 16-byte aligned
@@ -1246,15 +1395,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_warp_kernel(const GemvPar
       const bool valid = c < C;
       const int blk = c >> Fmt<FMT>::kChunkShift;
       uint4 w[R];
-      float dw[R];
+      RowScale<FMT> dw[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         if (valid) {
           w[r] = lds_v4(stage + r * qrow + (uint32_t)c * 16u);
-          dw[r] = f16_bits_to_f32(lds_u16(stage + R * qrow + r * srow + (uint32_t)blk * 2u));
+          dw[r] = row_scale_smem<FMT>(stage + R * qrow + r * srow, c);
         } else {
           w[r] = make_uint4(0u, 0u, 0u, 0u);
-          dw[r] = 0.f;
+          dw[r] = RowScale<FMT>{};
         }
       }
       XChunk xc[1];

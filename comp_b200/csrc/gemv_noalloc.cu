@@ -49,9 +49,9 @@ extern "C" int b2q_quant_gemv_splitk_noalloc(int fmt, const uint8_t* wq, int64_t
                                              const float* x, int64_t ldx, float* y, int64_t N, int64_t K, int64_t M,
                                              int splits, b2q_stream_t stream) {
   using namespace b2q;
-  if (fmt < 0 || fmt > 3)
-    return fail(B2Q_EINVAL, "b2q_quant_gemv_splitk_noalloc: fmt %d is not Q4_0 (0), TQ2_0 (1), Q8_0 (2) or IQ4_NL (3)",
-                fmt);
+  if (fmt < 0 || fmt > 4)
+    return fail(B2Q_EINVAL,
+                "b2q_quant_gemv_splitk_noalloc: fmt %d is not Q4_0 (0), TQ2_0 (1), Q8_0 (2), IQ4_NL (3) or Q4_K (4)", fmt);
   if (splits >= 2 && N > 0 && M > 0 && (size_t)splits * (size_t)M * (size_t)N * sizeof(float) > kStaticScratchBytes)
     return fail(B2Q_ERANGE,
                 "b2q_quant_gemv_splitk_noalloc: %d splits x M=%lld x N=%lld partial sums exceed the %zu-byte "

@@ -23,6 +23,7 @@ static KernelFn pick(int R, int MC) {
 
 KernelFn reg_kernel_for(int fmt, bool bytes, int R, int MC, bool xreg) {
   if (MC != 1) xreg = false;
+  if (fmt == 4) return nullptr;  // Q4_K runs on the TMA ring only
   if (fmt == 0) {
     if (bytes) return xreg ? pick<0, true, true>(R, MC) : pick<0, true, false>(R, MC);
     return xreg ? pick<0, false, true>(R, MC) : pick<0, false, false>(R, MC);

@@ -27,6 +27,7 @@ KernelFn ring_kernel_for(int fmt, int R, int MC, bool xreg) {
   if (fmt == 0) return xreg ? pick<0, true>(R, MC) : pick<0, false>(R, MC);
   if (fmt == 2) return xreg ? pick<2, true>(R, MC) : pick<2, false>(R, MC);
   if (fmt == 3) return xreg ? pick<3, true>(R, MC) : pick<3, false>(R, MC);
+  if (fmt == 4) return xreg ? pick<4, true>(R, MC) : pick<4, false>(R, MC);
   return xreg ? pick<1, true>(R, MC) : pick<1, false>(R, MC);
 }
 

@@ -23,7 +23,7 @@ KernelFn warp_kernel_for(int fmt, int R) {
       case 2: return gemv_warp_kernel<3, 2>;
       case 4: return gemv_warp_kernel<3, 4>;
     }
-  } else {
+  } else if (fmt == 1) {
     switch (R) {
       case 1: return gemv_warp_kernel<1, 1>;
       case 2: return gemv_warp_kernel<1, 2>;

@@ -82,7 +82,7 @@ static int mapped(const char* who, const char* what, const void* host, void** de
 }  // namespace b2q
 
 extern "C" size_t b2q_pinned_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
-  if (fmt < 0 || fmt > 3 || N <= 0 || K <= 0 || M <= 0) return 0;
+  if (fmt < 0 || fmt > 4 || N <= 0 || K <= 0 || M <= 0) return 0;
   return b2q::align256((size_t)M * (size_t)K * sizeof(float)) + b2q_workspace_size(fmt, N, K, M);
 }
 
@@ -91,8 +91,8 @@ extern "C" int b2q_quant_gemv_pinned(int fmt, const uint8_t* wq, int64_t ldwq, c
                                      size_t workspace_bytes, b2q_stream_t stream) {
   using namespace b2q;
   static const char* who = "b2q_quant_gemv_pinned";
-  if (fmt < 0 || fmt > 3)
-    return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1), Q8_0 (2) or IQ4_NL (3)", who, fmt);
+  if (fmt < 0 || fmt > 4)
+    return fail(B2Q_EINVAL, "%s: fmt %d is not Q4_0 (0), TQ2_0 (1), Q8_0 (2), IQ4_NL (3) or Q4_K (4)", who, fmt);
   if (N < 0 || K < 0 || M < 0) return fail(B2Q_EINVAL, "%s: negative size", who);
   if (N == 0 || M == 0) return B2Q_OK;  // empty output: nothing is touched
   void* y_dev = nullptr;

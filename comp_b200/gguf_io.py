@@ -1,4 +1,5 @@
-"""GGUF weight ingest: a Q4_0 / TQ2_0 / Q8_0 / IQ4_NL tensor of a GGUF file -> the GEMV's split planes in GPU memory.
+"""GGUF weight ingest: a Q4_0 / TQ2_0 / Q8_0 / IQ4_NL / Q4_K tensor of a GGUF file -> the GEMV's split planes in GPU
+memory.
 
 The tensor's bytes are copied to the GPU as stored (ggml blocks, row after row) and cut into WQ / WS there
 (`host.split_device`, the on-device form of `host.split`, src/komp/host.py:16-22). GGUF lists a 2-D weight's shape as
@@ -10,7 +11,7 @@ import torch
 
 from . import host
 
-GGUF_TYPES = {"Q4_0": "q4_0", "TQ2_0": "tq2_0", "Q8_0": "q8_0", "IQ4_NL": "iq4_nl"}
+GGUF_TYPES = {"Q4_0": "q4_0", "TQ2_0": "tq2_0", "Q8_0": "q8_0", "IQ4_NL": "iq4_nl", "Q4_K": "q4_k"}
 
 
 def tensor_info(reader, name):

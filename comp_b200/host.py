@@ -16,20 +16,22 @@ import torch
 
 from . import _lib
 
-# weights: block values, block bytes, quant offset/bytes in the ggml block, scale offset, activation format
-# (q4_0 and tq2_0: the same table as src/komp/host.py:9-12; q8_0 and iq4_nl are extensions beyond the reference,
-# ggml block_q8_0 / block_iq4_nl weights multiplied against q8_0 activations)
+# weights: block values, block bytes, quant offset/bytes in the ggml block, scale offset, int16s of the scale plane
+# per block, activation format (q4_0 and tq2_0: the same table as src/komp/host.py:9-12; q8_0, iq4_nl and q4_k are
+# extensions beyond the reference: ggml block_q8_0 / block_iq4_nl weights against q8_0 activations, block_q4_K
+# super-blocks against q8_K activations, split by split_q4_k into this backend's own planes)
 FORMATS = {
-    "q4_0": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
-    "tq2_0": dict(block=256, nbytes=66, qoff=0, qbytes=64, soff=64, act="q8_K"),
-    "q8_0": dict(block=32, nbytes=34, qoff=2, qbytes=32, soff=0, act="q8_0"),
-    "iq4_nl": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, act="q8_0"),
+    "q4_0": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, sshorts=1, act="q8_0"),
+    "tq2_0": dict(block=256, nbytes=66, qoff=0, qbytes=64, soff=64, sshorts=1, act="q8_K"),
+    "q8_0": dict(block=32, nbytes=34, qoff=2, qbytes=32, soff=0, sshorts=1, act="q8_0"),
+    "iq4_nl": dict(block=32, nbytes=18, qoff=2, qbytes=16, soff=0, sshorts=1, act="q8_0"),
+    "q4_k": dict(block=256, nbytes=144, qoff=16, qbytes=128, soff=0, sshorts=10, act="q8_K"),
 }
 MODES = {"bytes": 0, "dp4a": 2}  # src/komp/host.py:13
 ACT_BLOCK = {"q8_0": 32, "q8_K": 256}
-FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}
+FMT_ID = {"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3, "q4_k": 4}
 GEMV_ENTRY = {"q4_0": "b2q_gemv_q4_0", "tq2_0": "b2q_gemv_tq2_0", "q8_0": "b2q_gemv_q8_0",
-              "iq4_nl": "b2q_gemv_iq4_nl"}
+              "iq4_nl": "b2q_gemv_iq4_nl", "q4_k": "b2q_gemv_q4_k"}
 
 
 def _fmt(fmt):
@@ -44,7 +46,8 @@ def _fmt(fmt):
 
 
 def split(fmt, W, n, k):
-    """ggml blocks (bytes, n rows of k values) -> (WQ uint8 [n][quant bytes per row], WS int16 [n][k/block])."""
+    """ggml blocks (bytes, n rows of k values) -> (WQ uint8 [n][quant bytes per row], WS int16 [n][k/block])
+    (q4_k: WS int16 [n][k/256 * 10], see split_q4_k)."""
     f = _fmt(fmt)
     if k % f["block"]:
         raise ValueError(f"k={k} is not a multiple of the {fmt} block ({f['block']})")
@@ -53,9 +56,35 @@ def split(fmt, W, n, k):
     if raw.size != n * nb * f["nbytes"]:
         raise ValueError(f"{raw.size} bytes do not hold {n} x {nb} {fmt} blocks of {f['nbytes']} bytes")
     blocks = raw.reshape(n, nb, f["nbytes"])
+    if fmt == "q4_k":
+        return split_q4_k(blocks)
     wq = blocks[:, :, f["qoff"] : f["qoff"] + f["qbytes"]].reshape(n, nb * f["qbytes"]).copy()
     ws = blocks[:, :, f["soff"] : f["soff"] + 2].copy().view(np.int16).reshape(n, nb)
     return wq, ws
+
+
+def split_q4_k(blocks):
+    """ggml block_q4_K uint8 [n][nb][144] (f16 d, f16 dmin, 12 bytes of packed 6-bit scales and mins, 128 nibble
+    bytes) -> this backend's planes (WQ uint8 [n][nb*128], WS int16 [n][nb*10]):
+      WQ: per 32-value sub-block j one 16-byte chunk laid out like a Q4_0 block, byte i holding value i (low nibble)
+          and value i + 16 (high nibble); in the ggml block byte i of the 32-byte group g holds value i of sub-block
+          2g (low nibble) and of sub-block 2g + 1 (high nibble);
+      WS: per super-block 20 bytes: d, dmin (f16 bits), then the unpacked bytes sc_0, m_0, ..., sc_7, m_7 (ggml's
+          6-bit fields: j < 4 in the low 6 bits of scale bytes j (sc) and 4 + j (m); j >= 4 in the nibbles of byte
+          8 + (j - 4) for the low 4 bits and the top 2 bits of bytes j - 4 (sc) and j (m))."""
+    n, nb = blocks.shape[:2]
+    qs = blocks[:, :, 16:].reshape(n, nb, 4, 32)
+    sub = np.stack([qs & 0x0F, qs >> 4], axis=3).reshape(n, nb, 8, 32)  # sub-block 2g + h: nibble h of group g
+    wq = (sub[..., :16] | (sub[..., 16:] << 4)).astype(np.uint8).reshape(n, nb * 128)
+    p = blocks[:, :, 4:16]
+    lo, mid, top = p[..., 0:4], p[..., 4:8], p[..., 8:12]
+    sc = np.concatenate([lo & 0x3F, (top & 0x0F) | ((lo >> 2) & 0x30)], axis=-1)
+    mn = np.concatenate([mid & 0x3F, (top >> 4) | ((mid >> 2) & 0x30)], axis=-1)
+    rec = np.empty((n, nb, 20), dtype=np.uint8)
+    rec[:, :, 0:4] = blocks[:, :, 0:4]
+    rec[:, :, 4::2] = sc
+    rec[:, :, 5::2] = mn
+    return np.ascontiguousarray(wq), np.ascontiguousarray(rec.reshape(n, nb * 20)).view(np.int16)
 
 
 def split_q4_0(W, n, k):
@@ -80,7 +109,7 @@ def split_device(fmt, blocks, n, k, ldwq=None):
     qb = nb * f["qbytes"]
     ldwq = qb if ldwq is None else ldwq
     wq = torch.empty((n, ldwq), dtype=torch.uint8, device=dev)
-    ws = torch.empty((n, nb), dtype=torch.int16, device=dev)
+    ws = torch.empty((n, nb * f["sshorts"]), dtype=torch.int16, device=dev)
     with _on(dev):
         _lib.call("b2q_split_blocks", FMT_ID[fmt], blocks.data_ptr(), n, k, wq.data_ptr(), ldwq, ws.data_ptr(),
                   _stream(dev))
@@ -219,7 +248,7 @@ def _check_weights(fmt, wq, ws, n, k):
             (wq.numel() and wq.stride(1) != 1):
         raise ValueError(f"gemv: wq must be uint8 [{n}][>= {qbytes}] with unit column stride, got {wq.dtype} "
                          f"{tuple(wq.shape)}")
-    _check(ws, "ws", torch.int16, (n, k // f["block"]))
+    _check(ws, "ws", torch.int16, (n, k // f["block"] * f["sshorts"]))
     if ws.numel() and not ws.is_contiguous():
         raise ValueError("gemv: ws must be contiguous")
 

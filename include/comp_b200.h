@@ -48,6 +48,7 @@ typedef struct CUstream_st* b2q_stream_t;
 #define B2Q_FMT_TQ2_0 1
 #define B2Q_FMT_Q8_0 2 /* extension: ggml block_q8_0 weights (no counterpart in the reference) */
 #define B2Q_FMT_IQ4_NL 3 /* extension: ggml block_iq4_nl weights, GEMV path only (no counterpart in the reference) */
+#define B2Q_FMT_Q4_K 4   /* extension: ggml block_q4_K weights, GEMV path only (no counterpart in the reference) */
 #define B2Q_VARIANT_BYTES 0
 #define B2Q_VARIANT_DP4A 2
 
@@ -126,6 +127,24 @@ int b2q_gemv_iq4_nl(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const in
                     int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
 
 /*
+ * Q4_K x q8_K decode GEMV. A third extension beyond the reference: ggml block_q4_K super-blocks of 256 values, eight
+ * 32-value sub-blocks with 6-bit scales sc_j and mins m_j, value = d * sc_j * q - dmin * m_j (q = 0..15), against
+ * q8_K activations (the TQ2_0 activation planes). This backend's split planes (host.split("q4_k") and
+ * b2q_split_blocks fmt 4 make them from the ggml blocks):
+ *   wq: u8 [N][ldwq], 128 bytes per super-block: sub-block j as one 16-byte chunk laid out like a Q4_0 block (byte
+ *       i: value 32j+i in the low nibble, value 32j+16+i in the high nibble);
+ *   ws: int16 [N][K/256 * 10], 20 bytes per super-block: f16 d, f16 dmin, then the bytes sc_0, m_0, ..., sc_7, m_7;
+ *   xq: int8 [M][K], xd: f32 [M][K/256], y: f32 [M][N], s: int32 [M][N][K/256] or NULL.
+ * Y[m][n] = sum over sub-blocks of dx * (d * f32(sc_j * q.x) - dmin * f32(m_j * sum(x))); the integer parts are
+ * exact, s[m][n][b] = sum_j sc_j * (q.x over sub-block j). K must be a multiple of 1024 and ws 16-byte aligned (the
+ * scale records travel with the weights through the TMA ring, in whole 16-byte units); variant is ignored (one
+ * kernel). Every fused, split-K, pinned, no-alloc and multi-GPU entry takes fmt B2Q_FMT_Q4_K; 8+ columns stay on the
+ * GEMV path. No reference counterpart (COMP has Q4_0 and TQ2_0 only).
+ */
+int b2q_gemv_q4_k(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd, float* y,
+                  int32_t* s, int64_t N, int64_t K, int64_t M, int variant, b2q_stream_t stream);
+
+/*
  * Fused quantizer prologue + GEMV (one launch): every CTA quantizes f32 x into shared memory with exactly the math of
  * b2q_quant_q8_0 / b2q_quant_q8_K, then runs the GEMV. xq/xd (nullable) also receive the quantized activations
  * (written by CTA 0 only), byte-identical to the standalone quantizer. fmt = B2Q_FMT_Q4_0, B2Q_FMT_TQ2_0 or B2Q_FMT_Q8_0.
@@ -196,8 +215,9 @@ int b2q_stage_pinned(const float* x_host, int64_t ldx, float* stage, int64_t M, 
 
 /*
  * ggml blocks -> split planes on the device (model load path). blocks: n rows of k values as ggml Q4_0 (fmt 0,
- * 18-byte blocks: f16 d, 16 quant bytes), TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d) or Q8_0 (fmt 2,
- * 34-byte blocks: f16 d, 32 int8), row-major,
+ * 18-byte blocks: f16 d, 16 quant bytes), TQ2_0 (fmt 1, 66-byte blocks: 64 quant bytes, f16 d), Q8_0 (fmt 2,
+ * 34-byte blocks: f16 d, 32 int8), IQ4_NL (fmt 3, as Q4_0) or Q4_K (fmt 4, 144-byte blocks -> the planes described at
+ * b2q_gemv_q4_k: WS then holds 20 bytes per block and must be 16-byte aligned), row-major,
  * 16-byte aligned device memory (a GGUF tensor's bytes as stored). Writes WQ [n][ldwq] (ldwq >= quant bytes per row,
  * multiple of 16) and WS [n][k/blk] int16 (f16 bits), exactly host.split's planes. Replaces the host-side numpy cut
  * of src/komp/host.py:16-22 for weights already on the GPU.

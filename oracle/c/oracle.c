@@ -150,11 +150,57 @@ static int32_t dot_iq4_nl(const uint8_t* q, const int8_t* x) {
 }
 
 /*
+ * One Q4_K super-block in the split planes (an extension, pinned to gguf-py's Q4_K codec): 128 quant bytes, one
+ * 16-byte chunk per 32-value sub-block j laid out as a Q4_0 block (nibbles 0..15, no offset), and the 20-byte scale
+ * record (f16 d, f16 dmin, then the bytes sc_j, m_j). *S = sum_j sc_j * dot_j (exact), *MN = sum_j m_j * sum(x_j).
+ */
+static void dot_q4_k(const uint8_t* q, const uint8_t* rec, const int8_t* x, int32_t* S, int32_t* MN) {
+  int32_t st = 0, mt = 0;
+  for (int j = 0; j < 8; ++j) {
+    int32_t d = 0, sx = 0;
+    for (int i = 0; i < 16; ++i) {
+      d += (int32_t)(q[16 * j + i] & 15) * x[32 * j + i] + (int32_t)(q[16 * j + i] >> 4) * x[32 * j + i + 16];
+      sx += x[32 * j + i] + x[32 * j + i + 16];
+    }
+    st += (int32_t)rec[4 + 2 * j] * d;
+    mt += (int32_t)rec[5 + 2 * j] * sx;
+  }
+  *S = st;
+  *MN = mt;
+}
+
+/*
  * y[m][n] = KURN reference dot (f64, sequential over blocks; q4_0 / q8_0 / iq4_nl: (dw*dx)*s, tq2_0: (dx*dw)*s, dx of
  * q8_0 activations read back as its f16), s (nullable) = int32 block dots [M][N][nb]. fmt: 0 Q4_0, 1 TQ2_0, 2 Q8_0,
- * 3 IQ4_NL.
+ * 3 IQ4_NL, 4 Q4_K (ws: 20-byte records, row stride nb * 10; y = sum over super-blocks of dx * (d * S - dmin * MN)
+ * in f64, s = S).
  * nthreads <= 0 uses the OpenMP default.
  */
+static void orc_gemv_q4_k(const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd,
+                          int64_t N, int64_t K, int64_t M, double* y, int32_t* s) {
+  const int64_t nb = K / 256;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    const uint8_t* row = wq + n * ldwq;
+    const uint8_t* recs = (const uint8_t*)(ws + n * nb * 10);
+    for (int64_t m = 0; m < M; ++m) {
+      double total = 0.0;
+      for (int64_t b = 0; b < nb; ++b) {
+        int32_t S, MN;
+        const uint8_t* rec = recs + b * 20;
+        dot_q4_k(row + b * 128, rec, xq + m * K + b * 256, &S, &MN);
+        if (s) s[(m * N + n) * nb + b] = S;
+        uint16_t dh, mh;
+        memcpy(&dh, rec, 2);
+        memcpy(&mh, rec + 2, 2);
+        const double d = (double)orc_half_to_float(dh), dmin = (double)orc_half_to_float(mh);
+        total += (double)xd[m * nb + b] * (d * (double)S - dmin * (double)MN);
+      }
+      y[m * N + n] = total;
+    }
+  }
+}
+
 void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const int8_t* xq, const float* xd,
               int64_t N, int64_t K, int64_t M, double* y, int32_t* s, int nthreads) {
   const int blk = fmt == 1 ? 256 : 32;
@@ -165,6 +211,10 @@ void orc_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const
 #else
   (void)nthreads;
 #endif
+  if (fmt == 4) {
+    orc_gemv_q4_k(wq, ldwq, ws, xq, xd, N, K, M, y, s);
+    return;
+  }
 #pragma omp parallel for schedule(static)
   for (int64_t n = 0; n < N; ++n) {
     const uint8_t* row = wq + n * ldwq;

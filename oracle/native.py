@@ -64,10 +64,10 @@ def gemv(fmt, wq, ws, xq, xd, k, want_s=False, threads=0):
     xq = np.ascontiguousarray(xq, dtype=np.int8)
     xd = np.ascontiguousarray(xd, dtype=np.float32)
     n, m = wq.shape[0], xq.shape[0]
-    nb = k // (256 if fmt == "tq2_0" else 32)
+    nb = k // (256 if fmt in ("tq2_0", "q4_k") else 32)
     y = np.empty((m, n), np.float64)
     s = np.empty((m, n, nb), np.int32) if want_s else None
-    load().orc_gemv({"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3}[fmt], _p(wq), wq.shape[1], _p(ws), _p(xq), _p(xd), n, k, m, _p(y),
+    load().orc_gemv({"q4_0": 0, "tq2_0": 1, "q8_0": 2, "iq4_nl": 3, "q4_k": 4}[fmt], _p(wq), wq.shape[1], _p(ws), _p(xq), _p(xd), n, k, m, _p(y),
                     _p(s) if want_s else None, threads)
     return y, s
 

@@ -12,12 +12,18 @@ import numpy as np
 # iq4_nl weights are a second extension: ggml's IQ4_NL block (f16 scale, 16 bytes of nibbles laid out as Q4_0's) whose
 # nibbles index a fixed table of 16 int8 levels instead of nibble - 8; q8_0 activations and Q4_0's multiply order;
 # pinned to gguf-py's IQ4_NL codec.
-BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32}
-ACT = {"q4_0": "q8_0", "tq2_0": "q8_K", "q8_0": "q8_0", "iq4_nl": "q8_0"}
-QBYTES = {"q4_0": 16, "tq2_0": 64, "q8_0": 32, "iq4_nl": 16}
-NBYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18}
+# q4_k weights are a third extension: ggml's Q4_K super-block of 256 values (f16 d and dmin, eight 6-bit sub-block
+# scales and mins packed in 12 bytes, 128 bytes of nibbles), value = d * sc_j * q - dmin * m_j for sub-block j of 32
+# values, against q8_K activations; pinned to gguf-py's Q4_K codec. Its split planes are this backend's own layout
+# (split_q4_k below): nibbles regrouped so each 16-byte chunk holds one sub-block laid out as a Q4_0 block, and the
+# scales unpacked to 20 bytes per super-block.
+BLOCK = {"q4_0": 32, "tq2_0": 256, "q8_0": 32, "iq4_nl": 32, "q4_k": 256}
+ACT = {"q4_0": "q8_0", "tq2_0": "q8_K", "q8_0": "q8_0", "iq4_nl": "q8_0", "q4_k": "q8_K"}
+QBYTES = {"q4_0": 16, "tq2_0": 64, "q8_0": 32, "iq4_nl": 16, "q4_k": 128}
+NBYTES = {"q4_0": 18, "tq2_0": 66, "q8_0": 34, "iq4_nl": 18, "q4_k": 144}
 QOFF = {"q4_0": 2, "tq2_0": 0, "q8_0": 2, "iq4_nl": 2}
 SOFF = {"q4_0": 0, "tq2_0": 64, "q8_0": 0, "iq4_nl": 0}
+Q4K_SCALE_BYTES = 20  # split scale plane per super-block: f16 d, f16 dmin, (sc_j, m_j) bytes for j = 0..7
 # ggml's IQ4_NL levels (kvalues_iq4nl), the codebook of the format
 IQ4_NL_LEVELS = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], dtype=np.int8)
 TOL = 1e-5  # KURN's relative-error rule for the f32 GEMV output (src/komp/verify.py:28)
@@ -146,7 +152,119 @@ def decode_iq4_nl(wq, k):
 
 
 def decode(fmt, wq, k):
-    return {"q4_0": decode_q4_0, "tq2_0": decode_tq2_0, "q8_0": decode_q8_0, "iq4_nl": decode_iq4_nl}[fmt](wq, k)
+    return {"q4_0": decode_q4_0, "tq2_0": decode_tq2_0, "q8_0": decode_q8_0, "iq4_nl": decode_iq4_nl,
+            "q4_k": decode_q4_k_quants}[fmt](wq, k)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Q4_K (extension): ggml block_q4_K <-> this backend's split planes
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def q4_k_scale_min(scales):
+    """12 packed bytes per super-block [..][12] -> (sc, m) uint8 [..][8]: sub-blocks 0-3 take the low 6 bits of bytes
+    0-3 (scales) and 4-7 (mins); sub-blocks 4-7 take the nibbles of bytes 8-11 as their low 4 bits and the top 2 bits
+    of bytes 0-3 / 4-7 as their high 2 bits (ggml get_scale_min_k4)."""
+    b = np.asarray(scales, dtype=np.uint8)
+    d, m, md = b[..., 0:4], b[..., 4:8], b[..., 8:12]
+    sc = np.concatenate([d & 0x3F, (md & 0x0F) | ((d >> 2) & 0x30)], axis=-1)
+    mn = np.concatenate([m & 0x3F, (md >> 4) | ((m >> 2) & 0x30)], axis=-1)
+    return sc.astype(np.uint8), mn.astype(np.uint8)
+
+
+def q4_k_pack_scale_min(sc, mn):
+    """Inverse of q4_k_scale_min: 6-bit (sc, m) [..][8] -> 12 packed bytes [..][12]."""
+    sc = np.asarray(sc, dtype=np.uint8)
+    mn = np.asarray(mn, dtype=np.uint8)
+    d = (sc[..., :4] & 0x3F) | ((sc[..., 4:] >> 4) << 6)
+    m = (mn[..., :4] & 0x3F) | ((mn[..., 4:] >> 4) << 6)
+    md = (sc[..., 4:] & 0x0F) | ((mn[..., 4:] & 0x0F) << 4)
+    return np.concatenate([d, m, md], axis=-1).astype(np.uint8)
+
+
+def split_q4_k(W, n, k):
+    """ggml Q4_K blocks (144 bytes: f16 d, f16 dmin, 12 scale bytes, 128 nibble bytes) -> (WQ uint8 [n][k/2],
+    WS int16 [n][k/256 * 10]). WQ: per sub-block j of 32 values one 16-byte chunk laid out as a Q4_0 block (byte i:
+    value i in the low nibble, value i + 16 in the high nibble); in the ggml block, byte i of 32-byte group g holds
+    value i of sub-block 2g (low nibble) and of sub-block 2g + 1 (high nibble). WS: per super-block 20 bytes: d, dmin
+    (f16 bits), then (sc_j, m_j) for j = 0..7."""
+    nb = k // 256
+    b = np.frombuffer(W, dtype=np.uint8).reshape(n, nb, 144)
+    qs = b[:, :, 16:].reshape(n, nb, 4, 32)
+    q = np.stack([qs & 0x0F, qs >> 4], axis=3).reshape(n, nb, 8, 32)  # sub-block 2g + h = nibble h of group g
+    chunk = (q[..., :16] | (q[..., 16:] << 4)).astype(np.uint8)       # [n][nb][8][16]
+    wq = np.ascontiguousarray(chunk.reshape(n, nb * 128))
+    sc, mn = q4_k_scale_min(b[:, :, 4:16])
+    rec = np.zeros((n, nb, Q4K_SCALE_BYTES), dtype=np.uint8)
+    rec[:, :, 0:4] = b[:, :, 0:4]
+    rec[:, :, 4::2] = sc
+    rec[:, :, 5::2] = mn
+    return wq, np.ascontiguousarray(rec.reshape(n, nb * Q4K_SCALE_BYTES)).view(np.int16)
+
+
+def q4_k_parts(wq, ws, k):
+    """Split planes -> (q uint8 [n][k] nibbles in value order, d f32 [n][nb], dmin f32 [n][nb], sc [n][nb][8],
+    m [n][nb][8])."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    n, nb = wq.shape[0], k // 256
+    c = wq[:, : k // 2].reshape(n, k // 32, 16)
+    q = np.concatenate([c & 15, c >> 4], axis=-1).reshape(n, k)
+    rec = np.ascontiguousarray(np.asarray(ws, dtype=np.int16)).view(np.uint8).reshape(n, nb, Q4K_SCALE_BYTES)
+    d = rec[:, :, 0:2].copy().view(np.float16)[..., 0].astype(F32)
+    dmin = rec[:, :, 2:4].copy().view(np.float16)[..., 0].astype(F32)
+    return q, d, dmin, rec[:, :, 4::2], rec[:, :, 5::2]
+
+
+def decode_q4_k_quants(wq, k):
+    """Q4_K split quant plane -> the nibbles (0..15) in value order, int8 [n][k] (the integer part of the dots)."""
+    wq = np.asarray(wq, dtype=np.uint8)
+    n = wq.shape[0]
+    c = wq[:, : k // 2].reshape(n, k // 32, 16)
+    return np.concatenate([c & 15, c >> 4], axis=-1).reshape(n, k).astype(np.int8)
+
+
+def decode_q4_k(wq, ws, k):
+    """Q4_K split planes -> f32 weight values [n][k] = (d * sc_j) * q - dmin * m_j in f32, gguf-py's dequantize
+    arithmetic (so equal bit for bit)."""
+    q, d, dmin, sc, mn = q4_k_parts(wq, ws, k)
+    n, nb = d.shape
+    ds = (d[..., None] * sc.astype(F32)).astype(F32)        # [n][nb][8]
+    dm = (dmin[..., None] * mn.astype(F32)).astype(F32)
+    v = (ds[..., None] * q.reshape(n, nb, 8, 32).astype(F32) - dm[..., None]).astype(F32)
+    return v.reshape(n, k)
+
+
+def q4_k_idots(wq, ws, xq, k):
+    """Exact integer parts of the Q4_K dot per super-block, int64 [M][N][K/256] each: S = sum_j sc_j * sum_i q_i x_i
+    (the block dot the kernels dump) and Mn = sum_j m_j * sum_i x_i (the min term)."""
+    q, _, _, sc, mn = q4_k_parts(wq, ws, k)
+    n, nb = sc.shape[0], k // 256
+    xq = np.asarray(xq).astype(np.int64)
+    m = xq.shape[0]
+    if n == 0 or m == 0 or nb == 0:
+        z = np.zeros((m, n, nb), np.int64)
+        return z, z.copy()
+    qv = q.reshape(n, nb * 8, 32).astype(np.float64).transpose(1, 0, 2)      # [sb][n][32]
+    xv = xq.reshape(m, nb * 8, 32).astype(np.float64).transpose(1, 2, 0)     # [sb][32][m]
+    sub = np.rint(np.matmul(qv, xv)).astype(np.int64).transpose(2, 1, 0)     # [m][n][sb]
+    sub = sub.reshape(m, n, nb, 8)
+    s = (sub * sc[None].astype(np.int64)).sum(-1)
+    sx = xq.reshape(m, nb, 8, 32).sum(-1)                                   # [m][nb][8]
+    mnt = (sx[:, None] * mn[None].astype(np.int64)).sum(-1)
+    return s, mnt
+
+
+def q4_k_reference(ws, xd, s, mnt, k):
+    """f64 reference per output: sequential over super-blocks of dx * (d * S - dmin * Mn) -> f64 [M][N]."""
+    n = np.asarray(ws).shape[0]
+    _, d, dmin, _, _ = q4_k_parts(np.zeros((n, k // 2), np.uint8), ws, k)
+    dx = np.asarray(xd, dtype=np.float32).astype(np.float64)
+    m, _, nb = s.shape
+    total = np.zeros((m, n), np.float64)
+    for b in range(nb):
+        total += dx[:, None, b] * (d[None, :, b].astype(np.float64) * s[:, :, b] -
+                                   dmin[None, :, b].astype(np.float64) * mnt[:, :, b])
+    return total
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -192,7 +310,11 @@ def reference_dot(fmt, ws, xd, s):
 
 
 def gemv(fmt, wq, ws, xq, xd, k):
-    """-> (reference f64 [M][N], exact block dots int64 [M][N][nb]) for the GEMV of src/komp/kernels.py:48-142."""
+    """-> (reference f64 [M][N], exact block dots int64 [M][N][nb]) for the GEMV of src/komp/kernels.py:48-142
+    (q4_k: the block dots are S = sum_j sc_j * dot_j; the reference adds the min term)."""
+    if fmt == "q4_k":
+        s, mnt = q4_k_idots(wq, ws, xq, k)
+        return q4_k_reference(ws, xd, s, mnt, k), s
     s = idots(fmt, wq, xq, k)
     return reference_dot(fmt, ws, xd, s), s
 
@@ -239,6 +361,8 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
              the largest normal f16 below 2^8 and negative scales."""
     blk = BLOCK[fmt]
     nb = k // blk
+    if fmt == "q4_k":
+        return q4_k_blocks(rng, n, k, extreme)
     out = np.zeros((n, nb, NBYTES[fmt]), dtype=np.uint8)
     if fmt in ("q4_0", "iq4_nl"):
         if extreme:
@@ -268,6 +392,34 @@ def weight_blocks(fmt, rng, n, k, extreme=False):
     qoff, soff = QOFF[fmt], SOFF[fmt]
     out[:, :, qoff : qoff + QBYTES[fmt]] = q
     out[:, :, soff : soff + 2] = d.view(np.uint8).reshape(n, nb, 2)
+    return out.tobytes()
+
+
+def q4_k_blocks(rng, n, k, extreme=False):
+    """ggml Q4_K blocks: nibbles uniform 0..15, 6-bit scales and mins uniform 0..63, d = f16(|N(0, 0.002)|), dmin =
+    f16(|N(0, 0.004)|). extreme: nibbles 0 or 15, scales and mins 0 or 63, d and dmin including 0 and f16 extremes."""
+    nb = k // 256
+    out = np.zeros((n, nb, 144), dtype=np.uint8)
+    if extreme:
+        q = rng.choice(np.array([0, 15], dtype=np.uint8), size=(n, nb, 8, 32))
+        sc = rng.choice(np.array([0, 63], dtype=np.uint8), size=(n, nb, 8))
+        mn = rng.choice(np.array([0, 63], dtype=np.uint8), size=(n, nb, 8))
+    else:
+        q = rng.integers(0, 16, size=(n, nb, 8, 32), dtype=np.uint8)
+        sc = rng.integers(0, 64, size=(n, nb, 8), dtype=np.uint8)
+        mn = rng.integers(0, 64, size=(n, nb, 8), dtype=np.uint8)
+    d = np.abs(rng.normal(0.0, 0.002, size=(n, nb))).astype(np.float16)
+    dmin = np.abs(rng.normal(0.0, 0.004, size=(n, nb))).astype(np.float16)
+    if extreme and n * nb:
+        for arr in (d, dmin):
+            flat = arr.reshape(-1)
+            pick = rng.choice(flat.size, size=min(flat.size, 4), replace=False)
+            flat[pick] = np.array([0.0, 6e-8, 65504.0, 2.0 ** -14], dtype=np.float16)[: pick.size]
+    out[:, :, 0:2] = d.view(np.uint8).reshape(n, nb, 2)
+    out[:, :, 2:4] = dmin.view(np.uint8).reshape(n, nb, 2)
+    out[:, :, 4:16] = q4_k_pack_scale_min(sc, mn)
+    g = q.reshape(n, nb, 4, 2, 32)
+    out[:, :, 16:] = (g[:, :, :, 0] | (g[:, :, :, 1] << 4)).reshape(n, nb, 128)
     return out.tobytes()
 
 
@@ -329,7 +481,9 @@ def problem(fmt, n, k, m, seed=0, extreme=False):
 
 
 def split(fmt, W, n, k):
-    """ggml blocks -> (WQ uint8 [n][qbytes*k/blk], WS int16 [n][k/blk]) (src/komp/host.py:16-22)."""
+    """ggml blocks -> (WQ uint8 [n][qbytes*k/blk], WS int16 [n][k/blk]) (src/komp/host.py:16-22); q4_k: split_q4_k."""
+    if fmt == "q4_k":
+        return split_q4_k(W, n, k)
     blk = BLOCK[fmt]
     b = np.frombuffer(W, dtype=np.uint8).reshape(n, k // blk, NBYTES[fmt])
     qoff, soff = QOFF[fmt], SOFF[fmt]
@@ -342,6 +496,8 @@ def random_split(fmt, rng, n, k):
     """Split planes directly (fast path for large synthetic layers): same distributions as weight_blocks."""
     blk = BLOCK[fmt]
     nb = k // blk
+    if fmt == "q4_k":
+        return split_q4_k(q4_k_blocks(rng, n, k), n, k)
     if fmt in ("q4_0", "iq4_nl"):
         wq = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
         d = np.abs(rng.normal(0.0, 0.02 if fmt == "q4_0" else 0.002, size=(n, nb))).astype(np.float16)

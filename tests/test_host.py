@@ -44,8 +44,11 @@ def test_library_metadata_calls_need_no_gpu():
     # the newer entry points validate on the host too, before any CUDA call
     with pytest.raises(ValueError, match="multiple"):
         _lib.call("b2q_gemv_iq4_nl", 16, 16, 16, 16, 16, 16, None, 4, 100, 1, 2, None)
+    # Q4_K: K a multiple of 256 but not of 1024 (its scale records would not fill whole 16-byte units)
+    with pytest.raises(ValueError, match="Q4_K needs K a multiple of 1024"):
+        _lib.call("b2q_gemv_q4_k", 16, 384, 16, 16, 16, 16, None, 4, 768, 1, 2, None)
     assert lib.b2q_quant_gemv_pinned(9, None, 0, None, None, 0, None, 4, 64, 1, None, 0, None) == -1
-    assert "IQ4_NL (3)" in _lib.last_error()
+    assert "Q4_K (4)" in _lib.last_error()
     assert lib.b2q_quant_gemv_pinned(0, None, 0, None, None, 0, None, -1, 64, 1, None, 0, None) == -1
     assert lib.b2q_quant_gemv_pinned(0, None, 0, None, None, 0, None, 0, 64, 1, None, 0, None) == 0  # empty: no-op
     assert lib.b2q_stage_pinned(None, 0, None, -1, 64, None) == -1

@@ -161,3 +161,32 @@ def test_plant_a_mistake_in_the_oracle_is_caught(golden):
     idv = np.where(d != 0, np.float32(1) / np.where(d != 0, d, 1), 0).astype(np.float32)
     wrong = np.rint((b * idv[..., None]).astype(np.float32)).astype(np.int8).reshape(x.shape)
     assert not np.array_equal(wrong, golden["quant/q8_0/xq"])
+
+
+@pytest.mark.parametrize("extreme", [False, True])
+def test_q4_k_oracle_pinned_to_gguf(extreme):
+    """Q4_K weights (a third extension) against q8_K activations: the oracle's decode of this backend's split planes
+    equals gguf-py's Q4_K dequantization bit for bit, its block dots S are sum_j sc_j * (nibbles . x) of the
+    sub-blocks, its f64 reference equals the float64 product of gguf-py's dequantized operands, the host split equals
+    the oracle's, and the C oracle agrees bit for bit."""
+    gq = pytest.importorskip("gguf.quants")
+    gguf = pytest.importorskip("gguf")
+    from comp_b200 import host
+
+    n, k, m = 9, 2048, 3
+    W, x = ref.problem("q4_k", n, k, m, seed=17, extreme=extreme)
+    wq, ws = ref.split("q4_k", W, n, k)
+    hq, hs = host.split("q4_k", W, n, k)
+    assert np.array_equal(hq, wq) and np.array_equal(hs, ws) and ws.shape == (n, k // 256 * 10)
+    wdq = gq.dequantize(np.frombuffer(W, dtype=np.uint8).reshape(n, -1), gguf.GGMLQuantizationType.Q4_K)
+    assert np.array_equal(ref.decode_q4_k(wq, ws, k).view(np.uint32), wdq.astype(np.float32).view(np.uint32))
+    xq, xd = ref.quantize("q4_k", x)
+    r, s = ref.gemv("q4_k", wq, ws, xq, xd, k)
+    q, _, _, sc, _ = ref.q4_k_parts(wq, ws, k)
+    sub = np.einsum("nsv,msv->mns", q.astype(np.int64).reshape(n, k // 32, 32),
+                    xq.astype(np.int64).reshape(m, k // 32, 32)).reshape(m, n, k // 256, 8)
+    assert np.array_equal(s, (sub * sc[None].astype(np.int64)).sum(-1))
+    xdq = (xq.astype(np.float64).reshape(m, k // 256, 256) * xd.astype(np.float64)[..., None]).reshape(m, k)
+    assert ref.relerr(xdq @ wdq.astype(np.float64).T, r) <= 1e-6
+    rc, sc_ = native.gemv("q4_k", wq, ws, xq, xd, k, want_s=True)
+    assert np.array_equal(sc_, s) and np.array_equal(rc.view(np.uint64), r.view(np.uint64))
