@@ -388,6 +388,9 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
             const float4* dxp = reinterpret_cast<const float4*>(dk0 + j * C::DKB);
             const float dw = f16_bits_to_f32(sc0[j]);
             const float2 dw2 = make_float2(dw, dw);
+            // Q4_0 / Q8_0: f32(s) * dw in one fma, fl((2^23 + 2^22 + s) * dw - (2^23 + 2^22) * dw): the product
+            // 3 * 2^22 * dw of an f16 dw is exact in f32, so the fma rounds s * dw once, as the multiply would
+            const float2 mdw2 = make_float2(-kMagic * dw, -kMagic * dw);
 #pragma unroll
             for (int q = 0; q < CW; q += 4) {
               const float4 dx4 = dxp[(c0 + q) / 4];
@@ -395,15 +398,16 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
 #pragma unroll
               for (int e = 0; e < 4; e += 2) {
                 const int c = c0 + q + e;
-                const float2 f = __fadd2_rn(make_float2(__int_as_float((int)v[bb][q + e] + 0x4B400000),
-                                                        __int_as_float((int)v[bb][q + e + 1] + 0x4B400000)),
-                                            make_float2(-kMagic, -kMagic));  // exact f32(s) of both columns
+                const float2 fm = make_float2(__int_as_float((int)v[bb][q + e] + 0x4B400000),
+                                              __int_as_float((int)v[bb][q + e + 1] + 0x4B400000));  // 2^23+2^22+s
                 const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
                 float2 a2 = make_float2(acc[c], acc[c + 1]);
-                if (FMT != 1)
-                  a2 = __ffma2_rn(__fmul2_rn(f, dw2), dx2, a2);  // f32(s) * dw * dx
-                else
-                  a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);  // dx * dw * f32(s)
+                if (FMT != 1) {
+                  a2 = __ffma2_rn(__ffma2_rn(fm, dw2, mdw2), dx2, a2);  // f32(s) * dw * dx
+                } else {
+                  const float2 f = __fadd2_rn(fm, make_float2(-kMagic, -kMagic));  // exact f32(s)
+                  a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);                  // dx * dw * f32(s)
+                }
                 acc[c] = a2.x;
                 acc[c + 1] = a2.y;
               }

@@ -177,7 +177,7 @@ static size_t x_region_bytes(int fmt, int64_t K, int M, int C, int R, int MC, in
 
 static uint32_t ring_stage_bytes(int fmt, int64_t K, int C, int R) {
   const int nblk = (int)(K / fmt_block(fmt));
-  const uint32_t s = (uint32_t)R * (uint32_t)nblk * 2u;
+  const uint32_t s = (uint32_t)R * (uint32_t)nblk * (uint32_t)fmt_scale_bytes(fmt);
   return (uint32_t)R * (uint32_t)C * 16u + ((s + 15u) & ~15u);
 }
 

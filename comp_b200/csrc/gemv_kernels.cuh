@@ -1189,7 +1189,7 @@ __device__ __forceinline__ void issue_group(const GemvParams& p, int64_t g, uint
     for (int r = 0; r < rows; ++r) bulk_g2s(stage + r * qrow, wq + (r0 + r) * p.ldwq, qrow, bar, pol);
   }
   if (p.ldws == (int64_t)nblk * (Fmt<FMT>::kScaleBytes / 2)) {  // contiguous scale rows: one copy
-    bulk_g2s(stage + R * qrow, ws + r0 * nblk, (uint32_t)rows * srow, bar, pol);
+    bulk_g2s(stage + R * qrow, ws + r0 * p.ldws, (uint32_t)rows * srow, bar, pol);
   } else {
     for (int r = 0; r < rows; ++r) bulk_g2s(stage + R * qrow + r * srow, ws + (r0 + r) * p.ldws, srow, bar, pol);
   }
