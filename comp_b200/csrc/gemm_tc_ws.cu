@@ -9,8 +9,9 @@
 //     core matrices), and writes per column and weight block the scale dx;
 //   * warp 8 (producer) streams per stage -- 128 packed weight bytes of each of the tile's 128 rows -- the rows'
 //     weights (one 2-D TMA tensor copy of a 128-row x 128-byte box, 128-byte swizzled so that the unpacking reads are
-//     free of bank conflicts; rows past N read as zeros), the stage's activation tiles and its column scales (one
-//     bulk copy each) into a ring of P stages;
+//     free of bank conflicts; rows past N read as zeros) and the stage's activation tiles (one bulk copy) into a ring
+//     of P stages, and its column scales (one bulk copy) into a deeper ring of their own: the epilogue reads them up
+//     to two stages behind the MMAs, and a weight stage must not wait for it to be refilled;
 //   * warps 4-7 (thread r = tile row r) unpack each 32-value unit of their row into the MMA's A tile (a ring of RA
 //     tiles) as the signed weight values (Q4_0 nibble - 8, TQ2_0 crumb - 1), so the tensor cores' int32 dots are the
 //     exact block dots with no offset term;
@@ -68,30 +69,37 @@ struct WsCfg {
   static constexpr int BST = SU * BT;
   static constexpr int DKB = NT * 4;                              // column scales of one block
   static constexpr int DKS = SB * DKB;
-  static constexpr int STAGE = (RAW + BST + DKS + 1023) / 1024 * 1024;  // swizzled boxes start on 1024 bytes
+  static constexpr int STAGE = (RAW + BST + 1023) / 1024 * 1024;  // swizzled boxes start on 1024 bytes
   static constexpr int P = FMT == 0 ? (NT == 16 ? 3 : NT == 32 ? 2 : NT == 64 ? 4 : 3)
                                     : FMT == 1 ? (NT == 16 || NT == 64 ? 3 : 2) : (NT <= 32 ? 3 : 4);
   static constexpr int GU = NT == 128 && UPB == 1 ? 2 : 4;         // units per hand-over group
   static constexpr int RAG = 2;                                   // A-tile groups in flight
   static constexpr int RA = RAG * GU;                             // A tiles
   static constexpr int ATILE = 128 * 32;
-  static constexpr int AG = UPB == 1 ? GU : 1;                    // blocks per accumulator group
-  static constexpr int RTG = NT == 16 && UPB == 1 ? 4 : 2;          // accumulator groups in flight
+  // blocks per accumulator group (one epilogue hand-over each: Q4_0 at 16 columns takes a whole stage, measured
+  // faster than groups of 4)
+  static constexpr int AG = UPB == 1 ? (FMT == 0 && NT == 16 ? SB : GU) : 1;
+  static constexpr int RTG = NT == 16 && UPB == 1 ? 16 / AG : 2;  // accumulator groups in flight
   static constexpr int RT = RTG * AG;                             // accumulators (blocks) in tensor memory
   static constexpr int BB = NT == 16 && AG % 2 == 0 ? 2 : 1;      // blocks per tensor-memory round trip
   static constexpr int CW = NT == 64 ? 32 : 16;                   // columns per round trip (register budget)
   static constexpr int SBB = SB * 2;                              // scale bytes per row and stage (16, 4 or 8)
   static constexpr int PS = 3, LA = 2;                            // scale ring depth, prefetch distance (stages)
+  // column-scale ring (stages): the epilogue trails the MMAs by up to RTG accumulator groups, so the column scales
+  // live in their own, deeper ring and a weight stage is refilled as soon as its unpacking and MMAs are done
+  static constexpr int PD = P + (RTG * AG + SB - 1) / SB + 1;
   static constexpr int TCOLS = RT * NT <= 32 ? 32 : RT * NT <= 64 ? 64 : RT * NT <= 128 ? 128 : RT * NT <= 256 ? 256
                                                                                                            : 512;
   // + 1024: the kernel aligns its base to 1024 bytes (the swizzle pattern follows the shared-memory address bits)
-  static constexpr size_t SMEM = (size_t)P * STAGE + (size_t)RA * ATILE + (size_t)PS * 128 * SBB + 1024;
+  static constexpr size_t SMEM =
+      (size_t)P * STAGE + (size_t)(RA + 1) * ATILE + (size_t)PS * 128 * SBB + (size_t)PD * DKS + 1024;
   // registers are allocated per SM sub-partition (16K each) and a CTA's 10 warps land on them 3, 3, 2, 2: two CTAs
   // put 6 warps on one sub-partition, so two CTAs per SM need at most 85 registers a thread; one CTA at most 170
   static constexpr int MAXREG = NT <= 32 ? 80 : 168;
   static_assert(PS >= LA + 1, "scale ring: the slot refilled at a stage's start is no longer read");
   static_assert(SU % GU == 0 && SB % AG == 0 && (UPB == 1 || UPB % GU == 0), "groups never straddle stages");
   static_assert(RT * NT <= 512 && NT % 16 == 0 && CW % 16 == 0, "tensor memory");
+  static_assert(FMT != 0 || (AG * NT <= 256 && RT % AG == 0 && SU % AG == 0), "Q4_0: one offset MMA per group");
 };
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -121,23 +129,23 @@ __device__ __forceinline__ void bulk_g2s_plain(uint32_t dst, const void* src, ui
                : "memory");
 }
 
-// One 32-value unit of row r -> its row of an A tile: the signed weight values (int8) in value order. Per byte,
-// (f + 0x78) ^ 0x80 = f - 8 for a nibble f and (f + 0x7F) ^ 0x80 = f - 1 for a crumb f (no carry leaves a byte).
+// One 32-value unit of row r -> its row of an A tile in value order: Q4_0 nibbles and TQ2_0 crumbs as unsigned bytes
+// (their offsets -8 / -1 enter through a second MMA on the offset tile), Q8_0 weights as stored.
 // raw: the row's 128 bytes of the stage, whose 16-byte chunk c sits at chunk c ^ (r % 8) (TMA 128B swizzle).
 template <int FMT>
 __device__ __forceinline__ void unpack_unit(uint32_t raw, int sw, int u, uint8_t* at, int r, const uint4 (&tq)[2]) {
   uint4 lo, hi;
   if (FMT == 0) {
     const uint4 w = lds_v4(raw + (uint32_t)((u ^ sw) << 4));
-    auto nib = [](uint32_t x) { return ((x & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u; };
-    lo = make_uint4(nib(w.x), nib(w.y), nib(w.z), nib(w.w));
-    hi = make_uint4(nib(w.x >> 4), nib(w.y >> 4), nib(w.z >> 4), nib(w.w >> 4));
+    constexpr uint32_t m = 0x0F0F0F0Fu;
+    lo = make_uint4(w.x & m, w.y & m, w.z & m, w.w & m);
+    hi = make_uint4((w.x >> 4) & m, (w.y >> 4) & m, (w.z >> 4) & m, (w.w >> 4) & m);
   } else if (FMT == 2) {
     lo = lds_v4(raw + (uint32_t)(((2 * u) ^ sw) << 4));
     hi = lds_v4(raw + (uint32_t)(((2 * u + 1) ^ sw) << 4));
   } else {  // TQ2_0 k-step s = u % 8 of a block: values 32s..32s+31 = field s % 4 of the (preloaded) 32 bytes tq
     const int sh = 2 * (u & 3);
-    auto crumb = [sh](uint32_t x) { return (((x >> sh) & 0x03030303u) + 0x7F7F7F7Fu) ^ 0x80808080u; };
+    auto crumb = [sh](uint32_t x) { return (x >> sh) & 0x03030303u; };
     lo = make_uint4(crumb(tq[0].x), crumb(tq[0].y), crumb(tq[0].z), crumb(tq[0].w));
     hi = make_uint4(crumb(tq[1].x), crumb(tq[1].y), crumb(tq[1].z), crumb(tq[1].w));
   }
@@ -153,14 +161,16 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   constexpr int GU = C::GU, RAG = C::RAG, AG = C::AG, RTG = C::RTG;
   extern __shared__ __align__(1024) uint8_t ws_smem[];
   __shared__ __align__(8) uint64_t bar_full[P], bar_empty[P], bar_afull[RAG], bar_aempty[RAG], bar_accf[RTG],
-      bar_acce[RTG];
+      bar_acce[RTG], bar_dkf[C::PD], bar_dke[C::PD], bar_tinit;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const uint32_t sbase = (smem_addr(ws_smem) + 1023u) & ~1023u;
   const uint32_t a_base = sbase + P * C::STAGE;
-  const uint32_t sc_base = a_base + RA * C::ATILE;
+  const uint32_t off_tile = a_base + RA * C::ATILE;  // the weight offset (-8 or -1) in every byte
+  const uint32_t sc_base = off_tile + C::ATILE;
+  const uint32_t dk_base = sc_base + PS * 128 * C::SBB;
   const int nunits = (int)(p.K / 32);
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   const int S = nunits / SU;  // stages per tile
@@ -178,8 +188,13 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   if (t == 0) {
     for (int i = 0; i < P; ++i) {
       mbar_init(smem_addr(&bar_full[i]), 1);
-      mbar_init(smem_addr(&bar_empty[i]), 4 + 4 + 1);  // unpack warps, epilogue warps, the MMA commit
+      mbar_init(smem_addr(&bar_empty[i]), 4 + 1);  // unpack warps, the MMA commit
     }
+    for (int i = 0; i < C::PD; ++i) {
+      mbar_init(smem_addr(&bar_dkf[i]), 1);
+      mbar_init(smem_addr(&bar_dke[i]), 4);  // epilogue warps
+    }
+    mbar_init(smem_addr(&bar_tinit), 4);  // epilogue warps: the accumulators hold the conversion constant
     for (int i = 0; i < RAG; ++i) {
       mbar_init(smem_addr(&bar_afull[i]), 4);
       mbar_init(smem_addr(&bar_aempty[i]), 1);
@@ -218,7 +233,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         stage_tile(G, rt, ct, s);
         const uint32_t bar = smem_addr(&bar_full[G % P]);
         // the whole box counts, rows past N included (filled with zeros)
-        mbar_expect_tx(bar, (uint32_t)(C::RAW + C::BST + C::DKS));
+        mbar_expect_tx(bar, (uint32_t)(C::RAW + C::BST));
         tma_load_2d(sbase + (uint32_t)((G % P) * C::STAGE), &p.wmap, s * C::RB, rt * 128, bar, pol, stream_once);
       }
     };
@@ -229,9 +244,11 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         const uint32_t bar = smem_addr(&bar_full[G % P]);
         const uint32_t st = sbase + (uint32_t)((G % P) * C::STAGE);
         bulk_g2s_plain(st + C::RAW, p.xt + ((int64_t)ct * nunits + (int64_t)s * SU) * C::BT, C::BST, bar);
-        bulk_g2s_plain(st + C::RAW + C::BST,
+        const uint32_t dbar = smem_addr(&bar_dkf[G % C::PD]);
+        mbar_expect_tx(dbar, (uint32_t)C::DKS);
+        bulk_g2s_plain(dk_base + (uint32_t)((G % C::PD) * C::DKS),
                        reinterpret_cast<const uint8_t*>(p.dk) + ((int64_t)ct * nblk + (int64_t)s * SB) * C::DKB,
-                       C::DKS, bar);
+                       C::DKS, dbar);
       }
     };
     // the first stages' weights before waiting for the prep kernel (weights do not depend on it)
@@ -243,6 +260,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     for (int G = pre; G < total_stages; ++G) {
       bool ok = true;
       if (lane == 0) ok = mbar_wait(smem_addr(&bar_empty[G % P]), (uint32_t)(((G / P) & 1) ^ 1), kWaitLimit);
+      if (lane == 0 && ok && G >= C::PD)
+        ok = mbar_wait(smem_addr(&bar_dke[G % C::PD]), (uint32_t)(((G / C::PD) & 1) ^ 1), kWaitLimit);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) *abort_flag = 1;
@@ -256,9 +275,15 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = tc::instr_desc(NT, true);  // signed weight values (unpacked with their offset applied)
+      // Q4_0 / TQ2_0: the unpacked fields are unsigned (0..15, 0..3); MMAs on a tile that holds the offset (-8, -1)
+      // in every byte add offset * sum(x). Q4_0: one MMA per accumulator group, N = AG * NT columns at once (the
+      // group's accumulators are consecutive in tensor memory, and its units' activation tiles are consecutive rows
+      // of one K-major tile); TQ2_0: one per unit. Q8_0: the weights are signed int8 as stored.
+      const uint32_t idesc = tc::instr_desc(NT, FMT == 2);
+      const uint32_t idesc_off = tc::instr_desc(FMT == 0 ? NT * AG : NT, true);
       const int total_groups = total_stages * (SU / GU);
-      bool ok = true;
+      bool ok = mbar_wait(smem_addr(&bar_tinit), 0u, kWaitLimit);
+      tc::fence_after();
       for (int g = 0; g < total_groups && ok && !*abort_flag; ++g) {
         const int U0 = g * GU, G = U0 / SU, u0 = U0 - G * SU;
         if (u0 == 0) ok = mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1), kWaitLimit);
@@ -275,9 +300,14 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
             ok = mbar_wait(smem_addr(&bar_acce[a % RTG]), (uint32_t)(((a / RTG) & 1) ^ 1), kWaitLimit);
             if (!ok) break;
             tc::fence_after();
+            if (FMT == 0)
+              tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(off_tile),
+                         tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT)), idesc_off, 1u);
           }
-          tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)),
-                     tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT)), idesc, ub > 0 ? 1u : 0u);
+          // every MMA accumulates: the epilogue left 2^23 + 2^22 (as an integer) in each accumulator it released
+          const uint64_t bdesc = tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT));
+          tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)), bdesc, idesc, 1u);
+          if (FMT == 1) tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(off_tile), bdesc, idesc_off, 1u);
           if (ub == UPB - 1 && B % AG == AG - 1) tc::mma_commit(smem_addr(&bar_accf[(B / AG) % RTG]));
         }
         if (!ok) break;
@@ -295,6 +325,12 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     const int total_groups = total_stages * (SU / GU);
     uint32_t raw = 0;
     bool ok = true;
+    {  // this row of the offset tile (published to the tensor cores with the first group's unpacked tile)
+      const uint32_t o = FMT == 0 ? 0xF8F8F8F8u : 0xFFFFFFFFu;
+      uint8_t* ot = ws_smem + (off_tile - smem_addr(ws_smem));
+      *reinterpret_cast<uint4*>(ot + tc::core_off(r, 0)) = make_uint4(o, o, o, o);
+      *reinterpret_cast<uint4*>(ot + tc::core_off(r, 16)) = make_uint4(o, o, o, o);
+    }
     for (int g = 0; g < total_groups; ++g) {
       const int U0 = g * GU, G = U0 / SU, u0 = U0 - G * SU;
       if (u0 == 0) {
@@ -348,6 +384,15 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     };
 #pragma unroll
     for (int G = 0; G < LA; ++G) prefetch_scales(G);
+    // every accumulator starts at 2^23 + 2^22 as an integer: the MMAs add the exact block dot s onto it, so its bits
+    // read as an f32 are exactly 2^23 + 2^22 + s (|s| < 2^22) and the conversion costs no instruction
+    constexpr uint32_t kMagicBits = 0x4B400000u;
+#pragma unroll 1
+    for (int q = 0; q < RT * NT; q += 16) tc::tmem_st16_fill(tmem + lane_base + (uint32_t)q, kMagicBits);
+    tc::tmem_wait_st();
+    tc::fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(&bar_tinit));
     const int total_agroups = my_tiles * nblk / AG;
     int ep_k = 0, ep_b = 0;  // tile of this CTA's list and block in the tile
     bool ok = true;
@@ -356,8 +401,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
       if (j0 == 0) {  // a new stage: row scales LA stages ahead; this stage's column scales have landed
         prefetch_scales(GB + LA);
         cp_async_wait<LA>();
-        const bool got = __all_sync(0xffffffffu, mbar_wait(smem_addr(&bar_full[GB % P]), (uint32_t)((GB / P) & 1),
-                                                            kWaitLimit));
+        const bool got = __all_sync(
+            0xffffffffu, mbar_wait(smem_addr(&bar_dkf[GB % C::PD]), (uint32_t)((GB / C::PD) & 1), kWaitLimit));
         if (!got) ok = false;
         if (!got || aborted()) break;
       }
@@ -367,7 +412,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
       }
       tc::fence_after();
       // column and row scales by plain loads: the compiler may issue them ahead of the tensor-memory wait
-      const uint8_t* dk0 = ws_smem + (sbase - smem_addr(ws_smem)) + (GB % P) * C::STAGE + C::RAW + C::BST;
+      const uint8_t* dk0 = ws_smem + (dk_base - smem_addr(ws_smem)) + (GB % C::PD) * C::DKS;
       const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(ws_smem + (sc_base - smem_addr(ws_smem)) +
                                                               ((GB % PS) * 128 + t) * C::SBB);
 #pragma unroll
@@ -398,8 +443,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
 #pragma unroll
               for (int e = 0; e < 4; e += 2) {
                 const int c = c0 + q + e;
-                const float2 fm = make_float2(__int_as_float((int)v[bb][q + e] + 0x4B400000),
-                                              __int_as_float((int)v[bb][q + e + 1] + 0x4B400000));  // 2^23+2^22+s
+                const float2 fm = make_float2(__uint_as_float(v[bb][q + e]), __uint_as_float(v[bb][q + e + 1]));
                 const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
                 float2 a2 = make_float2(acc[c], acc[c + 1]);
                 if (FMT != 1) {
@@ -415,11 +459,18 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
           }
         }
       }
+      // the group's accumulators start over at the constant for their next blocks
+#pragma unroll
+      for (int jb = 0; jb < AG; ++jb)
+#pragma unroll
+        for (int h = 0; h < NT; h += 16)
+          tc::tmem_st16_fill(tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + h), kMagicBits);
+      tc::tmem_wait_st();
       tc::fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(smem_addr(&bar_acce[a % RTG]));
-        if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_empty[GB % P]));  // this warp is done with the stage's scales
+        if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_dke[GB % C::PD]));  // done with the stage's column scales
       }
       ep_b += AG;
       if (ep_b == nblk) {  // the tile's last block: store its rows of Y
@@ -443,9 +494,12 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   }
 
   // ---------------- teardown: nothing in flight when the CTA leaves ----------------
-  if (warp == 8 && lane == 0)
+  if (warp == 8 && lane == 0) {
     for (int G = max(0, issued - P); G < issued; ++G)
       mbar_wait(smem_addr(&bar_full[G % P]), (uint32_t)((G / P) & 1), kWaitLimit);
+    for (int G = max(0, issued - C::PD); G < issued; ++G)
+      mbar_wait(smem_addr(&bar_dkf[G % C::PD]), (uint32_t)((G / C::PD) & 1), kWaitLimit);
+  }
   if (warp == 9 && lane == 0 && g_issued > 0)
     mbar_wait(smem_addr(&bar_aempty[(g_issued - 1) % RAG]), (uint32_t)(((g_issued - 1) / RAG) & 1), kWaitLimit);
   tc::fence_before();
