@@ -39,6 +39,20 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[1
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld that names the 16 registers a load wrote, so that no use of them is scheduled above the wait
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+// orders 16 more registers after a preceding tmem_wait_ld_regs (an empty statement that names them)
+__device__ __forceinline__ void regs_ready(uint32_t (&v)[16]) {
+  asm volatile(""
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]));
+}
 // 16 consecutive 32-bit columns of this thread's lane <- v, in four stores of 4 columns (a store's registers are
 // consecutive: 4 of them hold v at a time), without waiting (tmem_wait_st before the tensor cores or a load read them)
 __device__ __forceinline__ void tmem_st16_fill(uint32_t taddr, uint32_t v) {
