@@ -43,6 +43,7 @@ struct WsParams {
   int64_t ldws;
   const int8_t* xt;   // activation tiles [nct][K/32][NT*32]
   const float* dk;    // [nct][nblk][NT]: the column scales dx
+  const int* fk;      // TQ2_0: [nct][nblk][NT]: each accumulator's start value, 2^23 + 2^22 - sum(x) of the block
   float* y;
   int64_t ldy;
   int64_t row0;
@@ -69,6 +70,12 @@ struct WsCfg {
   static constexpr int BST = SU * BT;
   static constexpr int DKB = NT * 4;                              // column scales of one block
   static constexpr int DKS = SB * DKB;
+  // TQ2_0: the crumbs' offset (-1) enters through the accumulators' start value (2^23 + 2^22 - sum(x) per column and
+  // block) instead of offset MMAs; each column-scale ring entry also carries the start values of the blocks that next
+  // use the stage's accumulators (RT blocks later)
+  static constexpr bool FILL = FMT == 1;
+  static constexpr int DKR = DKS + (FILL ? DKS : 0);  // column-scale ring entry
+  static constexpr int OT = FMT == 0 ? 1 : 0;          // the offset tile (Q4_0)
   static constexpr int STAGE = (RAW + BST + 1023) / 1024 * 1024;  // swizzled boxes start on 1024 bytes
   static constexpr int P = FMT == 0 ? (NT == 16 ? 3 : NT == 32 ? 2 : NT == 64 ? 4 : 3)
                                     : FMT == 1 ? (NT == 16 || NT == 64 ? 3 : 2) : (NT <= 32 ? 3 : 4);
@@ -76,10 +83,10 @@ struct WsCfg {
   static constexpr int RAG = 2;                                   // A-tile groups in flight
   static constexpr int RA = RAG * GU;                             // A tiles
   static constexpr int ATILE = 128 * 32;
-  // blocks per accumulator group (one epilogue hand-over each: Q4_0 at 16 columns takes a whole stage, measured
-  // faster than groups of 4)
-  static constexpr int AG = UPB == 1 ? (FMT == 0 && NT == 16 ? SB : GU) : 1;
-  static constexpr int RTG = NT == 16 && UPB == 1 ? 16 / AG : 2;  // accumulator groups in flight
+  // blocks per accumulator group (one epilogue hand-over each): a whole stage for Q4_0 and TQ2_0 at 16 columns
+  // (measured faster than groups of 4 blocks, or of one TQ2_0 block), else GU
+  static constexpr int AG = (FMT != 2 && NT == 16) ? SB : UPB == 1 ? GU : 1;
+  static constexpr int RTG = NT == 16 ? 16 / AG : 2;  // accumulator groups in flight (16 x NT tensor-memory columns)
   static constexpr int RT = RTG * AG;                             // accumulators (blocks) in tensor memory
   static constexpr int CW = NT == 64 ? 32 : 16;                   // columns per tensor-memory load (registers)
   static constexpr int SBB = SB * 2;                              // scale bytes per row and stage (16, 4 or 8)
@@ -91,7 +98,7 @@ struct WsCfg {
                                                                                                            : 512;
   // + 1024: the kernel aligns its base to 1024 bytes (the swizzle pattern follows the shared-memory address bits)
   static constexpr size_t SMEM =
-      (size_t)P * STAGE + (size_t)(RA + 1) * ATILE + (size_t)PS * 128 * SBB + (size_t)PD * DKS + 1024;
+      (size_t)P * STAGE + (size_t)(RA + OT) * ATILE + (size_t)PS * 128 * SBB + (size_t)PD * DKR + 1024;
   // registers are allocated per SM sub-partition (16K each) and a CTA's 10 warps land on them 3, 3, 2, 2: two CTAs
   // put 6 warps on one sub-partition, so two CTAs per SM need at most 85 registers a thread; one CTA at most 170
   static constexpr int MAXREG = NT <= 32 ? 80 : 168;
@@ -99,6 +106,8 @@ struct WsCfg {
   static_assert(SU % GU == 0 && SB % AG == 0 && (UPB == 1 || UPB % GU == 0), "groups never straddle stages");
   static_assert(RT * NT <= 512 && NT % 16 == 0 && CW % 16 == 0, "tensor memory");
   static_assert(FMT != 0 || (AG * NT <= 256 && RT % AG == 0 && SU % AG == 0), "Q4_0: one offset MMA per group");
+  static_assert(!FILL || (RT % SB == 0 && NT % 16 == 0), "start values travel a whole number of stages ahead");
+  static_assert(!FILL || (RT * NT * 4 <= PS * 128 * SBB && RT * NT <= 256), "first start values staged in the scale ring");
 };
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -168,8 +177,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   const uint32_t sbase = (smem_addr(ws_smem) + 1023u) & ~1023u;
   const uint32_t a_base = sbase + P * C::STAGE;
   const uint32_t off_tile = a_base + RA * C::ATILE;  // the weight offset (-8 or -1) in every byte
-  const uint32_t sc_base = off_tile + C::ATILE;
-  const uint32_t dk_base = sc_base + PS * 128 * C::SBB;
+  const uint32_t sc_base = off_tile + C::OT * C::ATILE;
+  const uint32_t dk_base = sc_base + PS * 128 * C::SBB;  // column-scale ring, PD entries of DKR bytes
   const int nunits = (int)(p.K / 32);
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
   const int S = nunits / SU;  // stages per tile
@@ -244,10 +253,17 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         const uint32_t st = sbase + (uint32_t)((G % P) * C::STAGE);
         bulk_g2s_plain(st + C::RAW, p.xt + ((int64_t)ct * nunits + (int64_t)s * SU) * C::BT, C::BST, bar);
         const uint32_t dbar = smem_addr(&bar_dkf[G % C::PD]);
-        mbar_expect_tx(dbar, (uint32_t)C::DKS);
-        bulk_g2s_plain(dk_base + (uint32_t)((G % C::PD) * C::DKS),
+        mbar_expect_tx(dbar, (uint32_t)C::DKR);
+        bulk_g2s_plain(dk_base + (uint32_t)((G % C::PD) * C::DKR),
                        reinterpret_cast<const uint8_t*>(p.dk) + ((int64_t)ct * nblk + (int64_t)s * SB) * C::DKB,
                        C::DKS, dbar);
+        if (C::FILL) {  // start values of the blocks RT later in this CTA's sequence (past its end: unused)
+          int rtf, ctf, sf;
+          stage_tile(min(G + C::RT / SB, total_stages - 1), rtf, ctf, sf);
+          bulk_g2s_plain(dk_base + (uint32_t)((G % C::PD) * C::DKR + C::DKS),
+                         reinterpret_cast<const uint8_t*>(p.fk) + ((int64_t)ctf * nblk + (int64_t)sf * SB) * C::DKB,
+                         C::DKS, dbar);
+        }
       }
     };
     // the first stages' weights before waiting for the prep kernel (weights do not depend on it)
@@ -274,12 +290,12 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      // Q4_0 / TQ2_0: the unpacked fields are unsigned (0..15, 0..3); MMAs on a tile that holds the offset (-8, -1)
-      // in every byte add offset * sum(x). Q4_0: one MMA per accumulator group, N = AG * NT columns at once (the
-      // group's accumulators are consecutive in tensor memory, and its units' activation tiles are consecutive rows
-      // of one K-major tile); TQ2_0: one per unit. Q8_0: the weights are signed int8 as stored.
+      // Q4_0 / TQ2_0: the unpacked fields are unsigned (0..15, 0..3). Q4_0: one MMA per accumulator group on a tile
+      // that holds the offset -8 in every byte adds -8 * sum(x), N = AG * NT columns at once (the group's
+      // accumulators are consecutive in tensor memory, and its units' activation tiles are consecutive rows of one
+      // K-major tile); TQ2_0: the accumulators start at 2^23 + 2^22 - sum(x). Q8_0: signed int8 as stored.
       const uint32_t idesc = tc::instr_desc(NT, FMT == 2);
-      const uint32_t idesc_off = tc::instr_desc(FMT == 0 ? NT * AG : NT, true);
+      const uint32_t idesc_off = tc::instr_desc(NT * AG, true);
       const int total_groups = total_stages * (SU / GU);
       bool ok = mbar_wait(smem_addr(&bar_tinit), 0u, kWaitLimit);
       tc::fence_after();
@@ -306,7 +322,6 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
           // every MMA accumulates: the epilogue left 2^23 + 2^22 (as an integer) in each accumulator it released
           const uint64_t bdesc = tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT));
           tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)), bdesc, idesc, 1u);
-          if (FMT == 1) tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(off_tile), bdesc, idesc_off, 1u);
           if (ub == UPB - 1 && B % AG == AG - 1) tc::mma_commit(smem_addr(&bar_accf[(B / AG) % RTG]));
         }
         if (!ok) break;
@@ -324,8 +339,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     const int total_groups = total_stages * (SU / GU);
     uint32_t raw = 0;
     bool ok = true;
-    {  // this row of the offset tile (published to the tensor cores with the first group's unpacked tile)
-      const uint32_t o = FMT == 0 ? 0xF8F8F8F8u : 0xFFFFFFFFu;
+    if (FMT == 0) {  // this row of the offset tile (published to the tensor cores with the first group's tile)
+      const uint32_t o = 0xF8F8F8F8u;
       uint8_t* ot = ws_smem + (off_tile - smem_addr(ws_smem));
       *reinterpret_cast<uint4*>(ot + tc::core_off(r, 0)) = make_uint4(o, o, o, o);
       *reinterpret_cast<uint4*>(ot + tc::core_off(r, 16)) = make_uint4(o, o, o, o);
@@ -369,6 +384,33 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     float acc[NT];
 #pragma unroll
     for (int c = 0; c < NT; ++c) acc[c] = 0.f;
+    // every accumulator starts at 2^23 + 2^22 as an integer: the MMAs add the exact block dot s onto it, so its bits
+    // read as an f32 are exactly 2^23 + 2^22 + s (|s| < 2^22) and the conversion costs no instruction
+    constexpr uint32_t kMagicBits = 0x4B400000u;
+    if constexpr (!C::FILL) {
+#pragma unroll 1
+      for (int q = 0; q < RT * NT; q += 16) tc::tmem_st16_fill(tmem + lane_base + (uint32_t)q, kMagicBits);
+    } else {
+      // TQ2_0: the first RT blocks' start values, 2^23 + 2^22 - sum(x), which the prep kernel (the preceding grid)
+      // writes: wait for it, stage the RT x NT values through the (not yet used) scale ring with one load per thread,
+      // then every thread stores them into its lane
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      uint32_t* stg = reinterpret_cast<uint32_t*>(ws_smem + (sc_base - smem_addr(ws_smem)));
+      const int e = 2 * t;
+      if (e < RT * NT) {
+        const int q = e / NT, c = e % NT;
+        int rt, ct, s;
+        stage_tile(min(q / SB, max(total_stages - 1, 0)), rt, ct, s);
+        const int* src = p.fk + ((int64_t)ct * nblk + (int64_t)s * SB + q % SB) * NT + c;
+        const int2 w = total_stages > 0 ? __ldg(reinterpret_cast<const int2*>(src)) : make_int2(0, 0);
+        *reinterpret_cast<int2*>(stg + e) = w;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+#pragma unroll 1
+      for (int q = 0; q < RT * NT; q += 4)
+        tc::tmem_st4(tmem + lane_base + (uint32_t)q, *reinterpret_cast<const uint4*>(stg + q));
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the staging area is the scale ring's again
+    }
     // this row's block scales of stage G, LA stages ahead, into its own slot of the scale ring
     auto prefetch_scales = [&](int G) {
       if (G < total_stages) {
@@ -383,11 +425,6 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     };
 #pragma unroll
     for (int G = 0; G < LA; ++G) prefetch_scales(G);
-    // every accumulator starts at 2^23 + 2^22 as an integer: the MMAs add the exact block dot s onto it, so its bits
-    // read as an f32 are exactly 2^23 + 2^22 + s (|s| < 2^22) and the conversion costs no instruction
-    constexpr uint32_t kMagicBits = 0x4B400000u;
-#pragma unroll 1
-    for (int q = 0; q < RT * NT; q += 16) tc::tmem_st16_fill(tmem + lane_base + (uint32_t)q, kMagicBits);
     tc::tmem_wait_st();
     tc::fence_before();
     __syncwarp();
@@ -411,7 +448,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
       }
       tc::fence_after();
       // column and row scales by plain loads: the compiler may issue them ahead of the tensor-memory wait
-      const uint8_t* dk0 = ws_smem + (dk_base - smem_addr(ws_smem)) + (GB % C::PD) * C::DKS;
+      const uint8_t* dk0 = ws_smem + (dk_base - smem_addr(ws_smem)) + (GB % C::PD) * C::DKR;
       const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(ws_smem + (sc_base - smem_addr(ws_smem)) +
                                                               ((GB % PS) * 128 + t) * C::SBB);
       // The group's accumulators in chunks of CW columns of one block (blocks ascending: the sum order of the
@@ -472,12 +509,21 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
           wait_chunk(v[PIPE ? (k + 1) & 1 : 0]);
         }
       }
-      // the group's accumulators start over at the constant for their next blocks
+      // the group's accumulators start over for their next blocks (RT later): at the constant, or for TQ2_0 at the
+      // start values that came with this stage's column scales
 #pragma unroll
       for (int jb = 0; jb < AG; ++jb)
 #pragma unroll
-        for (int h = 0; h < NT; h += 16)
-          tc::tmem_st16_fill(tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + h), kMagicBits);
+        for (int h = 0; h < NT; h += 16) {
+          const uint32_t ta = tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + h);
+          if constexpr (!C::FILL) {
+            tc::tmem_st16_fill(ta, kMagicBits);
+          } else {  // four columns per store: few registers live next to the NT sums
+            const uint4* src = reinterpret_cast<const uint4*>(dk0 + C::DKS + (j0 + jb) * C::DKB + h * 4);
+#pragma unroll
+            for (int e = 0; e < 16; e += 4) tc::tmem_st4(ta + (uint32_t)e, src[e / 4]);
+          }
+        }
       tc::tmem_wait_st();
       tc::fence_before();
       __syncwarp();
@@ -565,7 +611,8 @@ __global__ void __launch_bounds__(256) tc_prep_q8_0_kernel(const float* __restri
 template <int NT>
 __global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restrict__ x, int64_t ldx, int M, int64_t K,
                                                            int nct, int8_t* __restrict__ xt, float* __restrict__ dk,
-                                                           int8_t* __restrict__ xq_out, float* __restrict__ xd_out) {
+                                                           int* __restrict__ fk, int8_t* __restrict__ xq_out,
+                                                           float* __restrict__ xd_out) {
   pdl_wait_then_trigger();
   const int64_t nblk = K / 256, nunits = K / 32;
   const int64_t total = (int64_t)nct * NT * nblk;
@@ -587,7 +634,14 @@ __global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restri
     const int64_t unit = b * 8 + (lane >> 2);
     *reinterpret_cast<uint2*>(xt + ((int64_t)ct * nunits + unit) * (NT * 32) + tc::core_off(cl, (lane & 3) * 8)) =
         make_uint2(qlo, qhi);
-    if (lane == 0) dk[((int64_t)ct * nblk + b) * NT + cl] = valid ? d : 0.f;
+    // the block's sum of quantized values: the GEMM's accumulators start at 2^23 + 2^22 - sum (the crumbs' offset)
+    int qs = __dp4a((int)qlo, 0x01010101, __dp4a((int)qhi, 0x01010101, 0));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+    if (lane == 0) {
+      dk[((int64_t)ct * nblk + b) * NT + cl] = valid ? d : 0.f;
+      fk[((int64_t)ct * nblk + b) * NT + cl] = 0x4B400000 - qs;
+    }
     if (valid && xq_out) {
       *reinterpret_cast<uint2*>(xq_out + c * K + b * 256 + lane * 8) = make_uint2(qlo, qhi);
       if (lane == 0) xd_out[c * nblk + b] = d;
@@ -603,14 +657,18 @@ static int ws_nt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 
 
 static int ws_stage_values(int fmt) { return fmt == 0 ? 256 : fmt == 1 ? 512 : 128; }
 
-// Workspace bytes of the warp-specialized path (activation tiles, then the column scales), or 0 if the shape does
-// not fit its stages (K a whole number of stages: Q4_0 256, TQ2_0 512, Q8_0 128 values).
+static size_t align16(size_t n) { return (n + 15) / 16 * 16; }
+
+// Workspace bytes of the warp-specialized path (activation tiles, the column scales, and for TQ2_0 the accumulators'
+// start values, each 16-byte aligned), or 0 if the shape does not fit its stages (K a whole number of stages: Q4_0
+// 256, TQ2_0 512, Q8_0 128 values).
 size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M) {
   if (K <= 0 || M <= 0 || K % ws_stage_values(fmt)) return 0;
   const int NT = ws_nt(M);
   const int64_t cols = (M + NT - 1) / NT * NT;
   const int64_t nblk = K / (fmt == 1 ? 256 : 32);
-  return ((size_t)cols * (size_t)K + 15) / 16 * 16 + (size_t)cols * (size_t)nblk * 4;
+  const size_t per_col_blk = align16((size_t)cols * (size_t)nblk * 4);
+  return align16((size_t)cols * (size_t)K) + per_col_blk * (fmt == 1 ? 2 : 1);
 }
 
 template <int FMT, int NT>
@@ -639,7 +697,8 @@ static int launch_ws(const WsParams& wp, const float* x, int64_t ldx, int8_t* xq
     int8_t* xt = const_cast<int8_t*>(wp.xt);
     float* dk = const_cast<float*>(wp.dk);
     if constexpr (FMT == 1)
-      e = cudaLaunchKernelEx(&cfg, tc_prep_q8_K_kernel<NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk, xq_out, xd_out);
+      e = cudaLaunchKernelEx(&cfg, tc_prep_q8_K_kernel<NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk,
+                             const_cast<int*>(wp.fk), xq_out, xd_out);
     else
       e = cudaLaunchKernelEx(&cfg, tc_prep_q8_0_kernel<FMT, NT>, x, ldx, wp.M, wp.K, wp.nct, xt, dk, xq_out, xd_out);
     if (e != cudaSuccess) {
@@ -738,7 +797,9 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
   wp.nct = (int)((M + NT - 1) / NT);
   wp.xt = reinterpret_cast<const int8_t*>(workspace);
   wp.dk = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(workspace) +
-                                           ((size_t)wp.nct * NT * (size_t)K + 15) / 16 * 16);
+                                           align16((size_t)wp.nct * NT * (size_t)K));
+  wp.fk = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(wp.dk) +
+                                       align16((size_t)wp.nct * NT * (size_t)(K / (fmt == 1 ? 256 : 32)) * 4));
   wp.y = y;
   wp.ldy = ldy;
   wp.row0 = row0;
