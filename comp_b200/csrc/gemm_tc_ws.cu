@@ -296,6 +296,10 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
       // K-major tile); TQ2_0: the accumulators start at 2^23 + 2^22 - sum(x). Q8_0: signed int8 as stored.
       const uint32_t idesc = tc::instr_desc(NT, FMT == 2);
       const uint32_t idesc_off = tc::instr_desc(NT * AG, true);
+      // shared-memory descriptors formed once; per MMA only the address field (bytes / 16) advances, which stays
+      // below 2^14 because every operand lies inside this CTA's shared memory (< 228 KB)
+      const uint64_t adesc0 = tc::smem_desc(a_base), bdesc0 = tc::smem_desc(sbase + C::RAW);
+      const uint64_t odesc = tc::smem_desc(off_tile);
       const int total_groups = total_stages * (SU / GU);
       bool ok = mbar_wait(smem_addr(&bar_tinit), 0u, kWaitLimit);
       tc::fence_after();
@@ -305,8 +309,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         if (ok) ok = mbar_wait(smem_addr(&bar_afull[g % RAG]), (uint32_t)((g / RAG) & 1), kWaitLimit);
         if (!ok) break;
         tc::fence_after();
-        const uint32_t bst = sbase + (uint32_t)((G % P) * C::STAGE + C::RAW);
-        const uint32_t at = a_base + (uint32_t)((g % RAG) * GU * C::ATILE);
+        const uint64_t bst = bdesc0 + (uint64_t)(((G % P) * C::STAGE + u0 * C::BT) >> 4);
+        const uint64_t at = adesc0 + (uint64_t)(((g % RAG) * GU * C::ATILE) >> 4);
 #pragma unroll
         for (int i = 0; i < GU; ++i) {
           const int U = U0 + i, B = U / UPB, ub = U - B * UPB;
@@ -316,12 +320,11 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
             if (!ok) break;
             tc::fence_after();
             if (FMT == 0)
-              tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(off_tile),
-                         tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT)), idesc_off, 1u);
+              tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), odesc, bst + (uint64_t)((i * C::BT) >> 4), idesc_off, 1u);
           }
           // every MMA accumulates: the epilogue left 2^23 + 2^22 (as an integer) in each accumulator it released
-          const uint64_t bdesc = tc::smem_desc(bst + (uint32_t)((u0 + i) * C::BT));
-          tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), tc::smem_desc(at + (uint32_t)(i * C::ATILE)), bdesc, idesc, 1u);
+          tc::mma_i8(tmem + (uint32_t)((B % RT) * NT), at + (uint64_t)((i * C::ATILE) >> 4),
+                     bst + (uint64_t)((i * C::BT) >> 4), idesc, 1u);
           if (ub == UPB - 1 && B % AG == AG - 1) tc::mma_commit(smem_addr(&bar_accf[(B / AG) % RTG]));
         }
         if (!ok) break;
