@@ -51,7 +51,9 @@ struct WsParams {
   int64_t K;
   int M;
   int nct;     // column tiles
-  int ntiles;  // row tiles x column tiles
+  int ks;      // K splits (split-K for layers whose row tiles alone do not fill the GPU)
+  int ntiles;  // row tiles x column tiles x K splits
+  float* part; // ks > 1: the splits' partial sums [ks][M][N]; a combine kernel adds them in split order into Y
 };
 
 // Pipeline shape per weight format and column tile. A stage is 128 packed weight bytes of each row: 8 Q4_0 blocks,
@@ -181,7 +183,8 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   const uint32_t dk_base = sc_base + PS * 128 * C::SBB;  // column-scale ring, PD entries of DKR bytes
   const int nunits = (int)(p.K / 32);
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
-  const int S = nunits / SU;  // stages per tile
+  const int S = nunits / SU / p.ks;  // stages per tile (its K split)
+  const int nbt = nblk / p.ks;       // weight blocks per tile
   const int my_tiles = (int)blockIdx.x < p.ntiles ? (p.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int total_stages = my_tiles * S;
   volatile int* abort_flag = &s_abort;
@@ -220,13 +223,14 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
   tc::fence_after();
   const uint32_t tmem = s_tmem;
 
-  // (row tile, column tile, stage within the tile) of this CTA's global stage G
+  // (row tile, column tile, stage along K) of this CTA's global stage G; a tile is (row tile, column tile, K split)
   auto stage_tile = [&](int G, int& rt, int& ct, int& s) {
     const int k = G / S;
-    s = G - k * S;
     const int tile = (int)blockIdx.x + k * (int)gridDim.x;
-    rt = tile / p.nct;
-    ct = tile - rt * p.nct;
+    const int rc = tile / p.ks, kq = tile - rc * p.ks;
+    s = kq * S + (G - k * S);
+    rt = rc / p.nct;
+    ct = rc - rt * p.nct;
   };
 
   int issued = 0;    // producer: stages whose copies were issued
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
     tc::fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(&bar_tinit));
-    const int total_agroups = my_tiles * nblk / AG;
+    const int total_agroups = my_tiles * nbt / AG;
     int ep_k = 0, ep_b = 0;  // tile of this CTA's list and block in the tile
     bool ok = true;
     for (int a = 0; a < total_agroups; ++a) {
@@ -535,15 +539,22 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
         if (j0 + AG == SB) mbar_arrive(smem_addr(&bar_dke[GB % C::PD]));  // done with the stage's column scales
       }
       ep_b += AG;
-      if (ep_b == nblk) {  // the tile's last block: store its rows of Y
+      if (ep_b == nbt) {  // the tile's last block: store its rows of Y (or of its K split's partial sums)
         const int tile = (int)blockIdx.x + ep_k * (int)gridDim.x;
-        const int rt = tile / p.nct, ct = tile - rt * p.nct;
+        const int rc = tile / p.ks, kq = tile - rc * p.ks;
+        const int rt = rc / p.nct, ct = rc - rt * p.nct;
         const int64_t row = (int64_t)rt * 128 + t;
         const int col0 = ct * NT, ncols = min(NT, p.M - col0);
         if (row < p.N) {
+          if (p.ks == 1) {
 #pragma unroll
-          for (int c = 0; c < NT; ++c)
-            if (c < ncols) p.y[(int64_t)(col0 + c) * p.ldy + p.row0 + row] = acc[c];
+            for (int c = 0; c < NT; ++c)
+              if (c < ncols) p.y[(int64_t)(col0 + c) * p.ldy + p.row0 + row] = acc[c];
+          } else {
+#pragma unroll
+            for (int c = 0; c < NT; ++c)
+              if (c < ncols) p.part[((int64_t)kq * p.M + col0 + c) * p.N + row] = acc[c];
+          }
         }
 #pragma unroll
         for (int c = 0; c < NT; ++c) acc[c] = 0.f;
@@ -652,6 +663,20 @@ __global__ void __launch_bounds__(256) tc_prep_q8_K_kernel(const float* __restri
   }
 }
 
+// Split-K: Y[m][row0 + n] = the K splits' partial sums added in split order (deterministic)
+__global__ void __launch_bounds__(256) tc_splitk_combine_kernel(const float* __restrict__ part, int ks, int64_t M,
+                                                                int64_t N, float* __restrict__ y, int64_t ldy,
+                                                                int64_t row0) {
+  pdl_wait_then_trigger();
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float acc = part[i];
+    for (int k = 1; k < ks; ++k) acc += part[(int64_t)k * total + i];
+    y[m * ldy + row0 + n] = acc;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------------------------
@@ -662,16 +687,37 @@ static int ws_stage_values(int fmt) { return fmt == 0 ? 256 : fmt == 1 ? 512 : 1
 
 static size_t align16(size_t n) { return (n + 15) / 16 * 16; }
 
-// Workspace bytes of the warp-specialized path (activation tiles, the column scales, and for TQ2_0 the accumulators'
-// start values, each 16-byte aligned), or 0 if the shape does not fit its stages (K a whole number of stages: Q4_0
-// 256, TQ2_0 512, Q8_0 128 values).
-size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M) {
+// K splits for a layer whose tiles (128 rows x NT columns) do not fill the GPU: the fewest that give at least one tile
+// per SM, among the divisors of the stage count that leave each split two stages or more (at most 16); 1 when the
+// tiles alone fill it.
+int gemm_tc_ws_splits(int fmt, int64_t N, int64_t K, int64_t M) {
+  if (N <= 0 || K <= 0 || M <= 0 || K % ws_stage_values(fmt)) return 1;
+  DeviceInfo di;
+  if (device_info(&di) != B2Q_OK) return 1;
+  const int NT = ws_nt(M);
+  const int64_t tiles = (N + 127) / 128 * ((M + NT - 1) / NT);
+  if (tiles >= di.sms) return 1;
+  const int64_t stages = K / ws_stage_values(fmt);
+  int best = 1;
+  for (int d = 2; d <= 16 && stages / d >= 2; ++d) {
+    if (stages % d) continue;
+    best = d;
+    if (tiles * d >= di.sms) break;
+  }
+  return best;
+}
+
+// Workspace bytes of the warp-specialized path (activation tiles, the column scales, for TQ2_0 the accumulators'
+// start values, and with ks > 1 K splits the partial sums, each 16-byte aligned), or 0 if the shape does not fit its
+// stages (K a whole number of stages: Q4_0 256, TQ2_0 512, Q8_0 128 values).
+size_t gemm_tc_ws_bytes(int fmt, int64_t N, int64_t K, int64_t M, int ks) {
   if (K <= 0 || M <= 0 || K % ws_stage_values(fmt)) return 0;
   const int NT = ws_nt(M);
   const int64_t cols = (M + NT - 1) / NT * NT;
   const int64_t nblk = K / (fmt == 1 ? 256 : 32);
   const size_t per_col_blk = align16((size_t)cols * (size_t)nblk * 4);
-  return align16((size_t)cols * (size_t)K) + per_col_blk * (fmt == 1 ? 2 : 1);
+  const size_t parts = ks > 1 ? align16((size_t)ks * (size_t)M * (size_t)std::max<int64_t>(N, 0) * 4) : 0;
+  return align16((size_t)cols * (size_t)K) + per_col_blk * (fmt == 1 ? 2 : 1) + parts;
 }
 
 template <int FMT, int NT>
@@ -751,7 +797,23 @@ static int launch_ws(const WsParams& wp, const float* x, int64_t ldx, int8_t* xq
     cudaGetLastError();
     return fail(B2Q_ECUDA, "gemm_tc_ws: launch failed: %s", cudaGetErrorString(e));
   }
-  return after_launch(FMT == 0 ? "gemm_tc_ws_q4_0" : FMT == 1 ? "gemm_tc_ws_tq2_0" : "gemm_tc_ws_q8_0");
+  rc = after_launch(FMT == 0 ? "gemm_tc_ws_q4_0" : FMT == 1 ? "gemm_tc_ws_tq2_0" : "gemm_tc_ws_q8_0");
+  if (rc || wp.ks == 1) return rc;
+  // split-K: the combine, programmatically dependent on the GEMM
+  cudaLaunchConfig_t cc = {};
+  const int64_t total = (int64_t)wp.M * wp.N;
+  cc.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)di.sms * 8)));
+  cc.blockDim = dim3(256);
+  cc.stream = stream;
+  cc.attrs = attr;
+  cc.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cc, tc_splitk_combine_kernel, (const float*)wp.part, wp.ks, (int64_t)wp.M, wp.N, wp.y,
+                         wp.ldy, wp.row0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(B2Q_ECUDA, "gemm_tc_ws: combine launch failed: %s", cudaGetErrorString(e));
+  }
+  return after_launch("tc_splitk_combine");
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver library)
@@ -783,11 +845,12 @@ static int encode_weight_map(CUtensorMap* map, const uint8_t* wq, int64_t row_by
   return B2Q_OK;
 }
 
-// Fused quantize + tensor-core GEMM, warp-specialized (two launches). The caller checked gemm_tc_ws_bytes(...) > 0
-// and workspace_bytes >= it, a 16-byte aligned workspace, weights and x; ws rows contiguous (ldws = K / block).
+// Fused quantize + tensor-core GEMM, warp-specialized (two launches, three with ks > 1 K splits). The caller checked
+// gemm_tc_ws_bytes(..., ks) > 0 and workspace_bytes >= it, ks dividing the stage count, a 16-byte aligned workspace,
+// weights and x; ws rows contiguous (ldws = K / block).
 int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                       int8_t* xq_out, float* xd_out, float* y, int64_t ldy, int64_t row0, int64_t N, int64_t K,
-                      int64_t M, void* workspace, cudaStream_t stream, bool pdl) {
+                      int64_t M, int ks, void* workspace, cudaStream_t stream, bool pdl) {
   const int NT = ws_nt(M);
   WsParams wp{};
   const int64_t row_bytes = K / (fmt == 1 ? 256 : 32) * (fmt == 0 ? 16 : fmt == 1 ? 64 : 32);
@@ -809,7 +872,11 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
   wp.N = N;
   wp.K = K;
   wp.M = (int)M;
-  wp.ntiles = (int)((N + 127) / 128) * wp.nct;
+  wp.ks = std::max(1, ks);
+  wp.part = wp.ks > 1 ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                                 gemm_tc_ws_bytes(fmt, N, K, M, 1))
+                      : nullptr;
+  wp.ntiles = (int)((N + 127) / 128) * wp.nct * wp.ks;
 #define B2Q_WS_CASE(F, T) \
   if (fmt == F && NT == T) return launch_ws<F, T>(wp, x, ldx, xq_out, xd_out, stream, pdl);
   B2Q_WS_CASE(0, 16) B2Q_WS_CASE(0, 32) B2Q_WS_CASE(0, 64) B2Q_WS_CASE(0, 128)

@@ -452,10 +452,12 @@ int launch_gemm_tc(const GemvParams& base, int fmt, cudaStream_t stream, bool pd
 
 // Warp-specialized persistent tensor-core GEMM with its quantizing prep kernel (gemm_tc_ws.cu): the fused path's
 // schedule when the workspace holds its activation tiles (gemm_tc_ws_bytes > 0: K a whole number of stages).
-size_t gemm_tc_ws_bytes(int fmt, int64_t K, int64_t M);
+// Layers whose row tiles alone do not fill the GPU split K (gemm_tc_ws_splits), their partial sums in the workspace.
+int gemm_tc_ws_splits(int fmt, int64_t N, int64_t K, int64_t M);
+size_t gemm_tc_ws_bytes(int fmt, int64_t N, int64_t K, int64_t M, int ks);
 int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, const float* x, int64_t ldx,
                       int8_t* xq_out, float* xd_out, float* y, int64_t ldy, int64_t row0, int64_t N, int64_t K,
-                      int64_t M, void* workspace, cudaStream_t stream, bool pdl);
+                      int64_t M, int ks, void* workspace, cudaStream_t stream, bool pdl);
 
 // Columns from which a layer runs on the tensor-core GEMM (0 = never). Below it the GEMV kernels, which re-read the
 // weights per group of 4 columns, are the better fit.
@@ -465,10 +467,16 @@ static std::atomic<int> g_tc_schedule{0};
 
 // Scratch for the quantized activations when a fused call takes the tensor-core path: XQ [M][K], then XD (per-block
 // schedule), or the warp-specialized schedule's activation tiles -- whichever is larger.
-static size_t tc_act_bytes(int fmt, int64_t K, int64_t M) {
+// K splits of the warp-specialized schedule: only under the default column threshold (a lowered one is how the
+// tests force the tensor-core kernels onto narrow layers, where the two schedules must agree bit for bit)
+static int tc_splits(int fmt, int64_t N, int64_t K, int64_t M) {
+  return g_tc_min_m.load() >= 8 ? gemm_tc_ws_splits(fmt, N, K, M) : 1;
+}
+
+static size_t tc_act_bytes(int fmt, int64_t N, int64_t K, int64_t M) {
   const int64_t nblk = K / fmt_block(fmt);
   const size_t v1 = ((size_t)M * (size_t)K + 15) / 16 * 16 + (size_t)M * (size_t)nblk * sizeof(float);
-  return std::max(v1, gemm_tc_ws_bytes(fmt, K, M));
+  return std::max(v1, gemm_tc_ws_bytes(fmt, N, K, M, tc_splits(fmt, N, K, M)));
 }
 
 static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
@@ -487,11 +495,14 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   // (only when its CTAs -- 128 rows x up to 128 columns each -- fill the GPU: on narrow layers the GEMV path is faster)
   DeviceInfo tc_di;
   const int tc_nt = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
-  const bool tc_wide = device_info(&tc_di) == B2Q_OK &&
-                       ((a.N + 127) / 128) * ((a.M + tc_nt - 1) / tc_nt) >= (int64_t)tc_di.sms;
+  const int64_t tc_tiles = ((a.N + 127) / 128) * ((a.M + tc_nt - 1) / tc_nt);
+  const bool tc_wide = device_info(&tc_di) == B2Q_OK && tc_tiles >= (int64_t)tc_di.sms;
+  // narrower layers: the warp-specialized schedule with K split so that its tiles fill the GPU (when it applies)
+  const int tc_ks = tc_wide ? 1 : tc_splits(a.fmt, a.N, a.K, a.M);
+  const bool tc_split = !tc_wide && tc_ks > 1 && tc_tiles * tc_ks >= (int64_t)tc_di.sms;
   // (IQ4_NL has no tensor-core kernel: its many-column layers stay on the GEMV path)
-  if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || g_tc_min_m < 8) && !a.rx_peers && aligned(a.wq, 16) &&
-      a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
+  if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || tc_split || g_tc_min_m < 8) && !a.rx_peers &&
+      aligned(a.wq, 16) && a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
     // Measured on B200 (same box, lm_head-sized layers, M = 16..128): the warp-specialized schedule is faster everywhere
@@ -500,15 +511,19 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     const bool ws_fits = !(tc_nt == 128 && a.fmt != 1);
     if (a.x_f32 && !a.s && g_tc_schedule == 0 && ws_fits && a.workspace && aligned(a.workspace, 16) &&
         aligned(a.ws, 16) && aligned(a.x_f32, 16) && a.ldx % 4 == 0) {
-      const size_t wsb = gemm_tc_ws_bytes(a.fmt, a.K, a.M);
+      const int ks = tc_wide ? 1 : tc_ks;
+      const size_t wsb = gemm_tc_ws_bytes(a.fmt, a.N, a.K, a.M, ks);
       if (wsb && a.workspace_bytes >= wsb)
         return launch_gemm_tc_ws(a.fmt, a.wq, a.ldwq, a.ws, a.x_f32, a.ldx, a.xq_out, a.xd_out, a.y, a.ldy, a.row0,
-                                 a.N, a.K, a.M, a.workspace, stream, g_pdl != 0);
+                                 a.N, a.K, a.M, ks, a.workspace, stream, g_pdl != 0);
     }
-    if (a.x_f32) {
+    // the per-block kernel below cannot split K: a narrow layer that the split schedule could not take stays on the
+    // GEMV path
+    const bool per_block_ok = tc_wide || g_tc_min_m < 8;
+    if (a.x_f32 && per_block_ok) {
       int8_t* qo = a.xq_out;
       float* dq = a.xd_out;
-      if (!qo && a.workspace && a.workspace_bytes >= tc_act_bytes(a.fmt, a.K, a.M)) {
+      if (!qo && a.workspace && a.workspace_bytes >= tc_act_bytes(a.fmt, a.N, a.K, a.M)) {
         qo = reinterpret_cast<int8_t*>(a.workspace);
         dq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + ((size_t)a.M * a.K + 15) / 16 * 16);
       }
@@ -520,7 +535,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
         xd = dq;
       }
     }
-    if (xq) {
+    if (xq && per_block_ok) {
       GemvParams p{};
       p.wq = a.wq;
       p.ldwq = a.ldwq;
@@ -776,7 +791,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
-  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, K, M);  // GEMV ignores it
+  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, N, K, M);  // GEMV ignores it
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
 }

@@ -587,6 +587,33 @@ def test_tensor_core_persistent_tiles(cuda, fmt, n, k, m):
 
 
 
+@pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 2048, 8192, 16), ("q4_0", 1300, 8192, 9), ("tq2_0", 4096, 16384, 16),
+                                       ("q8_0", 2048, 4096, 16)])
+def test_tensor_core_split_k(cuda, fmt, n, k, m):
+    """A layer whose 128-row tiles alone do not fill the GPU runs the warp-specialized GEMM with K split into ranges
+    (three launches: prep, GEMM, the ordered combine of the ranges' partial sums), under the default planner: sampled
+    rows (row tails and padding columns included) against the C oracle within the f32 tolerance, two calls bit-identical
+    (the combine adds the ranges in order), and no bounded wait fired."""
+    import ctypes
+
+    rng = np.random.default_rng(93)
+    wq, ws = ref.random_split(fmt, rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    twq, tws, tx = _t(wq, cuda), _t(ws, cuda), _t(x, cuda)
+    before = _lib.launch_count()
+    y = host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy()
+    assert _lib.launch_count() - before == 3  # prep + split-K GEMM + combine
+    y2 = host.quant_gemv(fmt, twq, tws, tx, n, k).cpu().numpy()
+    assert _same_f32(y, y2)
+    rows = np.unique(np.concatenate([rng.choice(n, 256, replace=False), [0, 127, 128, n - 1]]))
+    oq, od = ref.quantize(fmt, x)
+    r, _ = native.gemv(fmt, wq[rows], ws[rows], oq, od, k)
+    assert ref.relerr(y[:, rows], r) <= TOL
+    code = ctypes.c_int(-1)
+    _lib.call("b2q_device_error", ctypes.byref(code), 1)
+    assert code.value == 0
+
+
 @pytest.mark.parametrize("fmt,n,k,m", [("iq4_nl", 37, 416, 3), ("iq4_nl", 1000, 4096, 1), ("iq4_nl", 300, 4096, 16)])
 def test_iq4_nl_variants_and_many_columns(cuda, fmt, n, k, m):
     """IQ4_NL (ggml's 16-level non-linear 4-bit format): the byte-wise and the byte-permute lookup variants give the
