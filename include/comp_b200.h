@@ -154,8 +154,11 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
                    int8_t* xq, float* xd, float* y, int64_t N, int64_t K, int64_t M, b2q_stream_t stream);
 
 /*
- * Split-K workspace: bytes of scratch b2q_quant_gemv_ws uses for this layer shape under the current split-K mode
- * (0 = the layer is not split; see b2q_set_splitk).
+ * Workspace bytes b2q_quant_gemv_ws uses for this layer shape (0 = none). With M at or above the tensor-core column
+ * threshold (b2q_set_gemm_min_columns) it holds the quantized activations in the MMA tile layout, and for a layer whose
+ * 128-row tiles alone do not fill the GPU also the partial sums of its K ranges (the warp-specialized GEMM then splits
+ * K, and a third launch adds the ranges in order). With fewer columns it is the GEMV's split-K scratch under the
+ * current split-K mode (0 = the layer is not split; see b2q_set_splitk).
  * Tall-K layers (rows of more than 256 16-byte chunks, e.g. K = 14336 Q4_0 or K = 28672 TQ2_0) are split over K
  * into 2-4 independent slices computed concurrently (blockIdx.y); each writes partial sums [splits][M][N] to the
  * workspace and a second kernel sums them in split order (deterministic). Part of the north star's split-K schedule
@@ -294,7 +297,10 @@ int b2q_set_gemm_min_columns(int m);
  * workspace of b2q_workspace_size bytes, K a whole number of 128-byte weight stages, and not the 128-column tiles
  * (M > 64) of Q4_0 / Q8_0, where the per-block schedule measured faster): a quantizing prep kernel writes
  * the activations in the MMA tile layout, then a persistent GEMM with producer, MMA and unpack/epilogue warps; 1 = the
- * per-block schedule. Identical results (same int32 dots, same f32 order). */
+ * per-block schedule. Identical results (same int32 dots, same f32 order), except that under the default column
+ * threshold a layer too narrow to fill the GPU with its row tiles splits K on the warp-specialized schedule (its Y then
+ * differs by the f32 order of adding the K ranges; the per-block schedule does not split, so such a layer stays on the
+ * GEMV path without the workspace). */
 int b2q_set_gemm_schedule(int schedule);
 
 /* Benchmark/tuning hook (process-wide): ring path with one column -- the CTAs of a thread-block cluster of this size
