@@ -460,60 +460,97 @@ __global__ void __launch_bounds__(320) __maxnreg__((WsCfg<FMT, NT>::MAXREG))
                                                               ((GB % PS) * 128 + t) * C::SBB);
       // The group's accumulators in chunks of CW columns of one block (blocks ascending: the sum order of the
       // reference). Up to 32 columns the loads are software-pipelined: chunk k + 1 is loaded from tensor memory while
-      // chunk k is scaled and summed (measured: Q4_0 lm_head at 16 columns 207 -> 201 us; at 64 columns the second
-      // register buffer made it slower, 518 -> 592 us, so there each chunk is loaded, waited for and used in turn).
+      // chunk k is scaled and summed (measured: Q4_0 lm_head at 16 columns 207 -> 201 us).
       constexpr int CPB = NT / CW, CH = AG * CPB;  // chunks per block, per group
       constexpr bool PIPE = NT <= 32;
-      uint32_t v[PIPE ? 2 : 1][CW];
-      auto load_chunk = [&](int k, uint32_t(&dst)[CW]) {
-        const int jb = k / CPB, c0 = (k % CPB) * CW;
-#pragma unroll
-        for (int h = 0; h < CW; h += 16)
-          tc::tmem_ld16_nowait(tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + c0 + h),
-                               *reinterpret_cast<uint32_t(*)[16]>(&dst[h]));
-      };
-      auto wait_chunk = [&](uint32_t(&dst)[CW]) {  // the wait names the registers: no use can move above it
-        tc::tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[16]>(&dst[0]));
-#pragma unroll
-        for (int h = 16; h < CW; h += 16) tc::regs_ready(*reinterpret_cast<uint32_t(*)[16]>(&dst[h]));
-      };
-      load_chunk(0, v[0]);
-      wait_chunk(v[0]);
-#pragma unroll
-      for (int k = 0; k < CH; ++k) {
-        if (PIPE && k + 1 < CH) load_chunk(k + 1, v[(k + 1) & 1]);
-        const int jb = k / CPB, c0 = (k % CPB) * CW;
-        const int j = j0 + jb;
-        const uint32_t(&vk)[CW] = v[PIPE ? k & 1 : 0];
-        const float4* dxp = reinterpret_cast<const float4*>(dk0 + j * C::DKB);
-        const float dw = f16_bits_to_f32(sc0[j]);
-        const float2 dw2 = make_float2(dw, dw);
-        // Q4_0 / Q8_0: f32(s) * dw in one fma, fl((2^23 + 2^22 + s) * dw - (2^23 + 2^22) * dw): the product
-        // 3 * 2^22 * dw of an f16 dw is exact in f32, so the fma rounds s * dw once, as the multiply would
-        const float2 mdw2 = make_float2(-kMagic * dw, -kMagic * dw);
-#pragma unroll
-        for (int q = 0; q < CW; q += 4) {
-          const float4 dx4 = dxp[(c0 + q) / 4];
-          const float dxs[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
-#pragma unroll
-          for (int e = 0; e < 4; e += 2) {
-            const int c = c0 + q + e;
-            const float2 fm = make_float2(__uint_as_float(vk[q + e]), __uint_as_float(vk[q + e + 1]));
-            const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
-            float2 a2 = make_float2(acc[c], acc[c + 1]);
-            if (FMT != 1) {
-              a2 = __ffma2_rn(__ffma2_rn(fm, dw2, mdw2), dx2, a2);  // f32(s) * dw * dx
-            } else {
-              const float2 f = __fadd2_rn(fm, make_float2(-kMagic, -kMagic));  // exact f32(s)
-              a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);                  // dx * dw * f32(s)
+      if constexpr (PIPE) {
+        auto compute_chunk = [&](int j, int c0, const uint32_t(&vk)[CW]) {
+          const float4* dxp = reinterpret_cast<const float4*>(dk0 + j * C::DKB);
+          const float dw = f16_bits_to_f32(sc0[j]);
+          const float2 dw2 = make_float2(dw, dw);
+          // Q4_0 / Q8_0: f32(s) * dw in one fma, fl((2^23 + 2^22 + s) * dw - (2^23 + 2^22) * dw): the product
+          // 3 * 2^22 * dw of an f16 dw is exact in f32, so the fma rounds s * dw once, as the multiply would
+          const float2 mdw2 = make_float2(-kMagic * dw, -kMagic * dw);
+  #pragma unroll
+          for (int q = 0; q < CW; q += 4) {
+            const float4 dx4 = dxp[(c0 + q) / 4];
+            const float dxs[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
+  #pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+              const int c = c0 + q + e;
+              const float2 fm = make_float2(__uint_as_float(vk[q + e]), __uint_as_float(vk[q + e + 1]));
+              const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
+              float2 a2 = make_float2(acc[c], acc[c + 1]);
+              if (FMT != 1) {
+                a2 = __ffma2_rn(__ffma2_rn(fm, dw2, mdw2), dx2, a2);  // f32(s) * dw * dx
+              } else {
+                const float2 f = __fadd2_rn(fm, make_float2(-kMagic, -kMagic));  // exact f32(s)
+                a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);                  // dx * dw * f32(s)
+              }
+              acc[c] = a2.x;
+              acc[c + 1] = a2.y;
             }
-            acc[c] = a2.x;
-            acc[c + 1] = a2.y;
           }
+        };
+        auto load_chunk = [&](int jb, int c0, uint32_t(&dst)[CW]) {
+  #pragma unroll
+          for (int h = 0; h < CW; h += 16)
+            tc::tmem_ld16_nowait(tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + c0 + h),
+                                 *reinterpret_cast<uint32_t(*)[16]>(&dst[h]));
+        };
+        uint32_t v[2][CW];
+        auto wait_chunk = [&](uint32_t(&dst)[CW]) {  // the wait names the registers: no use can move above it
+          tc::tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[16]>(&dst[0]));
+#pragma unroll
+          for (int h = 16; h < CW; h += 16) tc::regs_ready(*reinterpret_cast<uint32_t(*)[16]>(&dst[h]));
+        };
+        load_chunk(0, 0, v[0]);
+        wait_chunk(v[0]);
+#pragma unroll
+        for (int k = 0; k < CH; ++k) {
+          if (k + 1 < CH) load_chunk((k + 1) / CPB, ((k + 1) % CPB) * CW, v[(k + 1) & 1]);
+          compute_chunk(j0 + k / CPB, (k % CPB) * CW, v[k & 1]);
+          if (k + 1 < CH) wait_chunk(v[(k + 1) & 1]);
         }
-        if (k + 1 < CH) {
-          if (!PIPE) load_chunk(k + 1, v[0]);
-          wait_chunk(v[PIPE ? (k + 1) & 1 : 0]);
+      } else {
+        // wide tiles: one chunk at a time, in registers of its own, written out without the helper lambdas (measured:
+        // the pipelined form, and the same loop through the lambdas, spill at 64 columns and ran 518 -> 600 us)
+#pragma unroll
+        for (int jb = 0; jb < AG; ++jb) {
+#pragma unroll
+          for (int c0 = 0; c0 < NT; c0 += CW) {
+            uint32_t v[CW];
+#pragma unroll
+            for (int h = 0; h < CW; h += 16)
+              tc::tmem_ld16_nowait(tmem + lane_base + (uint32_t)(((B0 + jb) % RT) * NT + c0 + h),
+                                   *reinterpret_cast<uint32_t(*)[16]>(&v[h]));
+            tc::tmem_wait_ld();
+            const int j = j0 + jb;
+            const float4* dxp = reinterpret_cast<const float4*>(dk0 + j * C::DKB);
+            const float dw = f16_bits_to_f32(sc0[j]);
+            const float2 dw2 = make_float2(dw, dw);
+            const float2 mdw2 = make_float2(-kMagic * dw, -kMagic * dw);
+#pragma unroll
+            for (int q = 0; q < CW; q += 4) {
+              const float4 dx4 = dxp[(c0 + q) / 4];
+              const float dxs[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
+#pragma unroll
+              for (int e = 0; e < 4; e += 2) {
+                const int c = c0 + q + e;
+                const float2 fm = make_float2(__uint_as_float(v[q + e]), __uint_as_float(v[q + e + 1]));
+                const float2 dx2 = make_float2(dxs[e], dxs[e + 1]);
+                float2 a2 = make_float2(acc[c], acc[c + 1]);
+                if (FMT != 1) {
+                  a2 = __ffma2_rn(__ffma2_rn(fm, dw2, mdw2), dx2, a2);  // f32(s) * dw * dx
+                } else {
+                  const float2 f = __fadd2_rn(fm, make_float2(-kMagic, -kMagic));  // exact f32(s)
+                  a2 = __ffma2_rn(__fmul2_rn(dx2, dw2), f, a2);                  // dx * dw * f32(s)
+                }
+                acc[c] = a2.x;
+                acc[c + 1] = a2.y;
+              }
+            }
+          }
         }
       }
       // the group's accumulators start over for their next blocks (RT later): at the constant, or for TQ2_0 at the
