@@ -1028,9 +1028,11 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
 
 // ------------------------------------------------------------------------------------------------------------------
 // Cluster-shared activation prologue: the CTAs of a thread-block cluster split the activation chunks, each quantizes
-// its share once (the same load_x_direct arithmetic) and stores the q8 chunk into every member's shared memory
-// (distributed shared memory stores, no multicast loads), then every thread reads its own chunk back into registers.
-// Per SM this loads and quantizes 1/cluster of the activations instead of all of them.
+// its share once (the same load_x_direct arithmetic), keeps it in registers and sends the q8 chunk into every other
+// member's shared memory with asynchronous distributed-shared-memory stores (st.async, no multicast loads) that
+// complete bytes on the receiver's mbarrier; a thread whose chunk a peer computes waits on that mbarrier (bounded) and
+// reads the chunk. No cluster-wide barrier on the critical path: the one that makes the mbarriers visible to the peers
+// runs before the dependency wait. Per SM this loads and quantizes 1/cluster of the activations instead of all.
 // ------------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -1049,6 +1051,18 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
 __device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
   asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
 }
+// asynchronous store into another cluster member's shared memory; its bytes complete on that member's mbarrier rbar
+// (both addresses mapped to the member with cluster_map)
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v2(uint32_t addr, uint32_t a, uint32_t b, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "r"(a), "r"(b), "r"(rbar)
+               : "memory");
+}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -1060,40 +1074,57 @@ __host__ __device__ constexpr uint32_t cluster_slot_bytes(int C) {
   return (uint32_t)C * (16u * Fmt<FMT>::kFields + 8u);
 }
 
+// Chunks of the activations this cluster member quantizes: warps [rank * per, (rank + 1) * per) (whole warps, for the
+// quad shuffles of the q8_K prologue), and the bytes it receives from the other members.
+__device__ __forceinline__ int cluster_chunks_per_member(int C, int cs) { return (((C + cs - 1) / cs) + 31) & ~31; }
 template <int FMT>
-__device__ __forceinline__ void cluster_share_x(const GemvParams& p, uint32_t slots, XChunk& xr) {
+__device__ __forceinline__ uint32_t cluster_recv_bytes(int C, int cs, int rank) {
+  const int per = cluster_chunks_per_member(C, cs);
+  const int own = max(0, min(per, C - rank * per));
+  return (uint32_t)(C - own) * (16u * Fmt<FMT>::kFields + 8u);
+}
+
+// xbar: this CTA's mbarrier for the chunks the other members send (initialized with one arrival that expects
+// cluster_recv_bytes, made visible to the cluster before any member sends). Returns false if that wait timed out.
+template <int FMT>
+__device__ __forceinline__ bool cluster_share_x(const GemvParams& p, uint32_t slots, uint32_t xbar, XChunk& xr) {
   const int C = p.C, cs = p.cluster;
-  const int per = (((C + cs - 1) / cs) + 31) & ~31;  // chunks per member, in whole warps (the quad shuffles)
+  const int per = cluster_chunks_per_member(C, cs);
   const int c = (int)threadIdx.x;
   const int wfirst = c & ~31;
-  if (wfirst < C && wfirst / per == (int)cluster_ctarank()) {  // warp-uniform
-    XChunk o;
-    load_x_direct<FMT>(p, c, c < C, o);
-    if (c < C) {
-      for (int q = 0; q < cs; ++q) {
-#pragma unroll
-        for (int j = 0; j < Fmt<FMT>::kFields; ++j)
-          st_cluster_v4(cluster_map(slots + (uint32_t)(j * C + c) * 16u, (uint32_t)q), o.x[j]);
-        st_cluster_v2(cluster_map(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u, (uint32_t)q),
-                      (uint32_t)o.sum, __float_as_uint(o.dx));
-      }
-    }
-  }
-  cluster_sync_all();  // every member's slots are complete (release / acquire at cluster scope)
+  const int me = (int)cluster_ctarank();
 #pragma unroll
   for (int j = 0; j < 4; ++j) xr.x[j] = make_uint4(0u, 0u, 0u, 0u);
   xr.sum = 0;
   xr.dx = 0.f;
-  if (c < C) {
+  if (wfirst < C && wfirst / per == me) {  // warp-uniform: this member quantizes the warp's chunks
+    XChunk o;
+    load_x_direct<FMT>(p, c, c < C, o);
+    if (c < C) {
+      for (int q = 0; q < cs; ++q) {
+        if (q == me) continue;
+        const uint32_t rbar = cluster_map(xbar, (uint32_t)q);
 #pragma unroll
-    for (int j = 0; j < Fmt<FMT>::kFields; ++j) xr.x[j] = lds_v4(slots + (uint32_t)(j * C + c) * 16u);
-    uint32_t a, b;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
-                 : "=r"(a), "=r"(b)
-                 : "r"(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u));
-    xr.sum = (int)a;
-    xr.dx = __uint_as_float(b);
+        for (int j = 0; j < Fmt<FMT>::kFields; ++j)
+          st_async_v4(cluster_map(slots + (uint32_t)(j * C + c) * 16u, (uint32_t)q), o.x[j], rbar);
+        st_async_v2(cluster_map(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u, (uint32_t)q),
+                    (uint32_t)o.sum, __float_as_uint(o.dx), rbar);
+      }
+      xr = o;
+    }
+    return true;
   }
+  if (c >= C) return true;
+  if (!mbar_wait(xbar, 0u, kWaitLimit)) return false;  // every other member's chunks have landed (acquire)
+#pragma unroll
+  for (int j = 0; j < Fmt<FMT>::kFields; ++j) xr.x[j] = lds_v4(slots + (uint32_t)(j * C + c) * 16u);
+  uint32_t a, b;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+               : "=r"(a), "=r"(b)
+               : "r"(slots + (uint32_t)Fmt<FMT>::kFields * C * 16u + (uint32_t)c * 8u));
+  xr.sum = (int)a;
+  xr.dx = __uint_as_float(b);
+  return true;
 }
 
 template <int FMT, int MC, bool XREG>
@@ -1205,6 +1236,7 @@ template <int FMT, int R, int MC, bool XREG>
 __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
+  __shared__ __align__(8) uint64_t s_xbar;  // clusters: the other members' activation chunks have landed
   const int C = p.C, S = p.stages;
   const int Mx = XREG ? 0 : p.M;  // XREG: activations never touch shared memory
   const int nblk = (int)(p.K / Fmt<FMT>::kBlock);
@@ -1223,9 +1255,17 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   const uint32_t ring_addr = smem_addr(ring), bar_addr = smem_addr(bars);
   const uint64_t pol = evict_first_policy();
 
+  const bool share = XREG && p.cluster > 1;
+  const uint32_t xbar = smem_addr(&s_xbar);
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < S; ++s) mbar_init(bar_addr + 8 * s, 1);
+    if (share) {
+      mbar_init(xbar, 1);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
+                   "r"(cluster_recv_bytes<FMT>(C, p.cluster, (int)cluster_ctarank()))
+                   : "memory");
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // S - 1 groups before the dependency wait; the last stage is filled after the activation prologue. Filling the
     // whole ring up front measured slower (timestamped B200 runs: the extra bulk traffic delays both the preceding
@@ -1233,15 +1273,26 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
     for (int64_t j = 0; j < min((int64_t)(S - 1), ngroups); ++j)
       issue_group<FMT, R>(p, g_begin + j, ring_addr + (uint32_t)j * p.stage_bytes, bar_addr + 8 * (uint32_t)j, pol);
   }
+  // XREG: publish the barrier init and s_abort before the dependency wait (clusters: to every member, before any
+  // member sends chunks), so that the activation prologue after it needs no barrier
+  if (XREG) {
+    if (share)
+      cluster_sync_all();
+    else
+      __syncthreads();
+  }
   pdl_wait_then_trigger();
   const int rx_parity = call_parity(p);
   XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
   if (XREG) {
-    if (p.cluster > 1)
-      cluster_share_x<FMT>(p, smem_addr(slots), xr);
-    else
+    if (share) {
+      if (!cluster_share_x<FMT>(p, smem_addr(slots), xbar, xr)) {
+        s_abort = 1;
+        atomicCAS(&g_device_error, 0, kErrTimeout);
+      }
+    } else {
       load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
-    __syncthreads();  // publishes the barrier init and s_abort
+    }
   } else {
     stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
   }

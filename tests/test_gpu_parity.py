@@ -400,9 +400,10 @@ def test_warp_rows_path_matches_oracle(cuda, fmt, n, k):
                                      ("q4_0", 300, 28672), ("tq2_0", 5, 4096), ("tq2_0", 64, 14336),
                                      ("q8_0", 1001, 4096), ("q8_0", 300, 14336), ("iq4_nl", 1001, 4096)])
 def test_cluster_shared_prologue_identical(cuda, fmt, n, k):
-    """No cluster, and clusters of 2, 4 and 8 CTAs splitting the fused activation prologue (each member quantizes its share and stores
-    it into every member's shared memory): the same quantized bytes written out, bit-identical Y, the bounded waits
-    never fire -- also when the layer has fewer row groups than the cluster has members."""
+    """No cluster, and clusters of 2, 4 and 8 CTAs splitting the fused activation prologue (each member quantizes its
+    share and sends it into every other member's shared memory, completing on that member's mbarrier): the same
+    quantized bytes written out, bit-identical Y, the bounded waits never fire -- also when the layer has fewer row
+    groups than the cluster has members."""
     import ctypes
 
     wq, ws, x, twq, tws, tx = _layer(fmt, n, k, 1, 41, cuda)
