@@ -589,7 +589,7 @@ def test_tensor_core_persistent_tiles(cuda, fmt, n, k, m):
 
 
 @pytest.mark.parametrize("fmt,n,k,m", [("q4_0", 2048, 8192, 16), ("q4_0", 1300, 8192, 9), ("tq2_0", 4096, 16384, 16),
-                                       ("q8_0", 2048, 4096, 16)])
+                                       ("q8_0", 2048, 4096, 16), ("q4_0", 2048, 8192, 40), ("tq2_0", 4096, 16384, 100)])
 def test_tensor_core_split_k(cuda, fmt, n, k, m):
     """A layer whose 128-row tiles alone do not fill the GPU runs the warp-specialized GEMM with K split into ranges
     (three launches: prep, GEMM, the ordered combine of the ranges' partial sums), under the default planner: sampled
