@@ -1044,13 +1044,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(local_addr), "r"(rank));
   return a;
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
-  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
 // asynchronous store into another cluster member's shared memory; its bytes complete on that member's mbarrier rbar
 // (both addresses mapped to the member with cluster_map)
 __device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t rbar) {
