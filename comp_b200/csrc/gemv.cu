@@ -462,6 +462,12 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
 // Columns from which a layer runs on the tensor-core GEMM (0 = never). Below it the GEMV kernels, which re-read the
 // weights per group of 4 columns, are the better fit.
 static std::atomic<int> g_tc_min_m{8};
+// Under the default threshold, fused calls that can take the warp-specialized schedule (a workspace, f32 activations)
+// already do from this many columns. Measured on B200 (same box, GEMV path vs tensor cores, us): Q4_0 lm_head
+// 128256x8192 at M = 2 / 3 / 4 / 6: 182 / 249 / 352 / 534 vs 203; TQ2_0 gate_up 57344x8192 at M = 2 / 3 / 6: 102 / 133
+// / 468 vs 83; TQ2_0 down 8192x28672 (K split) at M = 3 / 6: 82 / 139 vs ~45. The per-block schedule keeps the
+// threshold.
+constexpr int kWsMinColumns = 3;
 // Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
 static std::atomic<int> g_tc_schedule{0};
 
@@ -500,17 +506,20 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   // narrower layers: the warp-specialized schedule with K split so that its tiles fill the GPU (when it applies)
   const int tc_ks = tc_wide ? 1 : tc_splits(a.fmt, a.N, a.K, a.M);
   const bool tc_split = !tc_wide && tc_ks > 1 && tc_tiles * tc_ks >= (int64_t)tc_di.sms;
-  // (IQ4_NL has no tensor-core kernel: its many-column layers stay on the GEMV path)
-  if (g_tc_min_m > 0 && a.M >= g_tc_min_m && (tc_wide || tc_split || g_tc_min_m < 8) && !a.rx_peers &&
-      aligned(a.wq, 16) && a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
+  const int tc_min = g_tc_min_m.load();
+  const bool ws_call = a.x_f32 && !a.s && g_tc_schedule == 0 && a.workspace && aligned(a.workspace, 16) &&
+                       aligned(a.ws, 16) && aligned(a.x_f32, 16) && a.ldx % 4 == 0;
+  const int tc_from = (tc_min == 8 && ws_call) ? kWsMinColumns : tc_min;  // columns from which the TC path applies
+  // (IQ4_NL and Q4_K have no tensor-core kernel: their many-column layers stay on the GEMV path)
+  if (tc_min > 0 && a.M >= tc_from && (tc_wide || tc_split || tc_min < 8) && !a.rx_peers && aligned(a.wq, 16) &&
+      a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
     const int8_t* xq = a.xq;
     const float* xd = a.xd;
     // Measured on B200 (same box, lm_head-sized layers, M = 16..128): the warp-specialized schedule is faster everywhere
     // except 128-column tiles of the 32-value block formats (Q4_0 1683 vs 1493 us, Q8_0 907 vs 772 us at M = 128),
     // where the per-block kernel stays; TQ2_0 keeps it at every width (198 vs 439 us at M = 128).
     const bool ws_fits = !(tc_nt == 128 && a.fmt != 1);
-    if (a.x_f32 && !a.s && g_tc_schedule == 0 && ws_fits && a.workspace && aligned(a.workspace, 16) &&
-        aligned(a.ws, 16) && aligned(a.x_f32, 16) && a.ldx % 4 == 0) {
+    if (ws_call && ws_fits) {
       const int ks = tc_wide ? 1 : tc_ks;
       const size_t wsb = gemm_tc_ws_bytes(a.fmt, a.N, a.K, a.M, ks);
       if (wsb && a.workspace_bytes >= wsb)
@@ -519,7 +528,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
     }
     // the per-block kernel below cannot split K: a narrow layer that the split schedule could not take stays on the
     // GEMV path
-    const bool per_block_ok = tc_wide || g_tc_min_m < 8;
+    const bool per_block_ok = (tc_wide || tc_min < 8) && a.M >= tc_min;
     if (a.x_f32 && per_block_ok) {
       int8_t* qo = a.xq_out;
       float* dq = a.xd_out;
@@ -791,7 +800,17 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
-  if (g_tc_min_m > 0 && M >= g_tc_min_m && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, N, K, M);  // GEMV ignores it
+  const int tc_min = g_tc_min_m.load();
+  if (tc_min > 0 && M >= tc_min && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, N, K, M);  // GEMV ignores it
+  // below the threshold, from 3 columns at the default one: the tensor-core workspace where the warp-specialized
+  // schedule would take this layer (its tiles, K split if need be, fill the GPU), else the GEMV's split-K scratch
+  if (tc_min == 8 && M >= kWsMinColumns && fmt != 3 && fmt != 4 && gemm_tc_ws_bytes(fmt, N, K, M, 1) > 0) {
+    DeviceInfo di;
+    const int NT = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+    const int64_t tiles = ((N + 127) / 128) * ((M + NT - 1) / NT);
+    if (device_info(&di) == B2Q_OK && tiles * gemm_tc_ws_splits(fmt, N, K, M) >= (int64_t)di.sms)
+      return tc_act_bytes(fmt, N, K, M);
+  }
   const int sp = choose_splits(fmt, K, M);
   return sp > 1 ? (size_t)sp * (size_t)M * (size_t)N * sizeof(float) : 0;
 }
