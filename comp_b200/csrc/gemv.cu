@@ -465,9 +465,10 @@ static std::atomic<int> g_tc_min_m{8};
 // Under the default threshold, fused calls that can take the warp-specialized schedule (a workspace, f32 activations)
 // already do from this many columns. Measured on B200 (same box, GEMV path vs tensor cores, us): Q4_0 lm_head
 // 128256x8192 at M = 2 / 3 / 4 / 6: 182 / 249 / 352 / 534 vs 203; TQ2_0 gate_up 57344x8192 at M = 2 / 3 / 6: 102 / 133
-// / 468 vs 83; TQ2_0 down 8192x28672 (K split) at M = 3 / 6: 82 / 139 vs ~45. The per-block schedule keeps the
-// threshold.
-constexpr int kWsMinColumns = 3;
+// / 468 vs 83; TQ2_0 down 8192x28672 (K split) at M = 2 / 3 / 6: 61 / 82 / 139 vs ~45. So TQ2_0 from 2 columns, the
+// 32-value block formats from 3 (Q4_0 and Q8_0 lm_head at M = 2: GEMV 182 vs 203, 103 vs 139). The per-block schedule
+// keeps the threshold.
+static int ws_min_columns(int fmt) { return fmt == 1 ? 2 : 3; }
 // Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
 static std::atomic<int> g_tc_schedule{0};
 
@@ -509,7 +510,7 @@ static int launch_gemv(const LaunchArgs& a, cudaStream_t stream) {
   const int tc_min = g_tc_min_m.load();
   const bool ws_call = a.x_f32 && !a.s && g_tc_schedule == 0 && a.workspace && aligned(a.workspace, 16) &&
                        aligned(a.ws, 16) && aligned(a.x_f32, 16) && a.ldx % 4 == 0;
-  const int tc_from = (tc_min == 8 && ws_call) ? kWsMinColumns : tc_min;  // columns from which the TC path applies
+  const int tc_from = (tc_min == 8 && ws_call) ? ws_min_columns(a.fmt) : tc_min;  // columns from which TC applies
   // (IQ4_NL and Q4_K have no tensor-core kernel: their many-column layers stay on the GEMV path)
   if (tc_min > 0 && a.M >= tc_from && (tc_wide || tc_split || tc_min < 8) && !a.rx_peers && aligned(a.wq, 16) &&
       a.ldwq % 16 == 0 && a.fmt != 3 && a.fmt != 4) {
@@ -802,9 +803,9 @@ size_t b2q_workspace_size(int fmt, int64_t N, int64_t K, int64_t M) {
   if (!fmt_ok(fmt) || N <= 0 || K <= 0 || M <= 0 || (K % fmt_block(fmt))) return 0;
   const int tc_min = g_tc_min_m.load();
   if (tc_min > 0 && M >= tc_min && fmt != 3 && fmt != 4) return tc_act_bytes(fmt, N, K, M);  // GEMV ignores it
-  // below the threshold, from 3 columns at the default one: the tensor-core workspace where the warp-specialized
+  // below the threshold, from 2-3 columns at the default one: the tensor-core workspace where the warp-specialized
   // schedule would take this layer (its tiles, K split if need be, fill the GPU), else the GEMV's split-K scratch
-  if (tc_min == 8 && M >= kWsMinColumns && fmt != 3 && fmt != 4 && gemm_tc_ws_bytes(fmt, N, K, M, 1) > 0) {
+  if (tc_min == 8 && M >= ws_min_columns(fmt) && fmt != 3 && fmt != 4 && gemm_tc_ws_bytes(fmt, N, K, M, 1) > 0) {
     DeviceInfo di;
     const int NT = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
     const int64_t tiles = ((N + 127) / 128) * ((M + NT - 1) / NT);
