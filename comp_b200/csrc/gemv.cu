@@ -235,7 +235,6 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
   int rc = device_info(&di);
   if (rc) return rc;
   const int C = (int)(K / fmt_chunk_values(fmt));
-  const int MC = M == 1 ? 1 : kMaxColumns;
   int CPT = (C + kMaxThreads - 1) / kMaxThreads;
   if (g_tune_cpt > 0) CPT = g_tune_cpt;
   const int T = std::min(kMaxThreads, ((C + CPT - 1) / CPT + 31) / 32 * 32);
@@ -247,16 +246,20 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
   Plan best{};
   double best_score = -1.0;
   const int cand[5] = {16, 8, 4, 2, 1};
-  const bool xreg = (M == 1) && CPT == 1;
   for (int pass = 0; pass < 2 && best_score < 0; ++pass) {
     const bool ring = use_ring && pass == 0;
     if (pass == 1 && (g_tune_path == 1 || fmt == 4)) break;  // Q4_K: ring only
+    // one chunk per thread: the activations in registers (XREG), for one column, or on the ring path for two (each
+    // thread holds its chunk of both: no shared-memory staging, no re-quantization per column group); otherwise
+    // staged in shared memory, 4 columns per pass
+    const bool xreg = CPT == 1 && (M == 1 || (M == 2 && ring));
+    const int MC = M == 1 ? 1 : xreg ? 2 : kMaxColumns;
     for (int ci = 0; ci < 5; ++ci) {
       const int R = cand[ci];
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
       // 16-row groups: ring path, one column, one chunk per thread, CTAs of at most 256 threads. Measured on B200:
       // TQ2_0 gate_up 2% faster than 8 rows, Q4_0 lm_head unchanged -- so TQ2_0 by default, Q4_0 on request.
-      if (R == 16 && (!ring || !xreg || T > 256 || (fmt != 1 && g_tune_rows != 16))) continue;
+      if (R == 16 && (!ring || !xreg || MC != 1 || T > 256 || (fmt != 1 && g_tune_rows != 16))) continue;
       const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T, xreg);
       const int64_t groups = (N + R - 1) / R;
       int stages = 0;
@@ -274,7 +277,8 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
       // short and the pair's exchange and barrier cost more than they save (measured on B200: gate_up 57344x8192
       // 23.6 vs 24.3 us, its 8-GPU slice 7168x8192 6.3 vs 7.5 us; K = 28672 rows and Q4_0 keep pairs)
       const int auto_cs = (fmt == 1 && C <= 128) ? 1 : 2;
-      if (ring && xreg) cs = g_tune_cluster > 1 ? g_tune_cluster.load() : (g_tune_cluster == 0 ? auto_cs : 1);
+      if (ring && xreg && MC == 1)
+        cs = g_tune_cluster > 1 ? g_tune_cluster.load() : (g_tune_cluster == 0 ? auto_cs : 1);
       const size_t slot = fmt_slot_bytes(fmt, C);
       if (cs > 1 && smem + slot > (size_t)di.max_smem_optin && g_tune_cluster == 0) cs = 1;
       if (cs > 1) smem += slot;
@@ -463,12 +467,11 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
 // weights per group of 4 columns, are the better fit.
 static std::atomic<int> g_tc_min_m{8};
 // Under the default threshold, fused calls that can take the warp-specialized schedule (a workspace, f32 activations)
-// already do from this many columns. Measured on B200 (same box, GEMV path vs tensor cores, us): Q4_0 lm_head
-// 128256x8192 at M = 2 / 3 / 4 / 6: 182 / 249 / 352 / 534 vs 203; TQ2_0 gate_up 57344x8192 at M = 2 / 3 / 6: 102 / 133
-// / 468 vs 83; TQ2_0 down 8192x28672 (K split) at M = 2 / 3 / 6: 61 / 82 / 139 vs ~45. So TQ2_0 from 2 columns, the
-// 32-value block formats from 3 (Q4_0 and Q8_0 lm_head at M = 2: GEMV 182 vs 203, 103 vs 139). The per-block schedule
-// keeps the threshold.
-static int ws_min_columns(int fmt) { return fmt == 1 ? 2 : 3; }
+// already do from 3 columns. Measured on B200 (same box, GEMV path vs tensor cores, us): Q4_0 lm_head 128256x8192 at
+// M = 3 / 4 / 6: 249 / 352 / 534 vs 203; TQ2_0 gate_up 57344x8192 at M = 3 / 6: 133 / 468 vs 83; TQ2_0 down 8192x28672
+// (K split) at M = 3 / 6: 82 / 139 vs ~45. Two columns stay on the GEMV, whose register path holds both columns'
+// chunks (Q4_0 lm_head 97 vs 203, gate_up 38 vs 83, down 24 vs 44). The per-block schedule keeps the threshold.
+static int ws_min_columns(int) { return 3; }
 // Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
 static std::atomic<int> g_tc_schedule{0};
 

@@ -744,7 +744,7 @@ __device__ __forceinline__ void load_unit(const GemvParams& p, int64_t g, int i,
 // threads of the block by xor-shuffles (all lanes of the warp take part; chunks past the row end are zero).
 // CTA 0 also stores the quantized activations when xq_out is given.
 template <int FMT>
-__device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool valid, XChunk& o) {
+__device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool valid, XChunk& o, int m = 0) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) o.x[j] = make_uint4(0u, 0u, 0u, 0u);
   o.sum = 0;
@@ -754,23 +754,23 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   if (p.x_f32 == nullptr) {
     if (!valid) return;
     if (Fmt<FMT>::kLayout == 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 32);
+      const uint4* src = reinterpret_cast<const uint4*>((Split<FMT>::xq(p) + (int64_t)m * p.ldxq) + (int64_t)c * 32);
       o.x[0] = src[0];
       o.x[1] = src[1];
-      o.dx = Split<FMT>::xd(p)[c >> Fmt<FMT>::kChunkShift];
+      o.dx = (Split<FMT>::xd(p) + (int64_t)m * p.ldxd)[c >> Fmt<FMT>::kChunkShift];
       if (FMT == 3) {  // no offset term; the chunk interleaved for the level lookups
         iq4nl_interleave(o.x);
         return;
       }
     } else if (FMT == 2) {
-      o.x[0] = *reinterpret_cast<const uint4*>(Split<FMT>::xq(p) + (int64_t)c * 16);
-      o.dx = Split<FMT>::xd(p)[c >> 1];
+      o.x[0] = *reinterpret_cast<const uint4*>((Split<FMT>::xq(p) + (int64_t)m * p.ldxq) + (int64_t)c * 16);
+      o.dx = (Split<FMT>::xd(p) + (int64_t)m * p.ldxd)[c >> 1];
     } else {
       const int b = c >> 2, cc = c & 3;
-      const int8_t* base = Split<FMT>::xq(p) + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
+      const int8_t* base = (Split<FMT>::xq(p) + (int64_t)m * p.ldxq) + (int64_t)b * 256 + (cc >> 1) * 128 + (cc & 1) * 16;
 #pragma unroll
       for (int j = 0; j < 4; ++j) o.x[j] = *reinterpret_cast<const uint4*>(base + j * 32);
-      o.dx = Split<FMT>::xd(p)[b];
+      o.dx = (Split<FMT>::xd(p) + (int64_t)m * p.ldxd)[b];
     }
     int sum = 0;
 #pragma unroll
@@ -785,7 +785,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     float4 v[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      v[i] = valid ? reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 16)[i]
+      v[i] = valid ? reinterpret_cast<const float4*>((Split<FMT>::xf(p) + (int64_t)m * p.ldx) + (int64_t)c * 16)[i]
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     float amax = 0.f;
 #pragma unroll
@@ -806,8 +806,8 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     o.x[0] = make_uint4(w[0], w[1], w[2], w[3]);
     o.dx = q8_0_stored_scale(d);
     if (writer) {
-      *reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 16) = o.x[0];
-      if ((c & 1) == 0 && p.xd_out) Split<FMT>::xd_out(p)[c >> 1] = o.dx;
+      *reinterpret_cast<uint4*>((Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq) + (int64_t)c * 16) = o.x[0];
+      if ((c & 1) == 0 && p.xd_out) (Split<FMT>::xd_out(p) + (int64_t)m * p.ldxd)[c >> 1] = o.dx;
     }
     return;
   }
@@ -819,7 +819,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     float v[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 f = valid ? *reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 32 + 4 * i)
+      const float4 f = valid ? *reinterpret_cast<const float4*>((Split<FMT>::xf(p) + (int64_t)m * p.ldx) + (int64_t)c * 32 + 4 * i)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
       v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
     }
@@ -887,16 +887,16 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     o.sum = sum;
     o.dx = nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
     if (writer) {
-      uint4* dst = reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 32);
+      uint4* dst = reinterpret_cast<uint4*>((Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq) + (int64_t)c * 32);
       dst[0] = o.x[0];
       dst[1] = o.x[1];
-      if ((c & 7) == 0 && p.xd_out) Split<FMT>::xd_out(p)[c >> 3] = o.dx;
+      if ((c & 7) == 0 && p.xd_out) (Split<FMT>::xd_out(p) + (int64_t)m * p.ldxd)[c >> 3] = o.dx;
     }
     return;
   }
   if (Fmt<FMT>::kLayout == 0) {
     if (!valid) return;
-    const float4* src = reinterpret_cast<const float4*>(Split<FMT>::xf(p) + (int64_t)c * 32);
+    const float4* src = reinterpret_cast<const float4*>((Split<FMT>::xf(p) + (int64_t)m * p.ldx) + (int64_t)c * 32);
     float4 v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = src[i];
@@ -921,10 +921,10 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
     o.sum = Fmt<FMT>::kOffset * sum;
     o.dx = q8_0_stored_scale(d);
     if (writer) {
-      uint4* dst = reinterpret_cast<uint4*>(Split<FMT>::xq_out(p) + (int64_t)c * 32);
+      uint4* dst = reinterpret_cast<uint4*>((Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq) + (int64_t)c * 32);
       dst[0] = o.x[0];
       dst[1] = o.x[1];
-      if (p.xd_out) Split<FMT>::xd_out(p)[c] = o.dx;
+      if (p.xd_out) (Split<FMT>::xd_out(p) + (int64_t)m * p.ldxd)[c] = o.dx;
     }
     if (FMT == 3) iq4nl_interleave(o.x);  // after the natural-order XQ write-out
     return;
@@ -934,7 +934,7 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   const int vbase = (cc >> 1) * 128 + (cc & 1) * 16;
   float v[4][16];
   if (valid) {
-    const float* base = Split<FMT>::xf(p) + (int64_t)b * 256 + vbase;
+    const float* base = (Split<FMT>::xf(p) + (int64_t)m * p.ldx) + (int64_t)b * 256 + vbase;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -1019,10 +1019,10 @@ __device__ __forceinline__ void load_x_direct(const GemvParams& p, int c, bool v
   o.sum = sum;
   o.dx = nz ? __fdiv_rn(1.0f, iscale) : 0.0f;
   if (writer) {
-    int8_t* dst = Split<FMT>::xq_out(p) + (int64_t)b * 256 + vbase;
+    int8_t* dst = (Split<FMT>::xq_out(p) + (int64_t)m * p.ldxq) + (int64_t)b * 256 + vbase;
 #pragma unroll
     for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + j * 32) = o.x[j];
-    if (cc == 0 && p.xd_out) Split<FMT>::xd_out(p)[b] = o.dx;
+    if (cc == 0 && p.xd_out) (Split<FMT>::xd_out(p) + (int64_t)m * p.ldxd)[b] = o.dx;
   }
 }
 
@@ -1122,9 +1122,10 @@ __device__ __forceinline__ bool cluster_share_x(const GemvParams& p, uint32_t sl
 
 template <int FMT, int MC, bool XREG>
 __device__ __forceinline__ void get_x(const GemvParams& p, const uint8_t* xs, const int* xsum, const float* xscale,
-                                      const XChunk& xr, int c, bool valid, XChunk (&xc)[MC]) {
+                                      const XChunk (&xr)[MC], int c, bool valid, XChunk (&xc)[MC]) {
   if (XREG) {
-    xc[0] = xr;
+#pragma unroll
+    for (int m = 0; m < MC; ++m) xc[m] = xr[m];
   } else {
 #pragma unroll
     for (int m = 0; m < MC; ++m)
@@ -1150,10 +1151,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_reg_kernel(const GemvPara
   load_unit<FMT, R>(p, g_begin, 0, g_begin < g_end, cur);
   pdl_wait_then_trigger();
   const int parity = call_parity(p);
-  XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
-  if (XREG)
-    load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
-  else
+  XChunk xr[MC];  // XREG: this thread's only chunk (CPT == 1) of each column, for the whole kernel
+  if (XREG) {
+#pragma unroll
+    for (int m = 0; m < MC; ++m) load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C && m < p.M, xr[m], m);
+  } else
     stage_activations<FMT>(p, xs, xsum, xscale);
 
   float acc[R * MC];
@@ -1248,7 +1250,7 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   const uint32_t ring_addr = smem_addr(ring), bar_addr = smem_addr(bars);
   const uint64_t pol = evict_first_policy();
 
-  const bool share = XREG && p.cluster > 1;
+  const bool share = XREG && MC == 1 && p.cluster > 1;
   const uint32_t xbar = smem_addr(&s_xbar);
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -1276,15 +1278,17 @@ __global__ void B2Q_RING_BOUNDS gemv_ring_kernel(const GemvParams p) {
   }
   pdl_wait_then_trigger();
   const int rx_parity = call_parity(p);
-  XChunk xr;  // XREG: this thread's only chunk (CPT == 1), for the whole kernel
+  XChunk xr[MC];  // XREG: this thread's only chunk (CPT == 1) of each column, for the whole kernel
   if (XREG) {
     if (share) {
-      if (!cluster_share_x<FMT>(p, smem_addr(slots), xbar, xr)) {
+      if (!cluster_share_x<FMT>(p, smem_addr(slots), xbar, xr[0])) {
         s_abort = 1;
         atomicCAS(&g_device_error, 0, kErrTimeout);
       }
     } else {
-      load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C, xr);
+#pragma unroll
+      for (int m = 0; m < MC; ++m)
+        load_x_direct<FMT>(p, (int)threadIdx.x, (int)threadIdx.x < C && m < p.M, xr[m], m);
     }
   } else {
     stage_activations<FMT>(p, xs, xsum, xscale);  // ends with __syncthreads (also publishes the barrier init)
