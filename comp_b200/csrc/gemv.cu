@@ -249,17 +249,18 @@ static int make_plan_uncached(int fmt, bool bytes, bool ring_ok, int64_t N, int6
   for (int pass = 0; pass < 2 && best_score < 0; ++pass) {
     const bool ring = use_ring && pass == 0;
     if (pass == 1 && (g_tune_path == 1 || fmt == 4)) break;  // Q4_K: ring only
-    // one chunk per thread: the activations in registers (XREG), for one column, or on the ring path for two (each
-    // thread holds its chunk of both: no shared-memory staging, no re-quantization per column group); otherwise
-    // staged in shared memory, 4 columns per pass
-    const bool xreg = CPT == 1 && (M == 1 || (M == 2 && ring));
-    const int MC = M == 1 ? 1 : xreg ? 2 : kMaxColumns;
+    // one chunk per thread: the activations in registers (XREG), for one column, or on the ring path for two to four
+    // (each thread holds its chunk of every column: no shared-memory staging; TQ2_0 only for two, its 64-value
+    // chunks spill at four); otherwise staged in shared memory, 4 columns per pass
+    const bool xreg = CPT == 1 && (M == 1 || (ring && (M == 2 || (M <= 4 && fmt != 1))));
+    const int MC = M == 1 ? 1 : (xreg && M == 2) ? 2 : kMaxColumns;
     for (int ci = 0; ci < 5; ++ci) {
       const int R = cand[ci];
       if (g_tune_rows > 0 && R != g_tune_rows) continue;
       // 16-row groups: ring path, one column, one chunk per thread, CTAs of at most 256 threads. Measured on B200:
       // TQ2_0 gate_up 2% faster than 8 rows, Q4_0 lm_head unchanged -- so TQ2_0 by default, Q4_0 on request.
       if (R == 16 && (!ring || !xreg || MC != 1 || T > 256 || (fmt != 1 && g_tune_rows != 16))) continue;
+      if (xreg && MC == 4 && R > 4 && fmt != 2) continue;  // the four-column register kernels spill above 4 rows
       const size_t xb = x_region_bytes(fmt, K, M, C, R, MC, T, xreg);
       const int64_t groups = (N + R - 1) / R;
       int stages = 0;
@@ -467,11 +468,13 @@ int launch_gemm_tc_ws(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* w
 // weights per group of 4 columns, are the better fit.
 static std::atomic<int> g_tc_min_m{8};
 // Under the default threshold, fused calls that can take the warp-specialized schedule (a workspace, f32 activations)
-// already do from 3 columns. Measured on B200 (same box, GEMV path vs tensor cores, us): Q4_0 lm_head 128256x8192 at
-// M = 3 / 4 / 6: 249 / 352 / 534 vs 203; TQ2_0 gate_up 57344x8192 at M = 3 / 6: 133 / 468 vs 83; TQ2_0 down 8192x28672
-// (K split) at M = 3 / 6: 82 / 139 vs ~45. Two columns stay on the GEMV, whose register path holds both columns'
-// chunks (Q4_0 lm_head 97 vs 203, gate_up 38 vs 83, down 24 vs 44). The per-block schedule keeps the threshold.
-static int ws_min_columns(int) { return 3; }
+// already do from this many columns. Measured on B200 (same box, us): the GEMV's register path (each thread holds its
+// chunk of every column) at M = 2 / 3 / 4 against the tensor cores: Q4_0 lm_head 128256x8192 97 / 162 / 185 vs 203,
+// Q8_0 lm_head 128256x4096 79 / 87 / 95 vs 139, and from M = 5 (staged in shared memory again) 273 vs 203, 174 vs 139;
+// TQ2_0 (whose four-column register kernels spill) gate_up 57344x8192 at M = 2 / 3: 38 / 133 vs 83, down 8192x28672
+// 24 / 82 vs 44 (K split). So TQ2_0 from 3 columns, the other formats from 5. The per-block schedule keeps the
+// threshold.
+static int ws_min_columns(int fmt) { return fmt == 1 ? 3 : 5; }
 // Fused tensor-core schedule: 0 = warp-specialized where it applies (default), 1 = always the per-block schedule
 static std::atomic<int> g_tc_schedule{0};
 

@@ -22,6 +22,14 @@ static KernelFn pick(int R, int MC) {
       default: return gemv_ring_kernel<FMT, 8, 2, true>;
     }
   }
+  if (MC == 4 && XREG) {  // three or four columns, each thread's chunks of all in registers
+    switch (R) {
+      case 1: return gemv_ring_kernel<FMT, 1, 4, true>;
+      case 2: return gemv_ring_kernel<FMT, 2, 4, true>;
+      case 4: return gemv_ring_kernel<FMT, 4, 4, true>;
+      default: return gemv_ring_kernel<FMT, 8, 4, true>;
+    }
+  }
   switch (R) {
     case 1: return gemv_ring_kernel<FMT, 1, 4, false>;
     case 2: return gemv_ring_kernel<FMT, 2, 4, false>;
@@ -31,7 +39,6 @@ static KernelFn pick(int R, int MC) {
 }
 
 KernelFn ring_kernel_for(int fmt, int R, int MC, bool xreg) {
-  if (MC > 2) xreg = false;
   if (fmt == 0) return xreg ? pick<0, true>(R, MC) : pick<0, false>(R, MC);
   if (fmt == 2) return xreg ? pick<2, true>(R, MC) : pick<2, false>(R, MC);
   if (fmt == 3) return xreg ? pick<3, true>(R, MC) : pick<3, false>(R, MC);

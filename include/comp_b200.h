@@ -155,7 +155,7 @@ int b2q_quant_gemv(int fmt, const uint8_t* wq, int64_t ldwq, const int16_t* ws, 
 
 /*
  * Workspace bytes b2q_quant_gemv_ws uses for this layer shape (0 = none). With M at or above the tensor-core column
- * threshold (b2q_set_gemm_min_columns; at its default from 3 columns, on layers the warp-specialized
+ * threshold (b2q_set_gemm_min_columns; at its default from 5 columns, TQ2_0 from 3, on layers the warp-specialized
  * schedule takes) it holds the quantized activations in the MMA tile layout, and for a layer whose 128-row tiles alone
  * do not fill the GPU also the partial sums of its K ranges (the warp-specialized GEMM then splits K, and a third
  * launch adds the ranges in order). With fewer columns it is the GEMV's split-K scratch under the current split-K mode
@@ -292,8 +292,8 @@ int b2q_set_warps(int warps);
  * MMA, weights read once for all columns; default 8, 0 = never). Fused calls then quantize first into the caller's
  * XQ / XD outputs or the workspace (b2q_workspace_size reports its size); int32 block dots are unchanged, Y differs
  * from the GEMV path only by the f32 summation order. At the default, a fused call with f32 activations and a workspace
- * of b2q_workspace_size bytes takes the warp-specialized tensor-core schedule from 3 columns already (small
- * speculative-decode batches: the GEMV path re-reads the weights once per 4 columns). */
+ * of b2q_workspace_size bytes takes the warp-specialized tensor-core schedule from 5 columns already (TQ2_0: from 3);
+ * up to 4 columns (TQ2_0: 2) the GEMV keeps every column's activation chunk in registers and reads the weights once. */
 int b2q_set_gemm_min_columns(int m);
 
 /* Tuning hook (process-wide): the fused tensor-core schedule. 0 (default) = warp-specialized where it applies (a
