@@ -736,42 +736,45 @@ def main():
             for L in layers:
                 L.obj.wq, L.obj.ws = L.w[0]
 
-    # ---- N = 1, decode at M = 1 only: the same layers with 16 activation columns (batched or speculative decode), the
-    # fused quantizer + tcgen05 GEMM path, each layer alone back to back over its rotating copies, event-timed ----
-    batched = None
+    # ---- N = 1, decode at M = 1 only: the same layers with 2, 4 and 16 activation columns (speculative or batched
+    # decode) through the same fused call (the planner's path: the GEMV with every column in registers, or the
+    # tcgen05 GEMM), each layer alone back to back over its rotating copies, event-timed ----
+    batched = {}
     if not args.no_extras and world == 1 and m == 1:
-        mb = 16
-        batched = []
-        for i, L in enumerate(layers):
-            xb = torch.from_numpy(make_x(L.k, mb, 300 + i)).to(dev)
-            yb = torch.empty((mb, L.n), dtype=torch.float32, device=dev)
-            wsb = host.workspace_size(L.fmt, L.n, L.k, mb)
-            wk = torch.empty(max(16, wsb), dtype=torch.uint8, device=dev)
-            nc = copies_for(weight_bytes(L.fmt, L.n, L.k))
-            ws_list = [L.w[c % copies] if c < copies else (L.w[0][0].clone(), L.w[0][1].clone()) for c in range(nc)]
+        for mb in (2, 4, 16):
+            rows_b = []
+            for i, L in enumerate(layers):
+                xb = torch.from_numpy(make_x(L.k, mb, 300 + i)).to(dev)
+                yb = torch.empty((mb, L.n), dtype=torch.float32, device=dev)
+                wsb = host.workspace_size(L.fmt, L.n, L.k, mb)
+                wk = torch.empty(max(16, wsb), dtype=torch.uint8, device=dev)
+                nc = copies_for(weight_bytes(L.fmt, L.n, L.k))
+                ws_list = [L.w[c % copies] if c < copies else (L.w[0][0].clone(), L.w[0][1].clone())
+                           for c in range(nc)]
 
-            def run_b(r, L=L, xb=xb, yb=yb, wk=wk, wsb=wsb, ws_list=ws_list, nc=nc):
-                wq, ws = ws_list[r % nc]
-                rc = lib.b2q_quant_gemv_ws(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), xb.data_ptr(),
-                                           xb.stride(0), None, None, yb.data_ptr(), L.n, L.k, mb, wk.data_ptr(), wsb,
-                                           sptr)
-                if rc != 0:
-                    raise RuntimeError(_lib.last_error())
-            reps = max(4 * nc, 40)
-            for r in range(2 * nc):
-                run_b(r)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for r in range(reps):
-                run_b(r)
-            e1.record(stream)
-            e1.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
-            gbs = algo_bytes(L.fmt, L.n, L.k, mb) / (us * 1e-6) / 1e9
-            batched.append({"name": L.name, "shape": f"{L.fmt} {L.n}x{L.k}", "m": mb, "us": round(us, 3),
-                            "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "launches_timed": reps})
-            del xb, yb, wk, ws_list
+                def run_b(r, L=L, xb=xb, yb=yb, wk=wk, wsb=wsb, ws_list=ws_list, nc=nc, mb=mb):
+                    wq, ws = ws_list[r % nc]
+                    rc = lib.b2q_quant_gemv_ws(L.fid, wq.data_ptr(), wq.stride(0), ws.data_ptr(), xb.data_ptr(),
+                                               xb.stride(0), None, None, yb.data_ptr(), L.n, L.k, mb, wk.data_ptr(),
+                                               wsb, sptr)
+                    if rc != 0:
+                        raise RuntimeError(_lib.last_error())
+                reps = max(4 * nc, 40)
+                for r in range(2 * nc):
+                    run_b(r)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for r in range(reps):
+                    run_b(r)
+                e1.record(stream)
+                e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                gbs = algo_bytes(L.fmt, L.n, L.k, mb) / (us * 1e-6) / 1e9
+                rows_b.append({"name": L.name, "shape": f"{L.fmt} {L.n}x{L.k}", "m": mb, "us": round(us, 3),
+                               "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "launches_timed": reps})
+                del xb, yb, wk, ws_list
+            batched[mb] = rows_b
         torch.cuda.empty_cache()
 
     # ---- sustained: >= 1 s of the same steps after the per-layer timing, event-timed, with its own clock record (a
@@ -975,7 +978,9 @@ def main():
             "us_per_gemv": round(ms * 1e3 / args.steps / len(layers), 3),
             "hbm_frac": round(value / world / peak, 4),
             "per_layer": per_layer,
-            "batched_m16": batched,
+            "batched_m2": batched.get(2),
+            "batched_m4": batched.get(4),
+            "batched_m16": batched.get(16),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": (f"quantizer + tcgen05 GEMM {tag} (2 launches, timed together)" if L_tc else
