@@ -182,8 +182,9 @@ class RowShardedGemv:
 
     # ---- NCCL exchange ----
     def local(self, x):
-        """This rank's output slice [M][rows] (no exchange)."""
-        return host.quant_gemv(self.fmt, self.wq, self.ws, x, self.rows, self.k)
+        """This rank's output slice [M][rows] (no exchange), on the same single-launch schedule as the fused exchange
+        (split=False), so that both exchanges give the unsharded split=False Y bit for bit."""
+        return host.quant_gemv(self.fmt, self.wq, self.ws, x, self.rows, self.k, split=False)
 
     def _nccl(self, x):
         m = x.shape[0]

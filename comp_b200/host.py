@@ -289,9 +289,10 @@ def quant_gemv(fmt, wq, ws, x, n, k, return_act=False, split=True, workspace=Non
     decode step.
 
     split=False: Y equals gemv(fmt, wq, ws, *quantize(fmt, x), n, k) exactly (same bytes, same schedule, same f32
-    order); one launch up to 4 columns, with more the quantizer and the tensor-core GEMM. split=True (default): tall-K layers run the split-K schedule with a workspace (allocated here
-    unless given; a CUDA byte tensor of at least workspace_size(...) bytes); Y then differs from the single-launch
-    result only by f32 rounding of the sum order, and is deterministic."""
+    order); one launch up to 4 columns, with more the quantizer and the tensor-core GEMM. split=True (default): with a
+    workspace (allocated here unless given; a CUDA byte tensor of at least workspace_size(...) bytes) tall-K layers
+    may run the split-K schedule, and from 5 columns (TQ2_0: 3) layers that fill the GPU the fused tensor-core GEMM;
+    Y then differs from the split=False result only by f32 rounding of the sum order, and is deterministic."""
     f = _fmt(fmt)
     dev = _need_cuda("quant_gemv", wq, ws, x)
     _check_weights(fmt, wq, ws, n, k)
